@@ -1,0 +1,319 @@
+// Elementwise / row-reduction kernels around attention, written to reproduce the
+// reference's eager PyTorch arithmetic step by step (each intermediate rounded where the
+// reference rounds it), so the decode step needs no Inductor/Triton kernels:
+//   RMSNorm            mini_vllm/layers/layernorm.py:18-28   (rms_forward)
+//   add + RMSNorm      mini_vllm/layers/layernorm.py:30-42   (add_rms_forward)
+//   QK-RMSNorm + RoPE  mini_vllm/models/qwen3.py:82-85, layers/rotary_embedding.py:8-16,39-50
+//   SiLU * mul         mini_vllm/layers/activation.py:12-16
+//   greedy argmax      logits.argmax(-1) (first index among equal maxima)
+#include "hl_common.cuh"
+
+namespace hl {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w), computed per row by one warp.
+// If `res` is given: x = in + res (fp32), res := bf16(x) first (the add_rms_forward order).
+// NV = hidden / 256 vectors of 8 elements per lane, so the row stays in registers.
+template <bool ADD, int NV>
+__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ res,
+                               const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows,
+                               int hidden, int64_t in_stride, int64_t out_stride, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const __nv_bfloat16* x = in + int64_t(warp) * in_stride;
+  __nv_bfloat16* r = ADD ? res + int64_t(warp) * hidden : nullptr;
+  __nv_bfloat16* y = out + int64_t(warp) * out_stride;
+  float buf[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NV; ++c) {
+    const int vi = lane + 32 * c;
+    const uint4 a = *reinterpret_cast<const uint4*>(x + 8 * vi);
+    const uint32_t wa[4] = {a.x, a.y, a.z, a.w};
+    float v[8];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      v[2 * t] = bf16lo(wa[t]);
+      v[2 * t + 1] = bf16hi(wa[t]);
+    }
+    if (ADD) {
+      const uint4 b = *reinterpret_cast<const uint4*>(r + 8 * vi);
+      const uint32_t wb[4] = {b.x, b.y, b.z, b.w};
+      uint32_t ro[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        v[2 * t] = __fadd_rn(v[2 * t], bf16lo(wb[t]));
+        v[2 * t + 1] = __fadd_rn(v[2 * t + 1], bf16hi(wb[t]));
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * t], v[2 * t + 1]);
+        ro[t] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      *reinterpret_cast<uint4*>(r + 8 * vi) = make_uint4(ro[0], ro[1], ro[2], ro[3]);
+    }
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      buf[c][t] = v[t];
+      ss = fmaf(v[t], v[t], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / float(hidden) + eps);
+#pragma unroll
+  for (int c = 0; c < NV; ++c) {
+    const int vi = lane + 32 * c;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * vi);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float a = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t], inv)), bf16lo(ww[t]));
+      const float b = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t + 1], inv)), bf16hi(ww[t]));
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
+      o[t] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+    *reinterpret_cast<uint4*>(y + 8 * vi) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// In-place QK-RMSNorm (over head_dim = 128) + NeoX RoPE on the q and k parts of the fused
+// qkv rows: qkv[t] = [q (Hq*128) | k (Hk*128) | v (Hk*128)].  One half-warp per (token,
+// head); lane ln owns dims [8ln, 8ln+8) and its RoPE partner dims live in lane ln ^ 8.
+// cos_sin[pos] = [cos(pos*f_0..63) | sin(pos*f_0..63)] fp32 (the reference's cos_sin_cache).
+__global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row_stride, int num_tokens,
+                                    int num_q_heads, int num_kv_heads, const __nv_bfloat16* __restrict__ qw,
+                                    const __nv_bfloat16* __restrict__ kw, const float* __restrict__ cos_sin,
+                                    const int64_t* __restrict__ positions, float eps) {
+  const int heads = num_q_heads + num_kv_heads;
+  const int64_t gid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;  // (token, head) index
+  const int ln = threadIdx.x & 15;
+  const bool active = gid < int64_t(num_tokens) * heads;
+  const int64_t tok = active ? gid / heads : 0;
+  const int hh = active ? int(gid % heads) : 0;
+  const bool is_q = hh < num_q_heads;
+  __nv_bfloat16* x = qkv + tok * row_stride + int64_t(hh) * 128 + 8 * ln;
+  float v[8];
+  {
+    const uint4 a = active ? *reinterpret_cast<const uint4*>(x) : make_uint4(0, 0, 0, 0);
+    const uint32_t wa[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      v[2 * t] = bf16lo(wa[t]);
+      v[2 * t + 1] = bf16hi(wa[t]);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) ss = fmaf(v[t], v[t], ss);
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = rsqrtf(ss / 128.f + eps);
+  const __nv_bfloat16* w = is_q ? qw : kw;
+  float nv[8];
+  {
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * ln);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      nv[2 * t] = bf16_round(__fmul_rn(bf16_round(__fmul_rn(v[2 * t], inv)), bf16lo(ww[t])));
+      nv[2 * t + 1] = bf16_round(__fmul_rn(bf16_round(__fmul_rn(v[2 * t + 1], inv)), bf16hi(ww[t])));
+    }
+  }
+  float pv[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) pv[t] = __shfl_xor_sync(0xffffffffu, nv[t], 8);
+  if (!active) return;
+  const int64_t pos = positions[tok];
+  const int f0 = (ln & 7) * 8;  // frequency index of this lane's first element
+  const float* cs = cos_sin + pos * 128;
+  const bool first_half = ln < 8;
+  uint32_t o[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    float r[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int e = 2 * t + u;
+      const float c = cs[f0 + e];
+      const float s = cs[64 + f0 + e];
+      // first half: y1 = x1*cos - x2*sin ; second half: y2 = x2*cos + x1*sin
+      r[u] = first_half ? __fsub_rn(__fmul_rn(nv[e], c), __fmul_rn(pv[e], s))
+                        : __fadd_rn(__fmul_rn(nv[e], c), __fmul_rn(pv[e], s));
+    }
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(r[0], r[1]);
+    o[t] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  *reinterpret_cast<uint4*>(x) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// out[t, i] = bf16(bf16(silu(x[t, i])) * y[t, i]) with x = in[t, :I], y = in[t, I:2I].
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, int rows,
+                                int inter, int64_t in_stride, int64_t out_stride) {
+  const int64_t vid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int nvec = inter / 8;
+  if (vid >= int64_t(rows) * nvec) return;
+  const int64_t r = vid / nvec;
+  const int c = int(vid % nvec);
+  const uint4 a = *reinterpret_cast<const uint4*>(in + r * in_stride + 8 * c);
+  const uint4 b = *reinterpret_cast<const uint4*>(in + r * in_stride + inter + 8 * c);
+  const uint32_t wa[4] = {a.x, a.y, a.z, a.w};
+  const uint32_t wb[4] = {b.x, b.y, b.z, b.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    float xs[2] = {bf16lo(wa[t]), bf16hi(wa[t])};
+    float ys[2] = {bf16lo(wb[t]), bf16hi(wb[t])};
+    float rr[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const float sx = bf16_round(__fdiv_rn(xs[u], __fadd_rn(1.0f, expf(-xs[u]))));
+      rr[u] = __fmul_rn(sx, ys[u]);
+    }
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(rr[0], rr[1]);
+    o[t] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  *reinterpret_cast<uint4*>(out + r * out_stride + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Greedy sampling: per row, index of the maximum (lowest index among ties; NaN never wins).
+// One CTA per row; writes the token both to out_tokens[row] and, when given, to
+// next_tokens[slot_of_row[row]] so the next decode step can read it on the device.
+__global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int vocab,
+                              int64_t* __restrict__ out_tokens) {
+  const int row = blockIdx.x;
+  const __nv_bfloat16* x = logits + int64_t(row) * row_stride;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const float v = __bfloat162float(x[i]);
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sb[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sb[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    if (lane == 0) out_tokens[row] = (bi == 0x7fffffff) ? 0 : bi;
+  }
+}
+
+}  // namespace
+}  // namespace hl
+
+using namespace hl;
+
+extern "C" int hl_rmsnorm(const void* in, int64_t in_stride, void* residual, const void* weight, void* out,
+                          int64_t out_stride, int rows, int hidden, float eps, void* stream) {
+  clear_error();
+  if (rows == 0) return HL_OK;
+  HL_CHECK_ARG(in && weight && out && rows > 0, "hl_rmsnorm: bad arguments");
+  HL_CHECK_ARG(hidden % 256 == 0 && hidden <= 8192, "hl_rmsnorm: hidden must be a multiple of 256, <= 8192");
+  HL_CHECK_ARG(aligned16(in) && aligned16(out) && aligned16(weight) && in_stride % 8 == 0 && out_stride % 8 == 0 &&
+                   (!residual || aligned16(residual)),
+               "hl_rmsnorm: 16-byte alignment required");
+  const int threads = 256;
+  const int blocks = (rows * 32 + threads - 1) / threads;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __nv_bfloat16* x = (const __nv_bfloat16*)in;
+  __nv_bfloat16* r = (__nv_bfloat16*)residual;
+  const __nv_bfloat16* wt = (const __nv_bfloat16*)weight;
+  __nv_bfloat16* y = (__nv_bfloat16*)out;
+#define HL_RMS_CASE(NV)                                                                                  \
+  case NV:                                                                                               \
+    if (r)                                                                                               \
+      rmsnorm_kernel<true, NV><<<blocks, threads, 0, s>>>(x, r, wt, y, rows, hidden, in_stride, out_stride, eps); \
+    else                                                                                                 \
+      rmsnorm_kernel<false, NV><<<blocks, threads, 0, s>>>(x, r, wt, y, rows, hidden, in_stride, out_stride, eps); \
+    break;
+  switch (hidden / 256) {
+    HL_RMS_CASE(1) HL_RMS_CASE(2) HL_RMS_CASE(3) HL_RMS_CASE(4) HL_RMS_CASE(5) HL_RMS_CASE(6) HL_RMS_CASE(8)
+    HL_RMS_CASE(10) HL_RMS_CASE(12) HL_RMS_CASE(14) HL_RMS_CASE(16) HL_RMS_CASE(20) HL_RMS_CASE(24)
+    HL_RMS_CASE(28) HL_RMS_CASE(32)
+    default:
+      set_error("hl_rmsnorm: hidden=%d not supported", hidden);
+      return HL_ERR_UNSUPPORTED;
+  }
+#undef HL_RMS_CASE
+  HL_CHECK_LAUNCH("hl_rmsnorm");
+  return HL_OK;
+}
+
+extern "C" int hl_qk_norm_rope(void* qkv, int64_t row_stride, int num_tokens, int num_q_heads, int num_kv_heads,
+                               int head_dim, const void* q_weight, const void* k_weight, const float* cos_sin,
+                               const int64_t* positions, float eps, void* stream) {
+  clear_error();
+  if (num_tokens == 0) return HL_OK;
+  HL_CHECK_ARG(qkv && q_weight && k_weight && cos_sin && positions && num_tokens > 0, "hl_qk_norm_rope: bad args");
+  HL_CHECK_ARG(head_dim == 128, "hl_qk_norm_rope: head_dim must be 128");
+  HL_CHECK_ARG(aligned16(qkv) && row_stride % 8 == 0, "hl_qk_norm_rope: 16-byte alignment required");
+  const int64_t groups = int64_t(num_tokens) * (num_q_heads + num_kv_heads);
+  const int threads = 256;
+  const int64_t blocks = (groups * 16 + threads - 1) / threads;
+  HL_CHECK_ARG(blocks < (1ll << 31), "hl_qk_norm_rope: grid too large");
+  qk_norm_rope_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      (__nv_bfloat16*)qkv, row_stride, num_tokens, num_q_heads, num_kv_heads, (const __nv_bfloat16*)q_weight,
+      (const __nv_bfloat16*)k_weight, cos_sin, positions, eps);
+  HL_CHECK_LAUNCH("hl_qk_norm_rope");
+  return HL_OK;
+}
+
+extern "C" int hl_silu_mul(const void* in, int64_t in_stride, void* out, int64_t out_stride, int rows,
+                           int intermediate, void* stream) {
+  clear_error();
+  if (rows == 0) return HL_OK;
+  HL_CHECK_ARG(in && out && rows > 0 && intermediate % 8 == 0, "hl_silu_mul: bad arguments");
+  HL_CHECK_ARG(aligned16(in) && aligned16(out) && in_stride % 8 == 0 && out_stride % 8 == 0,
+               "hl_silu_mul: 16-byte alignment required");
+  const int64_t n = int64_t(rows) * (intermediate / 8);
+  const int threads = 256;
+  silu_mul_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      (const __nv_bfloat16*)in, (__nv_bfloat16*)out, rows, intermediate, in_stride, out_stride);
+  HL_CHECK_LAUNCH("hl_silu_mul");
+  return HL_OK;
+}
+
+extern "C" int hl_argmax(const void* logits, int64_t row_stride, int rows, int vocab, int64_t* out_tokens,
+                         void* stream) {
+  clear_error();
+  if (rows == 0) return HL_OK;
+  HL_CHECK_ARG(logits && out_tokens && rows > 0 && vocab > 0, "hl_argmax: bad arguments");
+  argmax_kernel<<<rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>((const __nv_bfloat16*)logits, row_stride, vocab,
+                                                                       out_tokens);
+  HL_CHECK_LAUNCH("hl_argmax");
+  return HL_OK;
+}

@@ -1,0 +1,572 @@
+// Paged decode attention for B200 (sm_100a): split-K flash-decoding over a paged KV cache
+// with an in-kernel last-CTA reduction.
+//
+// Semantics (mini_vllm/layers/attention.py:162-170, flash_attn_with_kvcache with one query
+// token, causal=True, cache_seqlens=context_lens, block_table=block_tables):
+//   out[b, hq] = softmax_j(scale * q[b, hq] . K[b, j, hq / G]) @ V[b, j, hq / G],  j < L_b,
+//   token j of sequence b lives at slot block_tables[b, j / BS] * BS + j % BS,
+//   G = Hq / Hk (grouped-query attention).  L_b == 0 gives zeros.
+// FP8 variant (attention.py:134-141): K/V bytes are e4m3, dequantised in registers as
+// value * scale[h]; k_scale is folded into q and v_scale into the output.
+//
+// Work decomposition.  One CTA = one (split, sequence): SPLIT consecutive tokens of one page,
+// all local KV heads.  Because the cache is [block, offset, Hk, D], the K (and V) rows of a
+// run of tokens inside one page are one contiguous byte range, so each pipeline stage is a
+// single 16 KiB cp.async.bulk (TMA engine) per K and per V, completion tracked by an mbarrier.
+// 8 warps: warp w owns KV head w % Hk and a 1/(8/Hk) slice of each tile's tokens; within a
+// warp each half-warp takes one token at a time and its 16 lanes split D = 128 into 8-element
+// (16-byte) slices, so shared-memory reads are conflict-free 256-byte rows.  All G query
+// heads of the KV head are kept in registers, so every K/V byte is read from HBM once and
+// used G times.  Splits of one sequence are combined by the CTA that finishes last (atomic
+// ticket in the workspace); sequences that fit in one split write the output directly.
+#include "hl_common.cuh"
+
+namespace hl {
+namespace {
+
+constexpr int kDecodeThreads = 256;
+constexpr int kHeadDim = 128;
+constexpr int kSplit = 128;            // tokens per CTA (divides every supported block size)
+constexpr int kTileBytes = 16384;      // bytes per K (and per V) pipeline stage
+constexpr int kStages = 3;
+constexpr int kMaxBatch = 4096;        // capacity of the ticket array in the workspace
+constexpr int64_t kWsErrOff = 0;       // int32 error word(s)
+constexpr int64_t kWsTicketOff = 256;  // int32 tickets[kMaxBatch]
+constexpr int64_t kWsMlOff = kWsTicketOff + 4 * kMaxBatch + 256;  // float2 (m, l) [B][S][Hq]
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__host__ __device__ constexpr int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+struct DecodeParams {
+  const __nv_bfloat16* q;
+  int64_t q_row_stride;
+  const uint8_t* k_cache;
+  const uint8_t* v_cache;
+  const float* k_scale;
+  const float* v_scale;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int max_blocks;
+  const int32_t* context_lens;
+  int batch;
+  int block_size;
+  int64_t num_blocks;
+  int max_splits;
+  float scale_log2;  // softmax_scale * log2(e)
+  __nv_bfloat16* out;
+  int64_t out_row_stride;
+  uint8_t* ws;
+};
+
+template <bool FP8, int HK>
+struct Traits {
+  static constexpr int kElem = FP8 ? 1 : 2;
+  static constexpr int kRowBytes = HK * kHeadDim * kElem;  // one token, all local KV heads
+  static constexpr int kT = kTileBytes / kRowBytes;         // tokens per tile
+  static constexpr int kPhases = 8 / HK;                    // warps sharing one KV head
+  static constexpr int kTPW = kT / kPhases;                 // tokens per warp per tile
+  static constexpr int kTPH = kTPW / 2;                     // tokens per half-warp per tile
+  static_assert(kSplit % kT == 0, "split must be a whole number of tiles");
+  static_assert(kTPH >= 1, "tile too small");
+};
+
+// Load 8 consecutive K or V elements (this lane's D-slice) from shared memory as floats.
+template <bool FP8>
+__device__ __forceinline__ void load8(const uint8_t* p, float (&x)[8]) {
+  if constexpr (FP8) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    const uint32_t w[2] = {v.x, v.y};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float2 a = e4m3x2_to_float2(static_cast<uint16_t>(w[i] & 0xffffu));
+      const float2 b = e4m3x2_to_float2(static_cast<uint16_t>(w[i] >> 16));
+      x[4 * i + 0] = a.x;
+      x[4 * i + 1] = a.y;
+      x[4 * i + 2] = b.x;
+      x[4 * i + 3] = b.y;
+    }
+  } else {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = bf16lo(w[i]);
+      x[2 * i + 1] = bf16hi(w[i]);
+    }
+  }
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&x)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Merge softmax state (m2, l2, a2) into (m, l, a).  m == -inf means "empty".
+template <int G>
+__device__ __forceinline__ void merge_state(float (&m)[G], float (&l)[G], float (&a)[G][8], const float (&m2)[G],
+                                            const float (&l2)[G], const float (&a2)[G][8]) {
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const float mn = fmaxf(m[j], m2[j]);
+    if (mn == -INFINITY) continue;
+    const float c1 = exp2f(m[j] - mn);
+    const float c2 = exp2f(m2[j] - mn);
+    l[j] = l[j] * c1 + l2[j] * c2;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) a[j][d] = a[j][d] * c1 + a2[j][d] * c2;
+    m[j] = mn;
+  }
+}
+
+template <bool FP8, int G, int HK>
+__global__ void __launch_bounds__(kDecodeThreads, (G <= 4 ? 2 : 1)) paged_decode_kernel(const DecodeParams p) {
+  using Tr = Traits<FP8, HK>;
+  constexpr int kT = Tr::kT;
+  constexpr int kRow = Tr::kRowBytes;
+  constexpr int kTPW = Tr::kTPW;
+  constexpr int kTPH = Tr::kTPH;
+  constexpr int kHq = HK * G;
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * 2 * kTileBytes);
+  int* flag_smem = reinterpret_cast<int*>(full + kStages);
+
+  const int split = blockIdx.x;
+  const int b = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int ln = lane & 15;  // D-slice: elements [8*ln, 8*ln + 8)
+  const int hw = lane >> 4;  // half-warp
+  const int h = warp % HK;   // local KV head of this warp
+  const int phase = warp / HK;
+
+  int32_t* ws_err = reinterpret_cast<int32_t*>(p.ws + kWsErrOff);
+  int32_t* tickets = reinterpret_cast<int32_t*>(p.ws + kWsTicketOff);
+  float2* ws_ml = reinterpret_cast<float2*>(p.ws + kWsMlOff);
+  float* ws_o = reinterpret_cast<float*>(
+      p.ws + kWsMlOff + align256(int64_t(p.batch) * p.max_splits * kHq * sizeof(float2)));
+
+  int L = p.context_lens[b];
+  const int Lmax = p.max_blocks * p.block_size;
+  L = L < 0 ? 0 : (L > Lmax ? Lmax : L);
+  const int n_splits = (L + kSplit - 1) / kSplit;
+  __nv_bfloat16* out_b = p.out + int64_t(b) * p.out_row_stride;
+
+  if (split >= n_splits) {
+    if (split == 0) {  // empty sequence (padding row): finite zeros, like an empty softmax
+      for (int i = tid; i < kHq * kHeadDim / 8; i += kDecodeThreads)
+        reinterpret_cast<uint4*>(out_b)[i] = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+
+  const int tok0 = split * kSplit;
+  const int tok1 = min(L, tok0 + kSplit);
+  const int page = tok0 / p.block_size;
+  const int64_t block = p.block_tables[int64_t(b) * p.bt_stride + page];
+  const bool bad_block = block < 0 || block >= p.num_blocks;
+  const int ntiles = (tok1 - tok0 + kT - 1) / kT;
+  const int64_t base_slot = block * p.block_size + (tok0 % p.block_size);
+  const uint8_t* kbase = p.k_cache + base_slot * kRow;
+  const uint8_t* vbase = p.v_cache + base_slot * kRow;
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
+    fence_mbar_init();
+    *flag_smem = 0;
+  }
+  __syncthreads();
+
+  if (bad_block) {
+    if (tid == 0) atomicOr(ws_err, 2);
+  } else if (tid == 0) {
+    const int npre = ntiles < kStages ? ntiles : kStages;
+    for (int i = 0; i < npre; ++i) {
+      mbar_arrive_expect_tx(&full[i], 2 * kT * kRow);
+      bulk_g2s(smem + i * 2 * kTileBytes, kbase + int64_t(i) * kT * kRow, kT * kRow, &full[i]);
+      bulk_g2s(smem + i * 2 * kTileBytes + kTileBytes, vbase + int64_t(i) * kT * kRow, kT * kRow, &full[i]);
+    }
+  }
+
+  // Query slice of the G query heads that share KV head h, pre-scaled so that the
+  // softmax runs in base 2 (and, for FP8, with k_scale folded in).
+  float qs[G][8];
+  {
+    const float ks = (FP8 && p.k_scale) ? p.k_scale[h] : 1.0f;
+    const __nv_bfloat16* qb = p.q + int64_t(b) * p.q_row_stride;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(qb + (h * G + j) * kHeadDim + 8 * ln);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        qs[j][2 * i] = bf16lo(w[i]) * p.scale_log2 * ks;
+        qs[j][2 * i + 1] = bf16hi(w[i]) * p.scale_log2 * ks;
+      }
+    }
+  }
+
+  float m[G], l[G], acc[G][8];
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    m[j] = -INFINITY;
+    l[j] = 0.f;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) acc[j][d] = 0.f;
+  }
+
+  bool timed_out = false;
+  if (!bad_block) {
+    for (int t = 0; t < ntiles; ++t) {
+      const int stage = t % kStages;
+      // A wait that gives up is made warp-uniform here and CTA-uniform at the barrier
+      // below, so no thread is left alone in a shuffle or a __syncthreads.
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], (t / kStages) & 1));
+      if (ok) {
+      const uint8_t* Ks = smem + stage * 2 * kTileBytes;
+      const uint8_t* Vs = Ks + kTileBytes;
+      const int tile_tok0 = tok0 + t * kT;
+
+      float sc[G][kTPH];
+      bool valid[kTPH];
+#pragma unroll
+      for (int i = 0; i < kTPH; ++i) {
+        const int tt = phase * kTPW + 2 * i + hw;
+        valid[i] = tile_tok0 + tt < tok1;
+        float kx[8];
+        load8<FP8>(Ks + tt * kRow + (h * kHeadDim + 8 * ln) * Tr::kElem, kx);
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          float s = 0.f;
+#pragma unroll
+          for (int d = 0; d < 8; ++d) s = fmaf(qs[j][d], kx[d], s);
+          sc[j][i] = s;
+        }
+      }
+      // Sum the 16 partial dot products of each half-warp.
+#pragma unroll
+      for (int off = 8; off >= 1; off >>= 1) {
+#pragma unroll
+        for (int j = 0; j < G; ++j)
+#pragma unroll
+          for (int i = 0; i < kTPH; ++i) sc[j][i] += __shfl_xor_sync(0xffffffffu, sc[j][i], off);
+      }
+
+      float pr[G][kTPH];
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        float mt = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kTPH; ++i)
+          if (valid[i]) mt = fmaxf(mt, sc[j][i]);
+        const float mn = fmaxf(m[j], mt);
+        if (mn == -INFINITY) {
+#pragma unroll
+          for (int i = 0; i < kTPH; ++i) pr[j][i] = 0.f;
+          continue;
+        }
+        const float corr = exp2f(m[j] - mn);
+        float ps = 0.f;
+#pragma unroll
+        for (int i = 0; i < kTPH; ++i) {
+          pr[j][i] = valid[i] ? exp2f(sc[j][i] - mn) : 0.f;
+          ps += pr[j][i];
+        }
+        l[j] = l[j] * corr + ps;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) acc[j][d] *= corr;
+        m[j] = mn;
+      }
+#pragma unroll
+      for (int i = 0; i < kTPH; ++i) {
+        if (!valid[i]) continue;  // never touch V rows past the context (may hold NaN bits)
+        const int tt = phase * kTPW + 2 * i + hw;
+        float vx[8];
+        load8<FP8>(Vs + tt * kRow + (h * kHeadDim + 8 * ln) * Tr::kElem, vx);
+#pragma unroll
+        for (int j = 0; j < G; ++j)
+#pragma unroll
+          for (int d = 0; d < 8; ++d) acc[j][d] = fmaf(pr[j][i], vx[d], acc[j][d]);
+      }
+
+      }  // ok
+      // Every warp is done with this stage: refill it (or leave together on a timeout).
+      if (__syncthreads_or(!ok)) {
+        timed_out = true;
+        break;
+      }
+      if (tid == 0 && t + kStages < ntiles) {
+        const int nt = t + kStages;
+        mbar_arrive_expect_tx(&full[stage], 2 * kT * kRow);
+        bulk_g2s(smem + stage * 2 * kTileBytes, kbase + int64_t(nt) * kT * kRow, kT * kRow, &full[stage]);
+        bulk_g2s(smem + stage * 2 * kTileBytes + kTileBytes, vbase + int64_t(nt) * kT * kRow, kT * kRow,
+                 &full[stage]);
+      }
+    }
+  }
+  if (timed_out) {
+    if (tid == 0) {
+      atomicOr(ws_err, 1);
+      // Give copies still in flight a second bounded chance to land before the CTA's
+      // shared memory is released.
+      for (int i = 0; i < kStages; ++i) mbar_wait(&full[i], 0), mbar_wait(&full[i], 1);
+    }
+    return;
+  }
+
+  // Merge the two half-warps (they hold disjoint token subsets of the same D-slice).
+  {
+    float m2[G], l2[G], a2[G][8];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      m2[j] = __shfl_xor_sync(0xffffffffu, m[j], 16);
+      l2[j] = __shfl_xor_sync(0xffffffffu, l[j], 16);
+#pragma unroll
+      for (int d = 0; d < 8; ++d) a2[j][d] = __shfl_xor_sync(0xffffffffu, acc[j][d], 16);
+    }
+    merge_state<G>(m, l, acc, m2, l2, a2);
+  }
+
+  // Merge warps that share a KV head (only when Hk < 8).  Stage buffers are free: every
+  // issued bulk copy has been waited for.
+  if constexpr (Tr::kPhases > 1) {
+    __syncthreads();
+    float* scr = reinterpret_cast<float*>(smem);  // [warp][j][lane 0..15][10]
+    if (phase > 0 && hw == 0) {
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        float* e = scr + ((warp * G + j) * 16 + ln) * 10;
+        e[0] = m[j];
+        e[1] = l[j];
+#pragma unroll
+        for (int d = 0; d < 8; ++d) e[2 + d] = acc[j][d];
+      }
+    }
+    __syncthreads();
+    if (phase == 0) {
+      for (int ph = 1; ph < Tr::kPhases; ++ph) {
+        const int w2 = ph * HK + h;
+        float m2[G], l2[G], a2[G][8];
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          const float* e = scr + ((w2 * G + j) * 16 + ln) * 10;
+          m2[j] = e[0];
+          l2[j] = e[1];
+#pragma unroll
+          for (int d = 0; d < 8; ++d) a2[j][d] = e[2 + d];
+        }
+        merge_state<G>(m, l, acc, m2, l2, a2);
+      }
+    }
+  }
+
+  const float vs = (FP8 && p.v_scale) ? p.v_scale[h] : 1.0f;
+  if (n_splits == 1) {
+    if (phase == 0 && hw == 0) {
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        const float inv = l[j] > 0.f ? vs / l[j] : 0.f;
+        float o[8];
+#pragma unroll
+        for (int d = 0; d < 8; ++d) o[d] = acc[j][d] * inv;
+        *reinterpret_cast<uint4*>(out_b + (h * G + j) * kHeadDim + 8 * ln) = pack_bf16x8(o);
+      }
+    }
+    return;
+  }
+
+  // Write this split's partial state, then take a ticket; the last CTA combines.
+  if (phase == 0 && hw == 0) {
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int hq = h * G + j;
+      const int64_t row = (int64_t(b) * p.max_splits + split) * kHq + hq;
+      float* o = ws_o + row * kHeadDim + 8 * ln;
+      reinterpret_cast<float4*>(o)[0] = make_float4(acc[j][0] * vs, acc[j][1] * vs, acc[j][2] * vs, acc[j][3] * vs);
+      reinterpret_cast<float4*>(o)[1] = make_float4(acc[j][4] * vs, acc[j][5] * vs, acc[j][6] * vs, acc[j][7] * vs);
+      if (ln == 0) ws_ml[row] = make_float2(m[j], l[j]);
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int prev = atomicAdd(&tickets[b], 1);
+    *flag_smem = (prev == n_splits - 1);
+  }
+  __syncthreads();
+  if (!*flag_smem) return;
+  __threadfence();
+
+  // Last CTA of sequence b: combine the n_splits partials.  Each thread produces 8
+  // consecutive output elements of one query head.
+  for (int idx = tid; idx < kHq * (kHeadDim / 8); idx += kDecodeThreads) {
+    const int hq = idx / (kHeadDim / 8);
+    const int d0 = (idx % (kHeadDim / 8)) * 8;
+    const int64_t row0 = int64_t(b) * p.max_splits * kHq + hq;
+    float mx = -INFINITY;
+    for (int s = 0; s < n_splits; ++s) mx = fmaxf(mx, __ldcg(&ws_ml[row0 + int64_t(s) * kHq]).x);
+    float lsum = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (mx != -INFINITY) {
+      for (int s = 0; s < n_splits; ++s) {
+        const int64_t row = row0 + int64_t(s) * kHq;
+        const float2 ml = __ldcg(&ws_ml[row]);
+        if (ml.x == -INFINITY) continue;
+        const float c = exp2f(ml.x - mx);
+        lsum += ml.y * c;
+        const float4* src = reinterpret_cast<const float4*>(ws_o + row * kHeadDim + d0);
+        const float4 a = __ldcg(src), bq = __ldcg(src + 1);
+        o[0] += a.x * c;
+        o[1] += a.y * c;
+        o[2] += a.z * c;
+        o[3] += a.w * c;
+        o[4] += bq.x * c;
+        o[5] += bq.y * c;
+        o[6] += bq.z * c;
+        o[7] += bq.w * c;
+      }
+    }
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) o[d] *= inv;
+    *reinterpret_cast<uint4*>(out_b + hq * kHeadDim + d0) = pack_bf16x8(o);
+  }
+  if (tid == 0) tickets[b] = 0;  // ready for the next launch
+}
+
+template <bool FP8, int G, int HK>
+int launch_decode(const DecodeParams& p, cudaStream_t stream) {
+  constexpr size_t smem = size_t(kStages) * 2 * kTileBytes + kStages * sizeof(uint64_t) + 16;
+  static bool configured = false;  // first call happens before any graph capture
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<FP8, G, HK>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) {
+      set_error("hl_paged_decode: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+      return HL_ERR_CUDA;
+    }
+    configured = true;
+  }
+  dim3 grid(p.max_splits, p.batch);
+  paged_decode_kernel<FP8, G, HK><<<grid, kDecodeThreads, smem, stream>>>(p);
+  HL_CHECK_LAUNCH("hl_paged_decode");
+  return HL_OK;
+}
+
+template <bool FP8, int G>
+int dispatch_hk(int hk, const DecodeParams& p, cudaStream_t s) {
+  switch (hk) {
+    case 1: return launch_decode<FP8, G, 1>(p, s);
+    case 2: return launch_decode<FP8, G, 2>(p, s);
+    case 4: return launch_decode<FP8, G, 4>(p, s);
+    case 8: return launch_decode<FP8, G, 8>(p, s);
+  }
+  set_error("hl_paged_decode: num_kv_heads=%d not in {1,2,4,8}", hk);
+  return HL_ERR_UNSUPPORTED;
+}
+
+template <bool FP8>
+int dispatch_g(int g, int hk, const DecodeParams& p, cudaStream_t s) {
+  switch (g) {
+    case 1: return dispatch_hk<FP8, 1>(hk, p, s);
+    case 2: return dispatch_hk<FP8, 2>(hk, p, s);
+    case 4: return dispatch_hk<FP8, 4>(hk, p, s);
+    case 8: return dispatch_hk<FP8, 8>(hk, p, s);
+  }
+  set_error("hl_paged_decode: Hq/Hk=%d not in {1,2,4,8}", g);
+  return HL_ERR_UNSUPPORTED;
+}
+
+int64_t max_splits_for(int max_blocks, int block_size) {
+  return (int64_t(max_blocks) * block_size + kSplit - 1) / kSplit;
+}
+
+}  // namespace
+}  // namespace hl
+
+using namespace hl;
+
+extern "C" int64_t hl_paged_decode_workspace_size(int batch, int num_q_heads, int head_dim, int max_blocks_per_seq,
+                                                  int block_size) {
+  if (batch <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_blocks_per_seq <= 0 || block_size <= 0) return -1;
+  const int64_t S = max_splits_for(max_blocks_per_seq, block_size);
+  const int64_t rows = int64_t(batch) * S * num_q_heads;
+  return kWsMlOff + align256(rows * int64_t(sizeof(float2))) + rows * head_dim * int64_t(sizeof(float));
+}
+
+extern "C" int hl_paged_decode(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+                               int kv_dtype, const float* k_scale, const float* v_scale, const int32_t* block_tables,
+                               int64_t bt_stride, int max_blocks_per_seq, const int32_t* context_lens, int batch,
+                               int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                               float softmax_scale, void* out, int64_t out_row_stride, void* workspace,
+                               int64_t workspace_bytes, void* stream) {
+  clear_error();
+  HL_CHECK_ARG(batch >= 0, "hl_paged_decode: batch < 0");
+  if (batch == 0) return HL_OK;
+  HL_CHECK_ARG(batch <= kMaxBatch, "hl_paged_decode: batch %d > %d", batch, kMaxBatch);
+  HL_CHECK_ARG(q && k_cache && v_cache && block_tables && context_lens && out, "hl_paged_decode: null pointer");
+  HL_CHECK_ARG(head_dim == kHeadDim, "hl_paged_decode: head_dim %d != 128", head_dim);
+  HL_CHECK_ARG(block_size > 0 && block_size % 256 == 0, "hl_paged_decode: block_size %% 256 != 0");
+  HL_CHECK_ARG(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "hl_paged_decode: Hq %% Hk != 0");
+  HL_CHECK_ARG(kv_dtype == HL_KV_BF16 || kv_dtype == HL_KV_FP8_E4M3, "hl_paged_decode: bad kv_dtype");
+  HL_CHECK_ARG(max_blocks_per_seq > 0 && bt_stride >= max_blocks_per_seq, "hl_paged_decode: bad block table width");
+  HL_CHECK_ARG(aligned16(q) && q_row_stride % 8 == 0 && q_row_stride >= int64_t(num_q_heads) * head_dim,
+               "hl_paged_decode: q must be 16-byte aligned with row stride %% 8 == 0");
+  HL_CHECK_ARG(aligned16(out) && out_row_stride % 8 == 0 && out_row_stride >= int64_t(num_q_heads) * head_dim,
+               "hl_paged_decode: out must be 16-byte aligned with row stride %% 8 == 0");
+  HL_CHECK_ARG(aligned16(k_cache) && aligned16(v_cache), "hl_paged_decode: caches must be 16-byte aligned");
+  const int64_t need =
+      hl_paged_decode_workspace_size(batch, num_q_heads, head_dim, max_blocks_per_seq, block_size);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace)) {
+    set_error("hl_paged_decode: workspace of %lld bytes needed (got %lld)", (long long)need,
+              (long long)workspace_bytes);
+    return HL_ERR_WORKSPACE;
+  }
+  const int64_t S = max_splits_for(max_blocks_per_seq, block_size);
+  HL_CHECK_ARG(S <= 65535, "hl_paged_decode: too many splits");
+
+  DecodeParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.q_row_stride = q_row_stride;
+  p.k_cache = static_cast<const uint8_t*>(k_cache);
+  p.v_cache = static_cast<const uint8_t*>(v_cache);
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
+  p.block_tables = block_tables;
+  p.bt_stride = bt_stride;
+  p.max_blocks = max_blocks_per_seq;
+  p.context_lens = context_lens;
+  p.batch = batch;
+  p.block_size = block_size;
+  p.num_blocks = num_blocks;
+  p.max_splits = int(S);
+  p.scale_log2 = softmax_scale * kLog2e;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_row_stride = out_row_stride;
+  p.ws = static_cast<uint8_t*>(workspace);
+
+  const int g = num_q_heads / num_kv_heads;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (kv_dtype == HL_KV_FP8_E4M3) return dispatch_g<true>(g, num_kv_heads, p, s);
+  return dispatch_g<false>(g, num_kv_heads, p, s);
+}
+
+extern "C" int hl_paged_decode_read_errors(const void* workspace, int32_t* errors_out, void* stream) {
+  clear_error();
+  HL_CHECK_ARG(workspace && errors_out, "hl_paged_decode_read_errors: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(errors_out, static_cast<const uint8_t*>(workspace) + kWsErrOff, sizeof(int32_t),
+                                  cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    set_error("hl_paged_decode_read_errors: %s", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
+  return HL_OK;
+}

@@ -1,0 +1,121 @@
+"""Paged KV block allocator with a chained-hash prefix cache.
+
+Behaviour (and therefore every block id it hands out) is that of
+mini_vllm/engine/block_manager.py:8-115: blocks are taken from the head of a FIFO free list,
+freed blocks go to its tail, a full block's hash is xxh64(previous block hash as 8
+little-endian bytes || token ids as int64 bytes), and a cached block is reused only when its
+stored token ids equal the request's.
+"""
+from collections import deque
+
+import numpy as np
+import xxhash
+
+from hilda_vllm_b200.engine.sequence import Sequence
+
+
+class Block:
+
+    def __init__(self, block_id: int):
+        self.block_id = block_id
+        self.ref_count = 0
+        self.hash = -1
+        self.token_ids: list[int] = []
+
+    def update(self, hash: int, token_ids: list[int]):
+        self.hash = hash
+        self.token_ids = token_ids
+
+    def reset(self):
+        self.ref_count = 1
+        self.hash = -1
+        self.token_ids = []
+
+
+class BlockManager:
+
+    def __init__(self, num_blocks: int, block_size: int):
+        self.block_size = block_size
+        self.blocks: list[Block] = [Block(i) for i in range(num_blocks)]
+        self.hash_to_block_id: dict[int, int] = {}
+        self.free_block_ids: deque[int] = deque(range(num_blocks))
+        self.used_block_ids: set[int] = set()
+
+    @classmethod
+    def compute_hash(cls, token_ids: list[int], prefix: int = -1) -> int:
+        hasher = xxhash.xxh64()
+        if prefix != -1:
+            hasher.update(prefix.to_bytes(8, "little"))
+        hasher.update(np.asarray(token_ids, dtype=np.int64).tobytes())
+        return hasher.intdigest()
+
+    def _allocate_block(self, block_id: int) -> Block:
+        block = self.blocks[block_id]
+        assert block.ref_count == 0
+        block.reset()
+        self.free_block_ids.remove(block_id)
+        self.used_block_ids.add(block_id)
+        return block
+
+    def _deallocate_block(self, block_id: int) -> None:
+        assert self.blocks[block_id].ref_count == 0
+        self.used_block_ids.remove(block_id)
+        self.free_block_ids.append(block_id)
+
+    def can_allocate(self, seq: Sequence) -> bool:
+        return len(self.free_block_ids) >= seq.num_blocks
+
+    def allocate(self, seq: Sequence) -> None:
+        assert not seq.block_table
+        prev_hash = -1
+        missed = False
+        for i in range(seq.num_blocks):
+            token_ids = seq.block(i)
+            full = len(token_ids) == self.block_size
+            prev_hash = self.compute_hash(token_ids, prev_hash) if full else -1
+            cached_id = self.hash_to_block_id.get(prev_hash, -1)
+            if cached_id == -1 or self.blocks[cached_id].token_ids != token_ids:
+                missed = True
+            if missed:
+                block = self._allocate_block(self.free_block_ids[0])
+            else:
+                seq.num_cached_tokens += self.block_size
+                if cached_id in self.used_block_ids:
+                    block = self.blocks[cached_id]
+                    block.ref_count += 1
+                else:
+                    block = self._allocate_block(cached_id)
+            if prev_hash != -1:
+                block.update(prev_hash, token_ids)
+                self.hash_to_block_id[prev_hash] = block.block_id
+            seq.block_table.append(block.block_id)
+
+    def deallocate(self, seq: Sequence) -> None:
+        for block_id in reversed(seq.block_table):
+            block = self.blocks[block_id]
+            block.ref_count -= 1
+            if block.ref_count == 0:
+                self._deallocate_block(block_id)
+        seq.num_cached_tokens = 0
+        seq.decode_cache_ready = False
+        seq.block_table.clear()
+
+    def can_append(self, seq: Sequence) -> bool:
+        needs_block = len(seq) % self.block_size == 1
+        return len(self.free_block_ids) >= needs_block
+
+    def may_append(self, seq: Sequence) -> None:
+        table = seq.block_table
+        last = self.blocks[table[-1]]
+        phase = len(seq) % self.block_size
+        if phase == 1:
+            # The newest token starts a new page.
+            block = self._allocate_block(self.free_block_ids[0])
+            table.append(block.block_id)
+        elif phase == 0 and last.hash == -1:
+            # The last page just filled up: register it in the prefix cache.
+            token_ids = seq.block(seq.num_blocks - 1)
+            prefix = self.blocks[table[-2]].hash if len(table) > 1 else -1
+            h = self.compute_hash(token_ids, prefix)
+            last.update(h, token_ids)
+            self.hash_to_block_id[h] = last.block_id

@@ -1,0 +1,208 @@
+"""User-facing engine: LLM(model, **config) with add_request / step / generate / generate_stream.
+
+Same API and step semantics as mini_vllm/engine/llm_engine.py:17-470 (without speculative
+decoding): schedule -> run on the model runner(s) -> postprocess, the FP8 prefill->decode cache
+conversion after prefill steps, and the same throughput statistics in last_generate_stats.
+step() returns the reference's 13-tuple; the speculative-decoding fields are always zero.
+"""
+from __future__ import annotations
+
+import atexit
+from dataclasses import fields
+from time import perf_counter
+
+import torch.multiprocessing as mp
+
+from hilda_vllm_b200.config import Config
+from hilda_vllm_b200.engine.model_runner import ModelRunner
+from hilda_vllm_b200.engine.scheduler import Scheduler
+from hilda_vllm_b200.engine.sequence import Sequence
+from hilda_vllm_b200.sampling_params import SamplingParams
+from hilda_vllm_b200.utils.tokenizer import load_tokenizer
+
+
+class LLMEngine:
+
+    def __init__(self, model, **kwargs):
+        names = {f.name for f in fields(Config)}
+        config = Config(model, **{k: v for k, v in kwargs.items() if k in names})
+        self.config = config
+        self.ps = []
+        self.events = []
+        if config.distributed_executor == "external" and config.tensor_parallel_size > 1:
+            import torch.distributed as dist
+            rank = dist.get_rank()
+            if rank != 0:
+                # Worker rank: serve rank 0's calls until it exits, then return a shell.
+                ModelRunner(config, rank, None)
+                self.is_worker = True
+                return
+            self.model_runner = ModelRunner(config, 0, None)
+        else:
+            ctx = mp.get_context("spawn")
+            for i in range(1, config.tensor_parallel_size):
+                event = ctx.Event()
+                process = ctx.Process(target=ModelRunner, args=(config, i, event))
+                process.start()
+                self.ps.append(process)
+                self.events.append(event)
+            self.model_runner = ModelRunner(config, 0, self.events)
+        self.is_worker = False
+        self.tokenizer = load_tokenizer(config.model, config.hf_config)
+        config.eos = self.tokenizer.eos_token_id if self.tokenizer.eos_token_id is not None else -1
+        self.scheduler = Scheduler(config)
+        self.last_generate_stats = None
+        self.last_step_diagnostics = None
+        atexit.register(self.exit)
+
+    def exit(self):
+        if not hasattr(self, "model_runner"):
+            return
+        self.model_runner.call("exit")
+        del self.model_runner
+        for p in self.ps:
+            p.join()
+
+    def add_request(self, prompt: str | list[int], sampling_params: SamplingParams):
+        if isinstance(prompt, str):
+            prompt = self.tokenizer.encode(prompt)
+        seq = Sequence(prompt, sampling_params)
+        self.scheduler.add(seq)
+        return seq
+
+    def step(self):
+        seqs, is_prefill = self.scheduler.schedule()
+        if not seqs:
+            return [], False, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0
+        token_ids = self.model_runner.call("run", seqs, is_prefill)
+        self.last_step_diagnostics = {
+            "running": len(self.scheduler.running),
+            "waiting": len(self.scheduler.waiting),
+            "decode_batch": None if is_prefill else (self.model_runner.last_decode_batch_info or {}),
+        }
+        self.scheduler.postprocess(seqs, token_ids, is_prefill)
+        if is_prefill and self.config.kv_cache_dtype == "fp8":
+            ready = [s.seq for s in seqs if not s.is_padding and s.seq.is_prefill_done and not s.seq.is_finished
+                     and not s.seq.decode_cache_ready]
+            if ready:
+                self.model_runner.call("convert_prefill_to_decode_cache", ready)
+                for seq in ready:
+                    seq.decode_cache_ready = True
+        outputs = [(s.seq.seq_id, s.seq.completion_token_ids) for s in seqs if not s.is_padding and s.seq.is_finished]
+        if is_prefill:
+            num_prefill_tokens = sum(s.token_chunk_size for s in seqs if not s.is_padding)
+            num_decode_tokens = sum(1 for s, t in zip(seqs, token_ids) if not s.is_padding and t is not None)
+        else:
+            num_prefill_tokens = 0
+            num_decode_tokens = sum(1 for s in seqs if not s.is_padding)
+        return outputs, num_prefill_tokens, num_decode_tokens, 0, 0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0
+
+    def is_finished(self):
+        return self.scheduler.is_finished()
+
+    def _add_sequences(self, prompts, sampling_params) -> list[Sequence]:
+        if not isinstance(sampling_params, list):
+            sampling_params = [sampling_params] * len(prompts)
+        return [self.add_request(p, sp) for p, sp in zip(prompts, sampling_params)]
+
+    def generate_stream(self, prompts, sampling_params):
+        self.scheduler.reset_diagnostics()
+        seqs = self._add_sequences(prompts, sampling_params)
+        emitted = {seq.seq_id: 0 for seq in seqs}
+        index = {seq.seq_id: i for i, seq in enumerate(seqs)}
+        stats = self._init_generate_stats(seqs)
+        start = perf_counter()
+        while not self.is_finished():
+            t = perf_counter()
+            _, n_pre, n_dec, *_ = self.step()
+            self._update_generate_stats(stats, n_pre, n_dec, perf_counter() - t, self.last_step_diagnostics)
+            for seq in seqs:
+                done = seq.completion_token_ids
+                prev = emitted[seq.seq_id]
+                if len(done) <= prev:
+                    continue
+                emitted[seq.seq_id] = len(done)
+                yield {"request_index": index[seq.seq_id], "seq_id": seq.seq_id, "token_ids": list(done[prev:]),
+                       "completion_token_ids": list(done), "is_finished": seq.is_finished}
+        self._set_last_generate_stats(stats, perf_counter() - start)
+
+    def generate(self, prompts, sampling_params, use_tqdm: bool = True) -> list[dict]:
+        self.scheduler.reset_diagnostics()
+        pbar = None
+        if use_tqdm:
+            from tqdm.auto import tqdm
+            pbar = tqdm(total=len(prompts), desc="Generating", dynamic_ncols=True)
+        seqs = self._add_sequences(prompts, sampling_params)
+        outputs = {}
+        stats = self._init_generate_stats(seqs)
+        start = perf_counter()
+        while not self.is_finished():
+            t = perf_counter()
+            output, n_pre, n_dec, *_ = self.step()
+            pre_tps, dec_tps = self._update_generate_stats(stats, n_pre, n_dec, perf_counter() - t,
+                                                           self.last_step_diagnostics)
+            if pbar is not None:
+                pbar.set_postfix({"Prefill": f"{int(pre_tps)}tok/s", "Decode": f"{int(dec_tps)}tok/s"})
+            for seq_id, token_ids in output:
+                outputs[seq_id] = token_ids
+                if pbar is not None:
+                    pbar.update(1)
+        self._set_last_generate_stats(stats, perf_counter() - start)
+        if pbar is not None:
+            pbar.close()
+        return [{"text": self.tokenizer.decode(outputs[seq.seq_id]), "token_ids": outputs[seq.seq_id]} for seq in seqs]
+
+    # ------------------------------------------------------------------ statistics
+    @staticmethod
+    def _init_generate_stats(seqs):
+        return {
+            "num_requests": len(seqs), "prompt_tokens": sum(s.num_prompt_tokens for s in seqs),
+            "prefill_tokens": 0, "decode_tokens": 0, "prefill_time_s": 0.0, "decode_time_s": 0.0,
+            "decode_steps": 0, "decode_scheduled_bs_sum": 0, "decode_active_bs_sum": 0, "decode_graph_bs_sum": 0,
+            "decode_padded_slots_sum": 0, "decode_active_bs_max": 0, "running_max": 0, "waiting_max": 0,
+        }
+
+    @staticmethod
+    def _update_generate_stats(stats, n_prefill, n_decode, elapsed, diag=None):
+        pre_tps = dec_tps = 0.0
+        if n_prefill > 0:
+            stats["prefill_tokens"] += n_prefill
+            stats["prefill_time_s"] += elapsed
+            pre_tps = n_prefill / elapsed if elapsed else 0.0
+        if n_decode > 0:
+            stats["decode_tokens"] += n_decode
+            stats["decode_time_s"] += elapsed
+            dec_tps = n_decode / elapsed if elapsed else 0.0
+        if diag:
+            stats["running_max"] = max(stats["running_max"], diag.get("running", 0))
+            stats["waiting_max"] = max(stats["waiting_max"], diag.get("waiting", 0))
+            batch = diag.get("decode_batch")
+            if batch is not None:
+                active = batch.get("active_seqs", 0)
+                stats["decode_steps"] += 1
+                stats["decode_scheduled_bs_sum"] += batch.get("scheduled_bs", 0)
+                stats["decode_active_bs_sum"] += active
+                stats["decode_graph_bs_sum"] += batch.get("graph_bs", 0)
+                stats["decode_padded_slots_sum"] += batch.get("padded_slots", 0)
+                stats["decode_active_bs_max"] = max(stats["decode_active_bs_max"], active)
+        return pre_tps, dec_tps
+
+    def _set_last_generate_stats(self, stats, total_time):
+        out = stats["decode_tokens"]
+        steps = stats["decode_steps"]
+        res = {
+            "num_requests": stats["num_requests"], "prompt_tokens": stats["prompt_tokens"], "output_tokens": out,
+            "prefill_tokens": stats["prefill_tokens"], "decode_tokens": stats["decode_tokens"],
+            "prefill_time_s": stats["prefill_time_s"], "decode_time_s": stats["decode_time_s"],
+            "total_time_s": total_time,
+            "prefill_throughput_toks": stats["prefill_tokens"] / stats["prefill_time_s"] if stats["prefill_time_s"] else 0.0,
+            "decode_throughput_toks": stats["decode_tokens"] / stats["decode_time_s"] if stats["decode_time_s"] else 0.0,
+            "total_throughput_toks": out / total_time if total_time else 0.0,
+            "decode_steps": steps,
+        }
+        for key in ("scheduled_bs", "active_bs", "graph_bs", "padded_slots"):
+            res[f"avg_decode_{key}"] = stats[f"decode_{key}_sum"] / steps if steps else 0.0
+        res.update({"decode_active_bs_max": stats["decode_active_bs_max"], "running_max": stats["running_max"],
+                    "waiting_max": stats["waiting_max"]})
+        res.update(self.scheduler.get_diagnostics())
+        self.last_generate_stats = res

@@ -1,0 +1,576 @@
+"""Per-GPU model runner: KV pool, batch preparation, decode CUDA graphs, TP control plane.
+
+Mirrors mini_vllm/engine/model_runner.py (ModelRunner) for the non-speculative path:
+  - allocate_kv_cache (:141-220): the pool [2, L, NB, BS, Hk/tp, D] (plus the FP8 twin) sized
+    from free memory, per-layer views handed to each Attention module;
+  - prepare_prefill (:614-650): varlen metadata and slot mapping for the scheduled chunks;
+  - prepare_decode (:652-720): replaced by DecodePacker + the hl_pack_decode_batch kernel, so
+    the host sends one small packet per step instead of rewriting every slot;
+  - capture_cudagraph / run_model (:735-832): one graph per batch bucket [1,2,4,8,16,...,512];
+    each graph holds the pack kernel, the whole model, the LM head and (for greedy sampling)
+    the argmax, so a decode step is: one packet copy, one graph replay, one token copy back;
+  - convert_prefill_to_decode_cache (:483-502): one launch for all layers;
+  - the tensor-parallel RPC through shared memory (:82-130) with rank 0 driving.
+"""
+from __future__ import annotations
+
+import os
+import pickle
+from multiprocessing.shared_memory import SharedMemory
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from hilda_vllm_b200 import kernels
+from hilda_vllm_b200.engine.decode_packer import DecodePacker, packet_capacity_bytes
+from hilda_vllm_b200.engine.scheduler import ScheduledSequence
+from hilda_vllm_b200.engine.sequence import Sequence
+from hilda_vllm_b200.layers.attention import Attention
+from hilda_vllm_b200.layers.sampler import Sampler
+from hilda_vllm_b200.models.qwen3 import Qwen3ForCausalLM
+from hilda_vllm_b200.utils.context import get_context, reset_context, set_context
+from hilda_vllm_b200.utils.loader import has_checkpoint, load_model, random_init
+
+MODEL_REGISTRY = {"qwen3": Qwen3ForCausalLM}
+MAX_GRAPH_BS = 512
+
+
+def graph_batch_sizes(max_bs: int) -> list[int]:
+    max_bs = min(max_bs, MAX_GRAPH_BS)
+    return [b for b in (1, 2, 4, 8) if b <= max_bs] + list(range(16, max_bs + 1, 16))
+
+
+def prefill_metadata(seqs: list[ScheduledSequence], block_size: int) -> dict:
+    """Host-side prefill batch description, as the reference's prepare_prefill builds it
+    (mini_vllm/engine/model_runner.py:614-650): concatenated chunk tokens and positions,
+    cu_seqlens_q / cu_seqlens_k (keys = prefix + chunk), their maxima, the slot of every chunk
+    token (block_table[pos // BS] * BS + pos % BS, only for sequences with a block table) and,
+    when any chunk starts after position 0, the -1 padded block tables of all sequences."""
+    ids, pos, slots = [], [], []
+    cu_q, cu_k = [0], [0]
+    max_q = max_k = 0
+    has_prefix = False
+    for sched in seqs:
+        seq = sched.seq
+        start = seq.num_computed_tokens
+        end = start + sched.token_chunk_size
+        ids.extend(seq.token_ids[start:end])
+        p = np.arange(start, end, dtype=np.int64)
+        pos.append(p)
+        cu_q.append(cu_q[-1] + end - start)
+        cu_k.append(cu_k[-1] + end)
+        max_q = max(max_q, end - start)
+        max_k = max(max_k, end)
+        has_prefix = has_prefix or start > 0
+        if seq.block_table:
+            table = np.asarray(seq.block_table, dtype=np.int64)
+            slots.append(table[p // block_size] * block_size + p % block_size)
+    block_tables = None
+    if has_prefix:
+        width = max(len(s.seq.block_table) for s in seqs)
+        block_tables = np.full((len(seqs), width), -1, dtype=np.int32)
+        for i, s in enumerate(seqs):
+            block_tables[i, : len(s.seq.block_table)] = s.seq.block_table
+    return {
+        "input_ids": np.asarray(ids, dtype=np.int64),
+        "positions": np.concatenate(pos) if pos else np.zeros(0, np.int64),
+        "cu_seqlens_q": np.asarray(cu_q, dtype=np.int32),
+        "cu_seqlens_k": np.asarray(cu_k, dtype=np.int32),
+        "max_seqlen_q": max_q,
+        "max_seqlen_k": max_k,
+        "slot_mapping": (np.concatenate(slots) if slots else np.zeros(0, np.int64)).astype(np.int32),
+        "block_tables": block_tables,
+    }
+
+
+class ModelRunner:
+
+    def __init__(self, config, rank: int, event=None):
+        self.config = config
+        hf = config.hf_config
+        self.block_size = config.kvcache_block_size
+        self.max_num_decode_blocks = (config.max_model_len + self.block_size - 1) // self.block_size
+        self.enforce_eager = config.enforce_eager
+        self.world_size = config.tensor_parallel_size
+        self.rank = rank
+        self.event = event
+        self.use_fp8_kv_cache = config.kv_cache_dtype == "fp8"
+        self.last_decode_batch_info = None
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_pool = None
+
+        self.external = getattr(config, "distributed_executor", "spawn") == "external"
+        self.io_bytes = {"h2d": 0, "d2h": 0}
+        self.recording: list[torch.Tensor] | None = None
+        if not dist.is_initialized():
+            port = int(os.getenv("MINI_VLLM_DIST_PORT", "2333"))
+            dist.init_process_group("nccl", f"tcp://127.0.0.1:{port}", world_size=self.world_size, rank=rank)
+        self.rpc_group = None
+        if self.world_size > 1 and self.external:
+            # Ranks launched by torchrun: the control plane is a gloo group (object broadcast
+            # from rank 0) instead of the shared-memory block + events of the spawn mode.
+            self.rpc_group = dist.new_group(backend="gloo")
+        local = int(os.getenv("LOCAL_RANK", rank))
+        torch.cuda.set_device(local)
+        self.device = torch.device("cuda", local)
+        default_dtype = torch.get_default_dtype()
+        torch.set_default_dtype(torch.bfloat16)
+        torch.set_default_device(self.device)
+        try:
+            cls = MODEL_REGISTRY.get(hf.model_type, Qwen3ForCausalLM)
+            self.model = cls(hf)
+            if config.load_format == "auto" and has_checkpoint(config.model):
+                load_model(self.model, config.model)
+            else:
+                random_init(self.model, hf, seed=config.seed, std=config.init_std, device=self.device)
+            self.sampler = Sampler()
+            self.vocab_size = hf.vocab_size
+            self.warmup_model()
+            self.allocate_kv_cache()
+            self.allocate_decode_runtime_buffers()
+            if not self.enforce_eager:
+                self.capture_cudagraph()
+        finally:
+            torch.set_default_device("cpu")
+            torch.set_default_dtype(default_dtype)
+
+        if self.world_size > 1 and not self.external:
+            if rank == 0:
+                self.shm = SharedMemory(name="hilda_b200", create=True, size=2 ** 20)
+                dist.barrier()
+            else:
+                dist.barrier()
+                self.shm = SharedMemory(name="hilda_b200")
+                self.loop()
+        elif self.world_size > 1 and rank > 0:
+            self.loop()
+
+    # ------------------------------------------------------------------ TP control plane
+    def exit(self):
+        if self.world_size > 1 and not self.external:
+            self.shm.close()
+            dist.barrier()
+            if self.rank == 0:
+                self.shm.unlink()
+        self.graphs = {}
+        self.graph_pool = None
+        torch.cuda.synchronize()
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+    def loop(self):
+        while True:
+            method, args = self.read_shm()
+            self.call(method, *args)
+            if method == "exit":
+                break
+
+    def read_shm(self):
+        assert self.world_size > 1 and self.rank > 0
+        if self.external:
+            box = [None]
+            dist.broadcast_object_list(box, src=0, group=self.rpc_group)
+            method, *args = box[0]
+            return method, args
+        self.event.wait()
+        n = int.from_bytes(self.shm.buf[0:4], "little")
+        method, *args = pickle.loads(self.shm.buf[4:n + 4])
+        self.event.clear()
+        return method, args
+
+    def write_shm(self, method, *args):
+        assert self.world_size > 1 and self.rank == 0
+        if self.external:
+            dist.broadcast_object_list([[method, *args]], src=0, group=self.rpc_group)
+            return
+        data = pickle.dumps([method, *args])
+        self.shm.buf[0:4] = len(data).to_bytes(4, "little")
+        self.shm.buf[4:len(data) + 4] = data
+        for ev in self.event:
+            ev.set()
+
+    def call(self, method, *args):
+        if self.world_size > 1 and self.rank == 0:
+            self.write_shm(method, *args)
+        return getattr(self, method)(*args)
+
+    # ------------------------------------------------------------------ memory
+    def attention_layers(self) -> list[Attention]:
+        return [m for m in self.model.modules() if isinstance(m, Attention)]
+
+    @torch.inference_mode()
+    def warmup_model(self):
+        """Largest prefill (max_num_batched_tokens tokens) before the KV pool exists, so the
+        activation peak is known when the pool is sized (model_runner.py:132-139)."""
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats()
+        max_tokens, max_len = self.config.max_num_batched_tokens, self.config.max_model_len
+        num_seqs = max(1, min(max_tokens // max_len, self.config.max_num_seqs))
+        seqs = [ScheduledSequence(Sequence([0] * max_len), max_len) for _ in range(num_seqs)]
+        input_ids, positions = self.prepare_prefill(seqs)
+        self.model.compute_logits(self.model(input_ids, positions))
+        reset_context()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+    def kv_block_bytes(self) -> int:
+        hf = self.config.hf_config
+        hk = hf.num_key_value_heads // self.world_size
+        d = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
+        per_elem = 2 + (1 if self.use_fp8_kv_cache else 0)
+        return 2 * hf.num_hidden_layers * self.block_size * hk * d * per_elem
+
+    def allocate_kv_cache(self):
+        config = self.config
+        hf = config.hf_config
+        free, total = torch.cuda.mem_get_info()
+        used = total - free
+        stats = torch.cuda.memory_stats()
+        peak, current = stats["allocated_bytes.all.peak"], stats["allocated_bytes.all.current"]
+        # Room for the decode buffers, graph pool and workspace that are allocated afterwards.
+        reserve = 2 << 30
+        budget = int(total * config.gpu_memory_utilization - used - peak + current) - reserve
+        num_blocks = budget // self.kv_block_bytes()
+        if config.kvcache_block_cap > 0:
+            num_blocks = min(num_blocks, config.kvcache_block_cap)
+        config.num_kvcache_blocks = int(num_blocks)
+        assert config.num_kvcache_blocks > 0, "no memory left for the KV cache"
+        hk = hf.num_key_value_heads // self.world_size
+        d = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
+        shape = (2, hf.num_hidden_layers, config.num_kvcache_blocks, self.block_size, hk, d)
+        layers = self.attention_layers()
+        if self.use_fp8_kv_cache:
+            self.prefill_kv_cache = torch.empty(shape, dtype=torch.bfloat16)
+            self.decode_kv_cache = torch.empty(shape, dtype=torch.float8_e4m3fn)
+            self.kv_scales = torch.full((2, hf.num_hidden_layers, hk), float(config.kv_cache_scale),
+                                        dtype=torch.float32)
+        else:
+            self.kv_cache = torch.empty(shape, dtype=torch.bfloat16)
+        for layer_id, module in enumerate(layers):
+            module.kv_cache_dtype = config.kv_cache_dtype
+            if self.use_fp8_kv_cache:
+                module.prefill_k_cache = self.prefill_kv_cache[0, layer_id]
+                module.prefill_v_cache = self.prefill_kv_cache[1, layer_id]
+                module.decode_k_cache = self.decode_kv_cache[0, layer_id]
+                module.decode_v_cache = self.decode_kv_cache[1, layer_id]
+                module.k_cache = module.prefill_k_cache
+                module.v_cache = module.prefill_v_cache
+                module.k_scale = self.kv_scales[0, layer_id]
+                module.v_scale = self.kv_scales[1, layer_id]
+            else:
+                module.k_cache = self.kv_cache[0, layer_id]
+                module.v_cache = self.kv_cache[1, layer_id]
+
+    @torch.inference_mode()
+    def convert_prefill_to_decode_cache(self, seqs: list[Sequence]):
+        """FP8 mode: quantise the BF16 prefill-cache rows of every prompt token of `seqs` into
+        the FP8 decode cache, all layers in one launch (model_runner.py:483-502)."""
+        if not self.use_fp8_kv_cache or not seqs:
+            return
+        bs = self.block_size
+        slots = []
+        for seq in seqs:
+            table = np.asarray(seq.block_table, dtype=np.int64)
+            pos = np.arange(seq.num_prompt_tokens, dtype=np.int64)
+            slots.append(table[pos // bs] * bs + pos % bs)
+        slot_mapping = torch.from_numpy(np.concatenate(slots).astype(np.int32)).to(self.device, non_blocking=True)
+        kernels.copy_kvcache_fp8_layers(self.prefill_kv_cache[0], self.prefill_kv_cache[1],
+                                        self.decode_kv_cache[0], self.decode_kv_cache[1], slot_mapping,
+                                        self.kv_scales[0], self.kv_scales[1])
+
+    @torch.inference_mode()
+    def allocate_decode_runtime_buffers(self):
+        hf = self.config.hf_config
+        self.max_bs = max_bs = self.config.max_num_seqs
+        mb = self.max_num_decode_blocks
+        dev = self.device
+        # Persistent decode buffers: read by the captured graphs, written by the pack kernel.
+        self.graph_vars = dict(
+            input_ids=torch.zeros(max_bs, dtype=torch.int64, device=dev),
+            positions=torch.zeros(max_bs, dtype=torch.int64, device=dev),
+            slot_mapping=torch.full((max_bs,), -1, dtype=torch.int32, device=dev),
+            context_lens=torch.zeros(max_bs, dtype=torch.int32, device=dev),
+            block_tables=torch.full((max_bs, mb), -1, dtype=torch.int32, device=dev),
+            outputs=torch.zeros(max_bs, hf.hidden_size, dtype=torch.bfloat16, device=dev),
+            next_tokens=torch.zeros(max_bs, dtype=torch.int64, device=dev),
+            slot_seq_ids=torch.full((max_bs,), -1, dtype=torch.int64, device=dev),
+            slot_bt_lens=torch.zeros(max_bs, dtype=torch.int32, device=dev),
+        )
+        cap = packet_capacity_bytes(max_bs, mb)
+        cap = (cap + 15) & ~15
+        self.packet_dev = torch.zeros(cap, dtype=torch.uint8, device=dev)
+        self.packet_host = torch.zeros(cap, dtype=torch.uint8, device="cpu", pin_memory=True)
+        self.packer = DecodePacker(max_bs, mb, self.packet_host.numpy())
+        self.tokens_host = torch.zeros(max_bs, dtype=torch.int64, device="cpu", pin_memory=True)
+        self.copy_done = torch.cuda.Event()
+        hq = hf.num_attention_heads // self.world_size
+        d = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
+        self.decode_workspace = kernels.make_decode_workspace(max_bs, hq, d, mb, self.block_size, dev)
+        for module in self.attention_layers():
+            module.decode_workspace = self.decode_workspace
+        self.logits_buf = None
+
+    # ------------------------------------------------------------------ batch preparation
+    def prepare_prefill(self, seqs: list[ScheduledSequence]):
+        """Varlen metadata for the scheduled prefill chunks (model_runner.py:614-650)."""
+        meta = prefill_metadata(seqs, self.block_size)
+        dev = self.device
+
+        def h2d(arr):
+            self.io_bytes["h2d"] += arr.nbytes
+            return torch.from_numpy(arr).pin_memory().to(dev, non_blocking=True)
+
+        input_ids = h2d(meta["input_ids"])
+        positions = h2d(meta["positions"])
+        bt = meta["block_tables"]
+        set_context(True, h2d(meta["cu_seqlens_q"]), h2d(meta["cu_seqlens_k"]), meta["max_seqlen_q"],
+                    meta["max_seqlen_k"], h2d(meta["slot_mapping"]), None, None if bt is None else h2d(bt))
+        return input_ids, positions
+
+    def _decode_graph_batch_size(self, bs: int) -> int:
+        if self.enforce_eager or bs > MAX_GRAPH_BS:
+            return bs
+        return next(g for g in self.graph_bs if g >= bs)
+
+    @torch.inference_mode()
+    def prepare_decode(self, scheduled_seqs: list[ScheduledSequence]) -> int:
+        """Builds this step's packet on the host and copies it to the device; returns the
+        graph batch size.  The graph (or the eager path) then runs the pack kernel."""
+        bs = len(scheduled_seqs)
+        graph_bs = self._decode_graph_batch_size(bs)
+        nbytes = self.packer.build(scheduled_seqs, graph_bs)
+        self.packet_dev[:nbytes].copy_(self.packet_host[:nbytes], non_blocking=True)
+        self.io_bytes["h2d"] += nbytes
+        if self.recording is not None:
+            self.recording.append(self.packet_dev[:nbytes].clone())
+        active = sum(1 for s in scheduled_seqs if not s.is_padding)
+        self.last_decode_batch_info = {"scheduled_bs": bs, "graph_bs": graph_bs, "active_seqs": active,
+                                       "padded_slots": bs - active, "pack_events": self.packer.last_num_events}
+        return graph_bs
+
+    def _set_decode_context(self, n: int):
+        gv = self.graph_vars
+        set_context(False, slot_mapping=gv["slot_mapping"][:n], context_lens=gv["context_lens"][:n],
+                    block_tables=gv["block_tables"][:n])
+
+    def _decode_body(self, n: int, greedy: bool):
+        """Pack kernel + model + LM head (+ argmax) over the first n decode slots."""
+        gv = self.graph_vars
+        kernels.pack_decode_batch(self.packet_dev, n, self.block_size, gv["slot_seq_ids"], gv["slot_bt_lens"],
+                                  gv["next_tokens"], gv["input_ids"], gv["positions"], gv["slot_mapping"],
+                                  gv["context_lens"], gv["block_tables"])
+        self._set_decode_context(n)
+        hidden = self.model(gv["input_ids"][:n], gv["positions"][:n])
+        gv["outputs"][:n] = hidden
+        logits = self.logits_buf[:n]
+        torch.matmul(hidden, self.model.lm_head.weight.t(), out=logits)
+        if greedy and self.world_size == 1:
+            kernels.argmax(logits, gv["next_tokens"][:n])
+        return logits
+
+    def _ensure_logits_buf(self, rows: int):
+        vocab_local = self.model.lm_head.num_embeddings_per_partition
+        if self.logits_buf is None or self.logits_buf.shape[0] < rows:
+            self.logits_buf = torch.zeros(rows, vocab_local, dtype=torch.bfloat16, device=self.device)
+
+    def prepare_sample(self, seqs: list[Sequence]):
+        temps = torch.tensor([s.temperature for s in seqs], dtype=torch.float32).pin_memory()
+        ks = torch.tensor([s.top_k for s in seqs], dtype=torch.int32).pin_memory()
+        ps = torch.tensor([s.top_p for s in seqs], dtype=torch.float32).pin_memory()
+        return (temps.to(self.device, non_blocking=True), ks.to(self.device, non_blocking=True),
+                ps.to(self.device, non_blocking=True))
+
+    # ------------------------------------------------------------------ running
+    @torch.inference_mode()
+    def run(self, scheduled_seqs: list[ScheduledSequence], is_prefill: bool) -> list[int | None] | None:
+        if is_prefill:
+            return self._run_prefill(scheduled_seqs)
+        return self._run_decode(scheduled_seqs)
+
+    def _sample_rows(self, logits: torch.Tensor, seqs: list[Sequence]) -> list[int]:
+        if all(s.greedy for s in seqs):
+            return kernels.argmax(logits).tolist()
+        temps, ks, ps = self.prepare_sample(seqs)
+        sampled = self.sampler(logits, temps, ks, ps)
+        greedy_rows = [i for i, s in enumerate(seqs) if s.greedy]
+        if greedy_rows:
+            idx = torch.tensor(greedy_rows, device=self.device)
+            sampled[idx] = kernels.argmax(logits[idx].contiguous())
+        return sampled.tolist()
+
+    def _gather_logits(self, logits: torch.Tensor) -> torch.Tensor | None:
+        if self.world_size == 1:
+            return logits
+        parts = [torch.empty_like(logits) for _ in range(self.world_size)] if self.rank == 0 else None
+        dist.gather(logits, parts, 0)
+        return torch.cat(parts, -1) if self.rank == 0 else None
+
+    def _run_prefill(self, scheduled_seqs):
+        seqs = [s.seq for s in scheduled_seqs]
+        input_ids, positions = self.prepare_prefill(scheduled_seqs)
+        hidden = self.model(input_ids, positions)
+        logits = self._gather_logits(self.model.lm_head.local_logits(hidden))
+        token_ids = None
+        if self.rank == 0:
+            token_ids = [None] * len(scheduled_seqs)
+            rows = [i for i, s in enumerate(scheduled_seqs) if s.requires_sampling]
+            if rows:
+                sub = logits[rows] if len(rows) != logits.shape[0] else logits
+                sampled = self._sample_rows(sub.contiguous(), [seqs[i] for i in rows])
+                for i, t in zip(rows, sampled):
+                    token_ids[i] = t
+        reset_context()
+        return token_ids
+
+    def _run_decode(self, scheduled_seqs):
+        bs = len(scheduled_seqs)
+        graph_bs = self.prepare_decode(scheduled_seqs)
+        real = [i for i, s in enumerate(scheduled_seqs) if not s.is_padding]
+        real_seqs = [scheduled_seqs[i].seq for i in real]
+        greedy = all(s.greedy for s in real_seqs)
+        gv = self.graph_vars
+        if graph_bs in self.graphs and greedy and self.world_size == 1:
+            self.graphs[graph_bs].replay()
+            logits = None
+        else:
+            n = graph_bs
+            if graph_bs in self.graphs:
+                self.graphs[graph_bs].replay()
+                logits = self.logits_buf[:n]
+            else:
+                self._ensure_logits_buf(n)
+                logits = self._decode_body(n, greedy=False)
+            logits = self._gather_logits(logits)
+            if self.rank == 0 and real:
+                sub = logits[real].contiguous()
+                sampled = torch.tensor(self._sample_rows(sub, real_seqs), dtype=torch.int64)
+                toks = torch.zeros(bs, dtype=torch.int64)
+                toks[real] = sampled
+                gv["next_tokens"][:bs].copy_(toks.pin_memory(), non_blocking=True)
+            if self.world_size > 1:
+                dist.broadcast(gv["next_tokens"][:bs], 0)
+        # One device->host copy of the step's tokens.
+        self.tokens_host[:bs].copy_(gv["next_tokens"][:bs], non_blocking=True)
+        self.io_bytes["d2h"] += 8 * bs
+        self.copy_done.record()
+        self.copy_done.synchronize()
+        tokens = self.tokens_host[:bs].tolist()
+        self.packer.note_sampled(bs, tokens)
+        reset_context()
+        if self.rank != 0:
+            return None
+        out = [None] * bs
+        for i in real:
+            out[i] = tokens[i]
+        return out
+
+    @torch.inference_mode()
+    def capture_cudagraph(self):
+        self.graph_bs = graph_batch_sizes(self.config.max_num_seqs)
+        greedy = self.world_size == 1
+        self._ensure_logits_buf(self.graph_bs[-1])
+        # The packet is all zeros during capture: batch 0, every slot padding.
+        self.packet_dev.zero_()
+        for bs in reversed(self.graph_bs):
+            graph = torch.cuda.CUDAGraph()
+            self._decode_body(bs, greedy)  # warm-up outside the graph
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, self.graph_pool):
+                self._decode_body(bs, greedy)
+            if self.graph_pool is None:
+                self.graph_pool = graph.pool()
+            self.graphs[bs] = graph
+            torch.cuda.synchronize()
+            reset_context()
+        # Capture ran the pack kernel on an empty packet: reset the device-side slot state.
+        gv = self.graph_vars
+        gv["slot_seq_ids"].fill_(-1)
+        gv["slot_bt_lens"].zero_()
+        gv["block_tables"].fill_(-1)
+        gv["context_lens"].zero_()
+        gv["slot_mapping"].fill_(-1)
+        self.packer.forget_tokens()
+        torch.cuda.synchronize()
+
+    # ------------------------------------------------------------------ benchmarking support
+    def record_packets(self, enable: bool):
+        """Start (or stop) keeping a device copy of every decode packet sent."""
+        self.recording = [] if enable else None
+
+    def take_recording(self) -> list[torch.Tensor]:
+        rec, self.recording = self.recording or [], None
+        self.recorded_packets = rec
+        return rec
+
+    def reset_decode_state(self):
+        """Forget every decode slot (device buffers and the host mirror)."""
+        gv = self.graph_vars
+        gv["slot_seq_ids"].fill_(-1)
+        gv["slot_bt_lens"].zero_()
+        gv["block_tables"].fill_(-1)
+        gv["context_lens"].zero_()
+        gv["slot_mapping"].fill_(-1)
+        gv["positions"].zero_()
+        self.packer = DecodePacker(self.max_bs, self.max_num_decode_blocks, self.packet_host.numpy())
+
+    @torch.inference_mode()
+    def replay_recorded(self, bs: int, probe_every: int = 0):
+        """Replays the recorded decode packets back to back on the device (each: a device-to-
+        device packet copy + one graph replay, tokens fed back through next_tokens).  Returns
+        the elapsed seconds measured with CUDA events on the launching stream, and, when
+        probe_every > 0, (algorithmic bytes, seconds) samples of the layer-0 decode kernel timed
+        on its own between steps."""
+        graph = self.graphs[self._decode_graph_batch_size(bs)]
+        stream = torch.cuda.current_stream()
+        samples = []
+        if self.world_size > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i, pkt in enumerate(self.recorded_packets):
+            self.packet_dev[: pkt.numel()].copy_(pkt, non_blocking=True)
+            graph.replay()
+            if probe_every and i % probe_every == probe_every // 2:
+                samples.append(self._probe_decode(bs))
+        end.record(stream)
+        torch.cuda.synchronize()
+        elapsed = start.elapsed_time(end) / 1e3
+        if self.world_size > 1:  # the job is as slow as its slowest rank
+            t = torch.tensor([elapsed], device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            elapsed = float(t.item())
+        return elapsed, samples
+
+    def _probe_decode(self, bs: int):
+        hf = self.config.hf_config
+        hq = hf.num_attention_heads // self.world_size
+        hk = hf.num_key_value_heads // self.world_size
+        d = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
+        layer = self.attention_layers()[0]
+        gv = self.graph_vars
+        q = torch.randn(bs, hq, d, dtype=torch.bfloat16, device=self.device)
+        out = torch.empty_like(q)
+        ctx, bt = gv["context_lens"][:bs], gv["block_tables"][:bs]
+        k_cache = layer.decode_k_cache if self.use_fp8_kv_cache else layer.k_cache
+        v_cache = layer.decode_v_cache if self.use_fp8_kv_cache else layer.v_cache
+        elem = 1 if self.use_fp8_kv_cache else 2
+
+        def launch():
+            kernels.paged_decode(q, k_cache, v_cache, bt, ctx, layer.scale, out=out, workspace=self.decode_workspace,
+                                 k_scale=layer.k_scale, v_scale=layer.v_scale)
+
+        for _ in range(3):
+            launch()
+        stream = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        e0.record(stream)
+        for _ in range(reps):
+            launch()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        lens = ctx.tolist()
+        nbytes = sum(lens) * hk * d * elem * 2 + bs * hq * d * 2 * 2
+        return nbytes, e0.elapsed_time(e1) / 1e3 / reps

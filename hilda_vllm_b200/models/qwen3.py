@@ -1,0 +1,147 @@
+"""Qwen3 decoder (mini_vllm/models/qwen3.py:15-218) on the sm_100a kernels.
+
+Module names and parameter names match the reference (and Hugging Face checkpoints), so the
+reference's weight loader mapping works unchanged.  Per layer of a decode step the GPU runs:
+add+RMSNorm, qkv GEMM, fused QK-RMSNorm+RoPE (in place on the qkv rows), KV store + paged
+decode attention, o_proj GEMM (+ all-reduce under TP), add+RMSNorm, gate_up GEMM, SiLU*mul,
+down GEMM (+ all-reduce).
+"""
+import torch
+from torch import nn
+
+from hilda_vllm_b200 import kernels
+from hilda_vllm_b200.layers.activation import SiluAndMul
+from hilda_vllm_b200.layers.attention import Attention
+from hilda_vllm_b200.layers.embed_head import ParallelLMHead, VocabParallelEmbedding
+from hilda_vllm_b200.layers.layernorm import RMSNorm
+from hilda_vllm_b200.layers.linear import MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear, _tp
+from hilda_vllm_b200.layers.rotary_embedding import get_rope
+
+
+class Qwen3Attention(nn.Module):
+
+    def __init__(self, hidden_size: int, num_heads: int, num_kv_heads: int, max_position: int = 4096 * 32,
+                 head_dim: int | None = None, rms_norm_eps: float = 1e-06, qkv_bias: bool = False,
+                 rope_theta: float = 10000, rope_scaling: tuple | None = None) -> None:
+        super().__init__()
+        _, tp_size = _tp()
+        self.total_num_heads = num_heads
+        assert num_heads % tp_size == 0 and num_kv_heads % tp_size == 0
+        self.num_heads = num_heads // tp_size
+        self.total_num_kv_heads = num_kv_heads
+        self.num_kv_heads = num_kv_heads // tp_size
+        self.head_dim = head_dim or hidden_size // num_heads
+        self.q_size = self.num_heads * self.head_dim
+        self.kv_size = self.num_kv_heads * self.head_dim
+        self.scaling = self.head_dim ** -0.5
+        self.qkv_bias = qkv_bias
+        if qkv_bias:
+            raise NotImplementedError("Qwen2-style qkv bias is not part of this build")
+        self.rms_norm_eps = rms_norm_eps
+        self.qkv_proj = QKVParallelLinear(hidden_size, self.head_dim, num_heads, num_kv_heads, bias=False)
+        self.o_proj = RowParallelLinear(num_heads * self.head_dim, hidden_size, bias=False)
+        self.rotary_emb = get_rope(self.head_dim, rotary_dim=self.head_dim, max_position=max_position,
+                                   base=rope_theta, rope_scaling=rope_scaling)
+        self.attn = Attention(self.num_heads, self.head_dim, self.scaling, self.num_kv_heads)
+        self.q_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
+        self.k_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
+
+    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
+        qkv = self.qkv_proj(hidden_states)
+        kernels.qk_norm_rope(qkv, self.num_heads, self.num_kv_heads, self.head_dim, self.q_norm.weight,
+                             self.k_norm.weight, self.rotary_emb.cos_sin_cache, positions, self.rms_norm_eps)
+        q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
+        q = q.view(-1, self.num_heads, self.head_dim)
+        k = k.view(-1, self.num_kv_heads, self.head_dim)
+        v = v.view(-1, self.num_kv_heads, self.head_dim)
+        o = self.attn(q, k, v)
+        return self.o_proj(o.flatten(1, -1))
+
+
+class Qwen3MLP(nn.Module):
+
+    def __init__(self, hidden_size: int, intermediate_size: int, hidden_act: str) -> None:
+        super().__init__()
+        self.gate_up_proj = MergedColumnParallelLinear(hidden_size, [intermediate_size] * 2, bias=False)
+        self.down_proj = RowParallelLinear(intermediate_size, hidden_size, bias=False)
+        assert hidden_act == "silu"
+        self.act_fn = SiluAndMul()
+
+    def forward(self, x):
+        return self.down_proj(self.act_fn(self.gate_up_proj(x)))
+
+
+class Qwen3DecoderLayer(nn.Module):
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        self.self_attn = Qwen3Attention(
+            hidden_size=config.hidden_size,
+            num_heads=config.num_attention_heads,
+            num_kv_heads=config.num_key_value_heads,
+            max_position=config.max_position_embeddings,
+            rms_norm_eps=config.rms_norm_eps,
+            qkv_bias=getattr(config, "attention_bias", False),
+            head_dim=getattr(config, "head_dim", None),
+            rope_theta=getattr(config, "rope_theta", 1000000),
+            rope_scaling=getattr(config, "rope_scaling", None),
+        )
+        self.mlp = Qwen3MLP(config.hidden_size, config.intermediate_size, config.hidden_act)
+        self.input_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    def forward(self, positions, hidden_states, residual):
+        if residual is None:
+            hidden_states, residual = self.input_layernorm(hidden_states), hidden_states
+        else:
+            hidden_states, residual = self.input_layernorm(hidden_states, residual)
+        hidden_states = self.self_attn(positions, hidden_states)
+        hidden_states, residual = self.post_attention_layernorm(hidden_states, residual)
+        return self.mlp(hidden_states), residual
+
+
+class Qwen3Model(nn.Module):
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        self.embed_tokens = VocabParallelEmbedding(config.vocab_size, config.hidden_size)
+        self.layers = nn.ModuleList([Qwen3DecoderLayer(config) for _ in range(config.num_hidden_layers)])
+        self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    def forward(self, input_ids, positions):
+        hidden_states = self.embed_tokens(input_ids)
+        residual = None
+        for layer in self.layers:
+            hidden_states, residual = layer(positions, hidden_states, residual)
+        hidden_states, _ = self.norm(hidden_states, residual)
+        return hidden_states
+
+
+class Qwen3ForCausalLM(nn.Module):
+    packed_modules_mapping = {
+        "q_proj": ("qkv_proj", "q"),
+        "k_proj": ("qkv_proj", "k"),
+        "v_proj": ("qkv_proj", "v"),
+        "gate_proj": ("gate_up_proj", 0),
+        "up_proj": ("gate_up_proj", 1),
+    }
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        self.model = Qwen3Model(config)
+        self.lm_head = ParallelLMHead(config.vocab_size, config.hidden_size)
+        self.tie_word_embeddings = bool(getattr(config, "tie_word_embeddings", False))
+        if self.tie_word_embeddings:
+            self.tie_weights()
+
+    def tie_weights(self):
+        """LM head = this rank's vocabulary shard of the (replicated) embedding table."""
+        head = self.lm_head
+        rows = head.num_embeddings_per_partition
+        head.weight.data = self.model.embed_tokens.weight.data.narrow(0, head.vocab_start_idx, rows)
+
+    def forward(self, input_ids, positions):
+        return self.model(input_ids, positions)
+
+    def compute_logits(self, hidden_states):
+        return self.lm_head(hidden_states)

@@ -1,0 +1,230 @@
+/*
+ * hilda_b200.h — C ABI of the B200 (sm_100a) continuous-batching attention path.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, element strides and sizes (no framework types);
+ *   - launches on the caller's CUDA stream (`stream` is a cudaStream_t passed as void*);
+ *   - performs no allocation and no host synchronisation, so it can be captured in a
+ *     CUDA graph (the caller owns every buffer, including workspaces);
+ *   - returns HL_OK (0) or a non-zero hl_status; hl_last_error_string() then describes
+ *     the failure (thread-local, valid until the next call on the same thread).
+ *
+ * Memory layouts follow the reference engine (mini_vllm):
+ *   - paged KV cache, per layer and per K/V: [num_blocks, block_size, num_kv_heads, head_dim],
+ *     row-major, i.e. one "slot" (token) is num_kv_heads*head_dim contiguous elements
+ *     (mini_vllm/engine/model_runner.py:196-219);
+ *   - slot = block_id * block_size + offset_in_block; slot -1 means "do not store"
+ *     (mini_vllm/layers/attention.py:59-80);
+ *   - block_tables[b, i] = physical block of the i-th page of sequence b, -1 padded
+ *     (mini_vllm/engine/model_runner.py:551-584, 608-612).
+ */
+#ifndef HILDA_B200_H
+#define HILDA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  HL_OK = 0,
+  HL_ERR_INVALID = 1,      /* bad argument: shape, stride, alignment, null pointer */
+  HL_ERR_CUDA = 2,         /* a CUDA runtime call or kernel launch failed */
+  HL_ERR_UNSUPPORTED = 3,  /* a configuration the kernels are not built for */
+  HL_ERR_WORKSPACE = 4     /* workspace missing or too small */
+} hl_status;
+
+typedef enum {
+  HL_KV_BF16 = 0,
+  HL_KV_FP8_E4M3 = 1
+} hl_kv_dtype;
+
+/* Description of the last error on this thread ("" if none). */
+const char* hl_last_error_string(void);
+
+/* Library version, for load checks. */
+int hl_version(void);
+
+/* ------------------------------------------------------------------------------------
+ * KV store (scatter new K/V rows into the paged cache by slot_mapping).
+ * Replaces store_kvcache / store_kvcache_kernel, mini_vllm/layers/attention.py:59-90.
+ * key/value: [num_tokens, num_kv_heads, head_dim] bf16 with head stride head_dim and
+ * element stride 1 (the reference asserts the same, attention.py:86-89); their row
+ * strides (elements between consecutive tokens) may exceed num_kv_heads*head_dim because
+ * they are views into the fused qkv projection output.
+ * Slots equal to -1 are skipped; slots outside [0, num_slots) are skipped too (the
+ * reference kernel would write out of bounds there).
+ * ---------------------------------------------------------------------------------- */
+int hl_store_kv_bf16(const void* key, const void* value,
+                     int64_t key_row_stride, int64_t value_row_stride,
+                     void* k_cache, void* v_cache,
+                     const int32_t* slot_mapping, int64_t num_tokens, int64_t num_slots,
+                     int num_kv_heads, int head_dim, void* stream);
+
+/* FP8 e4m3 store with per-KV-head fp32 scales: cache = sat_e4m3(round_to_nearest_even(x / scale[h])).
+ * Replaces store_kvcache_fp8 -> hilda_store_kvcache_fp8, mini_vllm/layers/attention.py:51-52,133
+ * (the reference signature has no scales; unit scales reproduce it). */
+int hl_store_kv_fp8(const void* key, const void* value,
+                    int64_t key_row_stride, int64_t value_row_stride,
+                    void* k_cache, void* v_cache,
+                    const int32_t* slot_mapping, int64_t num_tokens, int64_t num_slots,
+                    int num_kv_heads, int head_dim,
+                    const float* k_scale, const float* v_scale, void* stream);
+
+/* Gather BF16 prefill-cache rows at slot_mapping and quantise them into the FP8 decode cache
+ * at the same slots, for num_layers layers at once (layer l uses base + l*layer_stride,
+ * strides in elements; scales advance by scale_layer_stride floats per layer).
+ * Replaces copy_kvcache_fp8 -> hilda_copy_kvcache_fp8, mini_vllm/layers/attention.py:55-56,
+ * called per layer by convert_prefill_to_decode_cache, mini_vllm/engine/model_runner.py:484-502. */
+int hl_copy_kv_bf16_to_fp8(const void* src_k, const void* src_v, void* dst_k, void* dst_v,
+                           const int32_t* slot_mapping, int64_t num_tokens, int64_t num_slots,
+                           int num_kv_heads, int head_dim,
+                           const float* k_scale, const float* v_scale,
+                           int num_layers, int64_t src_layer_stride, int64_t dst_layer_stride,
+                           int64_t scale_layer_stride, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Paged decode attention (one query token per sequence), split-K flash-decoding with an
+ * in-kernel last-CTA reduction.
+ * Replaces flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache, cache_seqlens=context_lens,
+ * block_table=block_tables, softmax_scale, causal=True), mini_vllm/layers/attention.py:162-170,
+ * and hilda_paged_attention_fp8_decode, attention.py:134-141 (kv_dtype = HL_KV_FP8_E4M3;
+ * k_scale/v_scale may be NULL for unit scales).
+ *   q:   [B, Hq, D] bf16, head stride D, row stride q_row_stride (elements)
+ *   out: [B, Hq, D] bf16, row stride out_row_stride (elements)
+ *   block_tables: [B, bt_stride] int32; only the first max_blocks_per_seq entries are read
+ *   context_lens: [B] int32; rows with 0 produce zeros.
+ * Requires head_dim == 128, block_size % 256 == 0, Hq % Hk == 0, Hk in {1,2,4,8},
+ * Hq/Hk in {1,2,4,8}.  The workspace (>= hl_paged_decode_workspace_size bytes) must be
+ * zero-filled once before first use; the kernel leaves it ready for the next launch.
+ * Launches that share one workspace must not overlap on the GPU.
+ * ---------------------------------------------------------------------------------- */
+int64_t hl_paged_decode_workspace_size(int batch, int num_q_heads, int head_dim,
+                                       int max_blocks_per_seq, int block_size);
+
+int hl_paged_decode(const void* q, int64_t q_row_stride,
+                    const void* k_cache, const void* v_cache, int kv_dtype,
+                    const float* k_scale, const float* v_scale,
+                    const int32_t* block_tables, int64_t bt_stride, int max_blocks_per_seq,
+                    const int32_t* context_lens, int batch,
+                    int num_q_heads, int num_kv_heads, int head_dim,
+                    int block_size, int64_t num_blocks, float softmax_scale,
+                    void* out, int64_t out_row_stride,
+                    void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Reads the error word the decode kernel keeps in its workspace (bit 0: an mbarrier wait
+ * timed out; bit 1: a block id was out of range).  Synchronous: copies 4 bytes to host. */
+int hl_paged_decode_read_errors(const void* workspace, int32_t* errors_out, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Varlen causal prefill attention (bottom-right aligned causal mask), optionally reading
+ * K/V (prefix + chunk) from the paged cache through block_tables.
+ * Replaces flash_attn_varlen_func(q, k|k_cache, v|v_cache, cu_seqlens_q, cu_seqlens_k,
+ * max_seqlen_q, max_seqlen_k, softmax_scale, causal=True, block_table),
+ * mini_vllm/layers/attention.py:120-131,149-160.
+ *   q:   [Tq, Hq, D] bf16 (row stride q_row_stride), out [Tq, Hq, D] (row stride out_row_stride)
+ *   paged (block_tables != NULL): k/v are the caches [num_blocks, block_size, Hk, D];
+ *   contiguous (block_tables == NULL): k/v are [Tk, Hk, D] with row strides k_row_stride,
+ *   v_row_stride, and sequence s's keys are rows cu_seqlens_k[s] .. cu_seqlens_k[s+1]-1.
+ * Requires head_dim == 128 and Hq % Hk == 0.
+ * ---------------------------------------------------------------------------------- */
+int hl_varlen_prefill(const void* q, int64_t q_row_stride,
+                      const void* k, const void* v, int64_t k_row_stride, int64_t v_row_stride,
+                      const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                      const int32_t* block_tables, int64_t bt_stride,
+                      int num_seqs, int max_seqlen_q, int max_seqlen_k,
+                      int num_q_heads, int num_kv_heads, int head_dim,
+                      int block_size, int64_t num_blocks, float softmax_scale,
+                      void* out, int64_t out_row_stride, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Decode-batch packing on the GPU.
+ * Replaces the host loop of ModelRunner.prepare_decode and its block-table row sync,
+ * mini_vllm/engine/model_runner.py:551-584 (_clear_decode_block_table_slot,
+ * _copy_decode_block_table_row, _sync_decode_block_table_row) and :652-720.
+ * The persistent graph buffers (input_ids int64, positions int64, slot_mapping int32,
+ * context_lens int32, block_tables int32 [>= graph_batch rows, bt_stride]) are rebuilt in
+ * place from the device's own per-slot state (slot_seq_ids, slot_bt_lens, the previous
+ * context_lens) plus a compact host packet of slot events.  A slot in [0, batch) without an
+ * event is "continuing": if it has an owner (slot_seq_ids != -1) its context length grows by
+ * one and its input id becomes next_tokens[slot] (the token sampled for it in the previous
+ * decode step); if it has no owner it is padding.  Slots in [batch, graph_batch) get
+ * position 0, context length 0 and slot -1 as the reference pads them
+ * (model_runner.py:709-712); their input ids and block-table rows are left as they are.
+ *
+ * The packet lives in device memory so one launch can be captured in a CUDA graph and
+ * replayed with a new packet each step (one host->device copy of the used bytes):
+ *   hl_pack_header, then num_events hl_pack_event records, then pool_len int32 block ids
+ *   starting at byte pool_offset.  At most one event per slot; graph_batch <= 1024.
+ * Out-of-range fields are ignored by the kernel (batch is clamped to graph_batch, events
+ * outside the packet or for slots >= batch are skipped, pool reads stay inside the pool).
+ * ---------------------------------------------------------------------------------- */
+typedef struct {
+  int32_t num_events;
+  int32_t batch;        /* scheduled decode batch (slots [0, batch) are live or padding) */
+  int32_t pool_offset;  /* byte offset of the block-id pool from the start of the packet */
+  int32_t pool_len;     /* number of int32 block ids in the pool */
+} hl_pack_header;
+
+typedef struct {
+  int32_t flags;      /* HL_EV_* bit set */
+  int32_t slot;       /* decode slot index, < batch */
+  int32_t ctx_len;    /* HL_EV_SCALARS: context length (tokens) of the owning sequence */
+  int32_t bt_len;     /* HL_EV_SCALARS / HL_EV_ROW: block-table length after this event */
+  int64_t seq_id;     /* HL_EV_SCALARS: id of the owning sequence */
+  int64_t token;      /* HL_EV_SCALARS: last token id of the owning sequence */
+  int32_t row_start;  /* HL_EV_ROW: first block-table entry written */
+  int32_t row_count;  /* HL_EV_ROW: number of entries written from the pool */
+  int32_t pool_off;   /* HL_EV_ROW: index of the first entry in the pool */
+  int32_t reserved;
+} hl_pack_event;
+
+enum {
+  HL_EV_SCALARS = 1,   /* slot owned by seq_id with ctx_len tokens, last token `token` */
+  HL_EV_ROW = 2,       /* row[row_start : row_start+row_count] := pool[pool_off : ...] */
+  HL_EV_ROW_FILL = 4,  /* with HL_EV_ROW: row[row_start+row_count :] := -1 (full rewrite) */
+  HL_EV_CLEAR = 8      /* padding slot that had an owner: row := -1, owner and length forgotten */
+};
+
+int hl_pack_decode_batch(const void* packet, int64_t packet_bytes, int graph_batch, int block_size,
+                         int64_t* slot_seq_ids, int32_t* slot_bt_lens, const int64_t* next_tokens,
+                         int64_t* input_ids, int64_t* positions, int32_t* slot_mapping,
+                         int32_t* context_lens, int32_t* block_tables, int64_t bt_stride,
+                         int max_blocks_per_seq, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Kernels around attention in the decode/prefill step (bf16 in/out, fp32 arithmetic with
+ * the reference's rounding points).
+ * ---------------------------------------------------------------------------------- */
+
+/* RMSNorm over `hidden` (multiple of 256, <= 8192).  residual == NULL: out = RMSNorm(in)
+ * (mini_vllm/layers/layernorm.py:18-28).  residual != NULL: x = in + residual in fp32,
+ * residual := bf16(x), out = RMSNorm(x) (add_rms_forward, layernorm.py:30-42).
+ * `residual` rows are contiguous (stride = hidden). */
+int hl_rmsnorm(const void* in, int64_t in_stride, void* residual, const void* weight, void* out,
+               int64_t out_stride, int rows, int hidden, float eps, void* stream);
+
+/* In place on the fused qkv projection rows [q | k | v]: per-head RMSNorm of q and k with
+ * q_weight / k_weight, then NeoX rotary embedding with cos_sin[pos] = [cos | sin] (fp32,
+ * head_dim entries per position), positions int64.  head_dim must be 128.
+ * Replaces Qwen3Attention.forward's q_norm/k_norm + rotary_emb, mini_vllm/models/qwen3.py:82-85,
+ * mini_vllm/layers/rotary_embedding.py:8-16,39-50. */
+int hl_qk_norm_rope(void* qkv, int64_t row_stride, int num_tokens, int num_q_heads, int num_kv_heads,
+                    int head_dim, const void* q_weight, const void* k_weight, const float* cos_sin,
+                    const int64_t* positions, float eps, void* stream);
+
+/* out = silu(in[:, :I]) * in[:, I:2I]  (SiluAndMul, mini_vllm/layers/activation.py:12-16). */
+int hl_silu_mul(const void* in, int64_t in_stride, void* out, int64_t out_stride, int rows,
+                int intermediate, void* stream);
+
+/* Greedy token per row: argmax over bf16 logits, lowest index among equal maxima
+ * (the greedy replacement of Sampler.forward, mini_vllm/layers/sampler.py:12-25). */
+int hl_argmax(const void* logits, int64_t row_stride, int rows, int vocab, int64_t* out_tokens,
+              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HILDA_B200_H */

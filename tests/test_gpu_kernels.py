@@ -1,0 +1,363 @@
+"""GPU parity of every kernel behind the C ABI against the CPU oracle (and the reference's
+golden fixtures).  Tolerances: integer / byte outputs bit-exact; BF16 attention within
+rtol 2e-2 / atol 2e-3 of the fp32 oracle, FP8-KV attention within atol 6e-2 (BASELINE
+north_star); elementwise layer kernels within 1 bf16 ulp of the reference modules."""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from hilda_vllm_b200 import kernels
+from oracle import attention as oattn
+from oracle import kv_store
+from oracle.decode_pack import ReferenceDecodeBuffers
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+BF16_TOL = dict(rtol=2e-2, atol=2e-3)
+
+
+def bf(a):
+    return torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16)
+
+
+def assert_close(got, want, rtol, atol, what=""):
+    got, want = got.float().cpu(), want.float().cpu()
+    err = (got - want).abs()
+    bad = err > atol + rtol * want.abs()
+    assert not bad.any(), f"{what}: {int(bad.sum())} / {bad.numel()} out of tolerance, max err {err.max():.3e}"
+
+
+def make_paged(g, b, hk, d, nb, bs, lens, dtype=torch.bfloat16):
+    k = torch.randn(nb, bs, hk, d, generator=g).to(dtype)
+    v = torch.randn(nb, bs, hk, d, generator=g).to(dtype)
+    mb = max(1, max(-(-n // bs) for n in lens))
+    perm = torch.randperm(nb, generator=g).tolist()
+    tables, off = [], 0
+    for n in lens:
+        nblk = -(-n // bs)
+        tables.append(perm[off:off + nblk] + [-1] * (mb - nblk))
+        off += nblk
+    assert off <= nb
+    return k, v, torch.tensor(tables, dtype=torch.int32), torch.tensor(lens, dtype=torch.int32)
+
+
+# ----------------------------------------------------------------------------- store
+def test_store_bf16_matches_reference_golden(golden_dir):
+    g = np.load(golden_dir / "store_kv.npz")
+    n, hq, hk, d, nb, bs = g["shape"].tolist()
+    qkv = bf(g["qkv"]).to(DEV)
+    key = qkv[:, hq * d:(hq + hk) * d].view(n, hk, d)
+    value = qkv[:, (hq + hk) * d:].view(n, hk, d)
+    kc = torch.zeros(nb, bs, hk, d, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    kernels.store_kvcache(key, value, kc, vc, torch.from_numpy(g["slot_mapping"]).to(DEV))
+    rows = torch.from_numpy(g["touched_slots"]).to(DEV)
+    assert torch.equal(kc.view(-1, hk * d)[rows].view(torch.int16).cpu(), torch.from_numpy(g["k_rows"]))
+    assert torch.equal(vc.view(-1, hk * d)[rows].view(torch.int16).cpu(), torch.from_numpy(g["v_rows"]))
+    nz = torch.nonzero(kc.view(-1, hk * d).float().abs().sum(1)).flatten().cpu()
+    assert nz.tolist() == g["k_nonzero_rows"].tolist()
+
+
+@pytest.mark.parametrize("n,hk", [(1, 8), (256, 8), (3000, 8), (77, 1), (64, 4)])
+def test_store_bf16_random(n, hk):
+    g = torch.Generator().manual_seed(n)
+    d, nb, bs = 128, 64, 256
+    qkv = torch.randn(n, (2 * hk + 2 * hk) * d, generator=g).bfloat16()
+    key = qkv[:, 2 * hk * d:3 * hk * d].view(n, hk, d)
+    value = qkv[:, 3 * hk * d:].view(n, hk, d)
+    slots = torch.randperm(nb * bs, generator=g)[:n].to(torch.int32)
+    slots[::7] = -1
+    kc = torch.randn(nb, bs, hk, d, generator=g).bfloat16()
+    vc = torch.randn(nb, bs, hk, d, generator=g).bfloat16()
+    kd, vd = kc.to(DEV), vc.to(DEV)
+    qd = qkv.to(DEV)  # strided key/value views into a fused projection, as in the model
+    kernels.store_kvcache(qd[:, 2 * hk * d:3 * hk * d].view(n, hk, d), qd[:, 3 * hk * d:].view(n, hk, d), kd, vd,
+                          slots.to(DEV))
+    kv_store.store_kvcache(key, value, kc, vc, slots)
+    assert torch.equal(kd.cpu(), kc) and torch.equal(vd.cpu(), vc)
+
+
+@pytest.mark.parametrize("hk,scaled", [(8, False), (8, True), (2, True)])
+def test_store_fp8_bit_exact(hk, scaled):
+    g = torch.Generator().manual_seed(hk + scaled)
+    n, d, nb, bs = 300, 128, 8, 256
+    key = (torch.randn(n, hk, d, generator=g) * torch.logspace(-4, 3, n).view(n, 1, 1)).bfloat16()
+    value = (torch.randn(n, hk, d, generator=g) * 3).bfloat16()
+    key[0, 0, :4] = torch.tensor([1e6, -1e6, 448.0, 2 ** -10]).bfloat16()
+    ks = (torch.rand(hk, generator=g) * 4 + 0.1) if scaled else None
+    vs = (torch.rand(hk, generator=g) * 0.5 + 0.05) if scaled else None
+    slots = torch.randperm(nb * bs, generator=g)[:n].to(torch.int32)
+    slots[5] = -1
+    kc = torch.zeros(nb, bs, hk, d, dtype=torch.uint8)
+    vc = torch.zeros_like(kc)
+    kv_store.store_kvcache_fp8(key, value, kc, vc, slots, ks, vs)
+    kd = torch.zeros(nb, bs, hk, d, dtype=torch.float8_e4m3fn, device=DEV)
+    vd = torch.zeros_like(kd)
+    kernels.store_kvcache_fp8(key.to(DEV), value.to(DEV), kd, vd, slots.to(DEV),
+                              None if ks is None else ks.to(DEV), None if vs is None else vs.to(DEV))
+    assert torch.equal(kd.view(torch.uint8).cpu(), kc)
+    assert torch.equal(vd.view(torch.uint8).cpu(), vc)
+
+
+def test_copy_bf16_to_fp8_all_layers_bit_exact():
+    g = torch.Generator().manual_seed(9)
+    layers, nb, bs, hk, d = 3, 6, 256, 8, 128
+    src = (torch.randn(2, layers, nb, bs, hk, d, generator=g) * 20).bfloat16()
+    scales = torch.rand(2, layers, hk, generator=g) + 0.2
+    slots = torch.randperm(nb * bs, generator=g)[:700].to(torch.int32)
+    dst = torch.zeros(2, layers, nb, bs, hk, d, dtype=torch.float8_e4m3fn, device=DEV)
+    kernels.copy_kvcache_fp8_layers(src[0].to(DEV), src[1].to(DEV), dst[0], dst[1], slots.to(DEV),
+                                    scales[0].contiguous().to(DEV), scales[1].contiguous().to(DEV))
+    for layer in range(layers):
+        want_k = torch.zeros(nb, bs, hk, d, dtype=torch.uint8)
+        want_v = torch.zeros_like(want_k)
+        kv_store.copy_kvcache_fp8(src[0, layer], src[1, layer], want_k, want_v, slots, scales[0, layer],
+                                  scales[1, layer])
+        assert torch.equal(dst[0, layer].view(torch.uint8).cpu(), want_k)
+        assert torch.equal(dst[1, layer].view(torch.uint8).cpu(), want_v)
+
+
+# ----------------------------------------------------------------------------- decode
+def run_decode(q, k, v, bt, lens, scale, fp8=False, ks=None, vs=None, ws=None):
+    if fp8:
+        kd = k.to(DEV).view(torch.float8_e4m3fn)
+        vd = v.to(DEV).view(torch.float8_e4m3fn)
+    else:
+        kd, vd = k.to(DEV), v.to(DEV)
+    return kernels.paged_decode(q.to(DEV), kd, vd, bt.to(DEV), lens.to(DEV), scale, workspace=ws,
+                                k_scale=None if ks is None else ks.to(DEV),
+                                v_scale=None if vs is None else vs.to(DEV))
+
+
+def test_decode_config1_shapes():
+    """8 sequences, lens ~ U[16,1024], 16 Q / 8 KV heads, 64 blocks of 256."""
+    g = torch.Generator().manual_seed(1)
+    lens = torch.randint(16, 1025, (8,), generator=g).tolist()
+    k, v, bt, ln = make_paged(g, 8, 8, 128, 64, 256, lens)
+    q = torch.randn(8, 16, 128, generator=g).bfloat16()
+    out = run_decode(q, k, v, bt, ln, 128 ** -0.5)
+    want = oattn.paged_decode(q, k, v, bt, ln, 128 ** -0.5)
+    assert_close(out, want, **BF16_TOL, what="config1")
+
+
+EDGE_LENS = [0, 1, 2, 127, 128, 129, 255, 256, 257, 511, 512, 1000, 1024, 1025, 2047, 3000, 4096]
+
+
+@pytest.mark.parametrize("hq,hk", [(16, 8), (32, 8), (8, 8), (16, 4), (8, 2), (8, 1), (64, 8), (4, 4)])
+def test_decode_gqa_layouts_and_edge_lengths(hq, hk):
+    g = torch.Generator().manual_seed(hq * 10 + hk)
+    lens = EDGE_LENS
+    k, v, bt, ln = make_paged(g, len(lens), hk, 128, 96, 256, lens)
+    q = torch.randn(len(lens), hq, 128, generator=g).bfloat16()
+    out = run_decode(q, k, v, bt, ln, 128 ** -0.5)
+    want = oattn.paged_decode(q, k, v, bt, ln, 128 ** -0.5)
+    assert torch.all(out[0] == 0)
+    assert torch.isfinite(out).all()
+    assert_close(out, want, **BF16_TOL, what=f"hq={hq} hk={hk}")
+
+
+def test_decode_workspace_reuse_and_padding_rows():
+    """Two launches sharing one workspace (tickets must be reset), with padding rows
+    (context 0, block table -1) as the CUDA graph buckets produce."""
+    g = torch.Generator().manual_seed(3)
+    lens = [700, 0, 300, 0, 1]
+    k, v, bt, ln = make_paged(g, 5, 8, 128, 16, 256, lens)
+    ws = kernels.make_decode_workspace(5, 16, 128, bt.shape[1], 256, DEV)
+    for trial in range(3):
+        q = torch.randn(5, 16, 128, generator=g).bfloat16()
+        out = run_decode(q, k, v, bt, ln, 0.1, ws=ws)
+        want = oattn.paged_decode(q, k, v, bt, ln, 0.1)
+        assert_close(out, want, **BF16_TOL, what=f"trial {trial}")
+    assert kernels.decode_errors(ws) == 0
+
+
+def test_decode_large_batch():
+    g = torch.Generator().manual_seed(4)
+    lens = torch.randint(65, 1089, (256,), generator=g).tolist()
+    k, v, bt, ln = make_paged(g, 256, 8, 128, 1400, 256, lens)
+    q = torch.randn(256, 16, 128, generator=g).bfloat16()
+    out = run_decode(q, k, v, bt, ln, 128 ** -0.5)
+    idx = list(range(0, 256, 9))
+    want = oattn.paged_decode(q[idx], k, v, bt[idx], ln[idx], 128 ** -0.5)
+    assert_close(out[idx], want, **BF16_TOL, what="B=256")
+
+
+def test_decode_inside_cuda_graph():
+    g = torch.Generator().manual_seed(5)
+    lens = [300, 17, 1024, 5]
+    k, v, bt, ln = make_paged(g, 4, 8, 128, 32, 256, [1024] * 4)
+    kd, vd, btd = k.to(DEV), v.to(DEV), bt.to(DEV)
+    lnd = torch.zeros(4, dtype=torch.int32, device=DEV)
+    qd = torch.zeros(4, 16, 128, dtype=torch.bfloat16, device=DEV)
+    out = torch.zeros(4, 16, 128, dtype=torch.bfloat16, device=DEV)
+    ws = kernels.make_decode_workspace(4, 16, 128, bt.shape[1], 256, DEV)
+    kernels.paged_decode(qd, kd, vd, btd, lnd, 0.1, out=out, workspace=ws)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        kernels.paged_decode(qd, kd, vd, btd, lnd, 0.1, out=out, workspace=ws)
+    for trial in range(3):
+        q = torch.randn(4, 16, 128, generator=g).bfloat16()
+        L = torch.tensor([(x * (trial + 1)) % 1025 for x in lens], dtype=torch.int32)
+        qd.copy_(q)
+        lnd.copy_(L)
+        graph.replay()
+        want = oattn.paged_decode(q, k, v, bt, L, 0.1)
+        assert_close(out, want, **BF16_TOL, what=f"graph replay {trial}")
+
+
+@pytest.mark.parametrize("hq,hk,scaled", [(16, 8, False), (16, 8, True), (32, 8, True), (8, 1, True)])
+def test_decode_fp8(hq, hk, scaled):
+    g = torch.Generator().manual_seed(7 + hq)
+    lens = [0, 1, 129, 256, 700, 1500]
+    kb, vb, bt, ln = make_paged(g, len(lens), hk, 128, 24, 256, lens)
+    ks = (torch.rand(hk, generator=g) + 0.5) if scaled else None
+    vs = (torch.rand(hk, generator=g) + 0.5) if scaled else None
+    kq = kv_store.quantize_e4m3(kb, ks)
+    vq = kv_store.quantize_e4m3(vb, vs)
+    q = torch.randn(len(lens), hq, 128, generator=g).bfloat16()
+    out = run_decode(q, kq, vq, bt, ln, 128 ** -0.5, fp8=True, ks=ks, vs=vs)
+    want = oattn.paged_decode(q, kq, vq, bt, ln, 128 ** -0.5, ks, vs, fp8=True)
+    assert_close(out, want, rtol=2e-2, atol=6e-2, what="fp8")
+    assert_close(out, want, **BF16_TOL, what="fp8 (tight)")
+
+
+# ----------------------------------------------------------------------------- prefill
+@pytest.mark.parametrize("hq,hk", [(16, 8), (32, 8), (8, 1)])
+def test_prefill_contiguous(hq, hk):
+    g = torch.Generator().manual_seed(11 + hq)
+    lens = [1, 5, 64, 64, 130, 257, 31]
+    cu = torch.tensor([0] + np.cumsum(lens).tolist(), dtype=torch.int32)
+    t = int(cu[-1])
+    qkv = torch.randn(t, (hq + 2 * hk) * 128, generator=g).bfloat16()
+    q = qkv[:, :hq * 128].view(t, hq, 128)
+    k = qkv[:, hq * 128:(hq + hk) * 128].view(t, hk, 128)
+    v = qkv[:, (hq + hk) * 128:].view(t, hk, 128)
+    qd = qkv.to(DEV)
+    out = kernels.varlen_prefill(qd[:, :hq * 128].view(t, hq, 128), qd[:, hq * 128:(hq + hk) * 128].view(t, hk, 128),
+                                 qd[:, (hq + hk) * 128:].view(t, hk, 128), cu.to(DEV), cu.to(DEV), max(lens),
+                                 max(lens), 128 ** -0.5)
+    want = oattn.varlen_prefill(q, k, v, cu, cu, 128 ** -0.5)
+    assert_close(out, want, **BF16_TOL, what="prefill contiguous")
+
+
+def test_prefill_paged_with_prefix_chunks():
+    """Chunked prefill over cached prefixes: queries are the chunk, keys = prefix + chunk
+    from the paged cache (block_table set), bottom-right causal mask."""
+    g = torch.Generator().manual_seed(12)
+    hq, hk, bs, nb = 16, 8, 256, 40
+    starts = [0, 256, 100, 512, 2048, 3]
+    chunks = [64, 128, 1, 300, 512, 700]
+    kl = [s + c for s, c in zip(starts, chunks)]
+    k, v, bt, _ = make_paged(g, len(kl), hk, 128, nb, bs, kl)
+    cuq = torch.tensor([0] + np.cumsum(chunks).tolist(), dtype=torch.int32)
+    cuk = torch.tensor([0] + np.cumsum(kl).tolist(), dtype=torch.int32)
+    q = torch.randn(int(cuq[-1]), hq, 128, generator=g).bfloat16()
+    out = kernels.varlen_prefill(q.to(DEV), k.to(DEV), v.to(DEV), cuq.to(DEV), cuk.to(DEV), max(chunks), max(kl),
+                                 128 ** -0.5, block_table=bt.to(DEV))
+    want = oattn.varlen_prefill(q, k, v, cuq, cuk, 128 ** -0.5, block_table=bt)
+    assert_close(out, want, **BF16_TOL, what="prefill paged")
+
+
+# ----------------------------------------------------------------------------- packing
+@pytest.mark.parametrize("name", ["sched_trace_churn", "sched_trace_prefix", "sched_trace_complete"])
+def test_pack_kernel_replays_reference_trace(golden_dir, seq_block_size, name):
+    from tests.test_trace_parity import _load, _replay
+    from hilda_vllm_b200.engine.decode_packer import DecodePacker, packet_capacity_bytes
+    from hilda_vllm_b200.engine.sequence import SequenceStatus
+
+    trace = _load(golden_dir, name)
+    meta = trace["meta"]
+    bs, max_bs = meta["block_size"], meta["max_bs"]
+    mb = -(-meta["max_model_len"] // bs)
+    cap = (packet_capacity_bytes(max_bs, mb) + 15) & ~15
+    host = torch.zeros(cap, dtype=torch.uint8)
+    packer = DecodePacker(max_bs, mb, host.numpy())
+    pkt = torch.zeros(cap, dtype=torch.uint8, device=DEV)
+    st = dict(input_ids=torch.zeros(max_bs, dtype=torch.int64, device=DEV),
+              positions=torch.zeros(max_bs, dtype=torch.int64, device=DEV),
+              slot_mapping=torch.full((max_bs,), -1, dtype=torch.int32, device=DEV),
+              context_lens=torch.zeros(max_bs, dtype=torch.int32, device=DEV),
+              block_tables=torch.full((max_bs, mb), -1, dtype=torch.int32, device=DEV))
+    seq_ids = torch.full((max_bs,), -1, dtype=torch.int64, device=DEV)
+    bt_lens = torch.zeros(max_bs, dtype=torch.int32, device=DEV)
+    next_tokens = torch.zeros(max_bs, dtype=torch.int64, device=DEV)
+    n = [0]
+
+    def check(rec, scheduled, is_prefill):
+        if is_prefill:
+            return
+        graph_bs = rec["graph_bs"]
+        nbytes = packer.build(scheduled, graph_bs)
+        pkt[:nbytes].copy_(host[:nbytes])
+        kernels.pack_decode_batch(pkt, graph_bs, bs, seq_ids, bt_lens, next_tokens, st["input_ids"],
+                                  st["positions"], st["slot_mapping"], st["context_lens"], st["block_tables"])
+        for key, want in rec["decode"].items():
+            got = st[key][:graph_bs].cpu().numpy()
+            np.testing.assert_array_equal(got, np.asarray(want), err_msg=key)
+        toks = [0 if t is None else t for t in rec["tokens"]]
+        next_tokens[: len(toks)] = torch.tensor(toks, device=DEV)
+        packer.note_sampled(len(toks), toks)
+        n[0] += 1
+
+    _replay(trace, seq_block_size, check)
+    assert n[0] > 10
+
+
+# ----------------------------------------------------------------------------- layer kernels
+def ulp_diff(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    ai = a.view(torch.int16).to(torch.int32)
+    bi = b.view(torch.int16).to(torch.int32)
+    # map sign-magnitude to a monotonic integer line
+    ai = torch.where(ai < 0, -(ai & 0x7FFF), ai)
+    bi = torch.where(bi < 0, -(bi & 0x7FFF), bi)
+    return (ai - bi).abs()
+
+
+def assert_ulps(got, want_bits, what):
+    d = ulp_diff(got.cpu().contiguous(), torch.from_numpy(want_bits).view(torch.bfloat16))
+    assert int(d.max()) <= 1, f"{what}: max {int(d.max())} ulp"
+    assert float((d > 0).float().mean()) < 0.02, f"{what}: {float((d > 0).float().mean()):.3%} differ"
+
+
+def test_rmsnorm_kernels_match_reference_modules(golden_dir):
+    g = np.load(golden_dir / "layers.npz")
+    x, r, w = bf(g["rms_x"]).to(DEV), bf(g["rms_r"]).to(DEV), bf(g["rms_w"]).to(DEV)
+    assert_ulps(kernels.rmsnorm(x, w, 1e-6), g["rms_y"], "rmsnorm")
+    res = r.clone()
+    y, res = kernels.rmsnorm(x, w, 1e-6, residual=res)
+    assert_ulps(y, g["add_y"], "add_rmsnorm")
+    assert torch.equal(res.cpu().view(torch.int16), torch.from_numpy(g["add_r"]))
+
+
+def test_qk_norm_rope_matches_reference_modules(golden_dir):
+    from hilda_vllm_b200.layers.rotary_embedding import RotaryEmbedding
+    g = np.load(golden_dir / "layers.npz")
+    q = bf(g["rope_q"])  # [T, 4, 128] treated as 2 q heads + 2 k heads with the same weight
+    t = q.shape[0]
+    w = bf(g["rope_w"]).to(DEV)
+    qkv = torch.cat([q.reshape(t, -1), torch.zeros(t, 2 * 128, dtype=torch.bfloat16)], 1).to(DEV)
+    rope = RotaryEmbedding(128, 128, 4096, 1000000.0)
+    cos_sin = rope.cos_sin_cache.to(DEV).contiguous()
+    kernels.qk_norm_rope(qkv, 2, 1, 128, w, w, cos_sin, torch.from_numpy(g["rope_pos"]).to(DEV), 1e-6)
+    want = g["rope_out"].reshape(t, -1)
+    assert_ulps(qkv[:, :3 * 128], want[:, :3 * 128], "qk_norm_rope")
+    assert torch.all(qkv[:, 3 * 128:] == 0)  # v untouched
+
+
+def test_silu_mul_matches_reference_module(golden_dir):
+    g = np.load(golden_dir / "layers.npz")
+    a = bf(g["silu_in"]).to(DEV)
+    assert_ulps(kernels.silu_mul(a), g["silu_out"], "silu_mul")
+
+
+def test_argmax_lowest_index_on_ties():
+    g = torch.Generator().manual_seed(13)
+    logits = torch.randn(37, 151936, generator=g).bfloat16()
+    logits[5, 100] = logits[5, 2000] = 50.0  # tie -> 100
+    logits[6, :] = -1.0
+    got = kernels.argmax(logits.to(DEV)).cpu()
+    assert got[5] == 100 and got[6] == 0
+    assert torch.equal(got, logits.float().argmax(-1))

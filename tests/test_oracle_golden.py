@@ -1,0 +1,156 @@
+"""Pins the CPU oracle against fixtures produced by the reference's own code
+(tests/golden/make_golden.py) and against torch's float8_e4m3fn cast."""
+import json
+
+import numpy as np
+import torch
+
+from oracle import attention as oattn
+from oracle import kv_store
+from oracle.build import load as load_oracle_c
+from oracle.qwen3_model import Qwen3Oracle, decode_context, prefill_context
+
+
+def bf(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16)
+
+
+def test_store_oracle_matches_reference_triton_kernel(golden_dir):
+    g = np.load(golden_dir / "store_kv.npz")
+    n, hq, hk, d, nb, bs = g["shape"].tolist()
+    qkv = bf(g["qkv"])
+    key = qkv[:, hq * d:(hq + hk) * d].view(n, hk, d)
+    value = qkv[:, (hq + hk) * d:].view(n, hk, d)
+    kc = torch.zeros(nb, bs, hk, d, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    kv_store.store_kvcache(key, value, kc, vc, torch.from_numpy(g["slot_mapping"]))
+    rows = torch.from_numpy(g["touched_slots"])
+    assert torch.equal(kc.view(-1, hk * d)[rows].view(torch.int16), torch.from_numpy(g["k_rows"]))
+    assert torch.equal(vc.view(-1, hk * d)[rows].view(torch.int16), torch.from_numpy(g["v_rows"]))
+    nz = torch.nonzero(kc.view(-1, hk * d).float().abs().sum(1)).flatten()
+    assert nz.tolist() == g["k_nonzero_rows"].tolist()  # slot -1 skipped, nothing else touched
+
+
+def test_e4m3_c_oracle_matches_torch_exhaustively():
+    lib = load_oracle_c()
+    allb = torch.arange(0, 65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    vals = allb[torch.isfinite(allb.float())]
+    src = vals.view(torch.int16).numpy().copy()
+    for scale in (1.0, 0.37, 3.5, 1e-3):
+        out = np.zeros(len(vals), np.uint8)
+        sc = np.array([scale], np.float32)
+        lib.oracle_quantize_rows(src.ctypes.data, 1, 1, len(vals), sc.ctypes.data, out.ctypes.data)
+        ref = torch.clamp(vals.float() / torch.tensor(scale, dtype=torch.float32), -448, 448)
+        ref = ref.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+        assert (out == ref).all(), scale
+    dec = np.array([lib.oracle_e4m3_to_float(i) for i in range(256)], np.float32)
+    tdec = torch.arange(256, dtype=torch.int32).to(torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    both_nan = np.isnan(dec) & np.isnan(tdec)
+    assert ((dec == tdec) | both_nan).all()
+
+
+def test_fp8_store_and_copy_oracles_agree():
+    g = torch.Generator().manual_seed(5)
+    key = (torch.randn(6, 2, 128, generator=g) * 40).bfloat16()
+    value = torch.randn(6, 2, 128, generator=g).bfloat16()
+    ks, vs = torch.tensor([0.5, 2.0]), torch.tensor([0.01, 1.0])
+    kc = torch.zeros(2, 8, 2, 128, dtype=torch.uint8)
+    vc = torch.zeros_like(kc)
+    sm = torch.tensor([0, 3, -1, 9, 15, 4], dtype=torch.int32)
+    kv_store.store_kvcache_fp8(key, value, kc, vc, sm, ks, vs)
+    # copy path: BF16 cache -> FP8 cache at the same slots gives the same bytes
+    kb = torch.zeros(2, 8, 2, 128, dtype=torch.bfloat16)
+    vb = torch.zeros_like(kb)
+    kv_store.store_kvcache(key, value, kb, vb, sm)
+    kc2 = torch.zeros_like(kc)
+    vc2 = torch.zeros_like(vc)
+    kv_store.copy_kvcache_fp8(kb, vb, kc2, vc2, sm, ks, vs)
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    want = torch.clamp(key[1].float() / ks.view(2, 1), -448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+    assert torch.equal(kc.view(-1, 2, 128)[3], want)
+
+
+def test_attention_oracle_edge_cases():
+    g = torch.Generator().manual_seed(6)
+    kc = torch.randn(4, 256, 2, 128, generator=g).bfloat16()
+    vc = torch.randn(4, 256, 2, 128, generator=g).bfloat16()
+    q = torch.randn(3, 4, 128, generator=g).bfloat16()
+    bt = torch.tensor([[2, 0, -1], [1, -1, -1], [3, 2, 1]], dtype=torch.int32)
+    lens = torch.tensor([300, 0, 1], dtype=torch.int32)
+    out = oattn.paged_decode(q, kc, vc, bt, lens, 128 ** -0.5)
+    assert torch.all(out[1] == 0)  # empty row
+    # one cached token: softmax of one element = 1, output = that V row (slot 3*256+0)
+    assert torch.allclose(out[2], vc.view(-1, 2, 128)[768].float().repeat_interleave(2, 0))
+    # decode of a sequence equals the last row of its causal prefill
+    k = kc.view(-1, 2, 128)[torch.cat([torch.arange(512, 768), torch.arange(0, 44)])]
+    v = vc.view(-1, 2, 128)[torch.cat([torch.arange(512, 768), torch.arange(0, 44)])]
+    qs = torch.randn(300, 4, 128, generator=g).bfloat16()
+    qs[-1] = q[0]
+    cu = torch.tensor([0, 300], dtype=torch.int32)
+    pre = oattn.varlen_prefill(qs, k, v, cu, cu, 128 ** -0.5)
+    assert torch.allclose(pre[-1], out[0], atol=1e-5, rtol=1e-5)
+    # keys fewer than queries: rows with no visible key are zero
+    cuk = torch.tensor([0, 10], dtype=torch.int32)
+    cuq = torch.tensor([0, 12], dtype=torch.int32)
+    short = oattn.varlen_prefill(qs[:12], k[:10], v[:10], cuq, cuk, 128 ** -0.5)
+    assert torch.all(short[:2] == 0) and torch.all(short[2:].abs().sum(-1) > 0)
+
+
+def test_layer_restatements_match_reference_modules(golden_dir):
+    g = np.load(golden_dir / "layers.npz")
+    from types import SimpleNamespace
+
+    cfg = SimpleNamespace(num_attention_heads=4, num_key_value_heads=2, head_dim=128, hidden_size=512,
+                          rms_norm_eps=1e-6, rope_theta=1000000.0, rope_scaling=None, max_position_embeddings=4096,
+                          num_hidden_layers=0)
+    o = Qwen3Oracle(cfg, {"model.embed_tokens.weight": torch.zeros(2, 2)}, 1, 256)
+    x, r, w = bf(g["rms_x"]), bf(g["rms_r"]), bf(g["rms_w"])
+    assert torch.equal(o.rms(x, w).view(torch.int16), torch.from_numpy(g["rms_y"]))
+    y2, r2 = o.add_rms(x, r, w)
+    assert torch.equal(y2.view(torch.int16), torch.from_numpy(g["add_y"]))
+    assert torch.equal(r2.view(torch.int16), torch.from_numpy(g["add_r"]))
+    q = bf(g["rope_q"])
+    out = o.rope(o.rms(q, bf(g["rope_w"])), torch.from_numpy(g["rope_pos"]))
+    assert torch.equal(out.view(torch.int16), torch.from_numpy(g["rope_out"]))
+    a = bf(g["silu_in"])
+    gate, up = a.chunk(2, -1)
+    assert torch.equal((torch.nn.functional.silu(gate) * up).view(torch.int16), torch.from_numpy(g["silu_out"]))
+
+
+def test_oracle_model_matches_reference_modules_greedy(golden_dir):
+    """Tiny Qwen3 through the oracle reproduces the reference modules' greedy tokens."""
+    from transformers import Qwen3Config
+
+    from hilda_vllm_b200.models.qwen3 import Qwen3ForCausalLM  # noqa: F401  (weights only)
+    from hilda_vllm_b200.utils.loader import checkpoint_tensor_shapes
+    import zlib
+
+    gold = json.loads((golden_dir / "tiny_model_greedy.json").read_text())
+    cfg = Qwen3Config(**gold["config"])
+    weights = {}
+    for name, shape, is_norm in checkpoint_tensor_shapes(cfg):
+        if is_norm:
+            weights[name] = torch.ones(shape, dtype=torch.bfloat16)
+        else:
+            gen = torch.Generator().manual_seed((gold["seed"] * 1_000_003 + zlib.crc32(name.encode())) & 0x7FFF_FFFF_FFFF_FFFF)
+            weights[name] = (torch.randn(shape, generator=gen, dtype=torch.float32) * 0.02).bfloat16()
+    bs = 256
+    model = Qwen3Oracle(cfg, weights, 16, bs)
+    prompts = gold["prompts"]
+    tables = [[0], [1], [2, 3]]
+    ids, pos, ctx = prefill_context(prompts, [0] * 3, [len(p) for p in prompts], tables, bs)
+    with torch.no_grad():
+        logits = model.logits(model.forward(ids, pos, ctx), ctx)
+    toks = logits.argmax(-1).tolist()
+    assert toks == gold["steps"][0]["tokens"]
+    seqs = [p + [t] for p, t in zip(prompts, toks)]
+    for step in gold["steps"][1:]:
+        for s, t in zip(seqs, tables):
+            if (len(s) - 1) // bs >= len(t):
+                t.append(max(max(x) for x in tables) + 1)
+        lens = [len(s) for s in seqs]
+        ids, pos, ctx = decode_context(lens, [s[-1] for s in seqs], tables, bs, 4)
+        with torch.no_grad():
+            toks = model.logits(model.forward(ids, pos, ctx), ctx).argmax(-1).tolist()
+        assert toks == step["tokens"]
+        seqs = [s + [t] for s, t in zip(seqs, toks)]

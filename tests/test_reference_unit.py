@@ -1,0 +1,228 @@
+"""The reference's own unit tests (tests/test_correctness.py, test_block_manager.py,
+test_scheduler.py, test_sampler.py of kirsten-1/hilda-vllm), run against this package's
+host API: the behaviours they pin must carry over unchanged."""
+import itertools
+import pickle
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+from hilda_vllm_b200.engine.block_manager import BlockManager
+from hilda_vllm_b200.engine.scheduler import Scheduler
+from hilda_vllm_b200.engine.sequence import Sequence, SequenceStatus
+from hilda_vllm_b200.layers.sampler import Sampler
+from hilda_vllm_b200.sampling_params import SamplingParams
+
+
+@pytest.fixture(autouse=True)
+def reset_sequence_state():
+    bs, counter = Sequence.block_size, Sequence.counter
+    Sequence.block_size = 4
+    Sequence.counter = itertools.count()
+    yield
+    Sequence.block_size, Sequence.counter = bs, counter
+
+
+def make_config(**overrides):
+    cfg = dict(max_num_seqs=2, max_num_batched_tokens=8, eos=99, num_kvcache_blocks=6, kvcache_block_size=2,
+               enable_chunked_prefill=True, chunked_prefill_size=4, chunked_prefill_min_size=2,
+               chunked_prefill_tile_size=2)
+    cfg.update(overrides)
+    return SimpleNamespace(**cfg)
+
+
+# ---- test_correctness.py
+def test_sequence_tracks_prompt_and_completion_tokens():
+    seq = Sequence([1, 2, 3], SamplingParams(max_tokens=5))
+    seq.append_token(4)
+    seq.append_token(5)
+    assert seq.prompt_token_ids == [1, 2, 3]
+    assert seq.completion_token_ids == [4, 5]
+    assert seq.num_completion_tokens == 2
+    assert seq.num_blocks == 2
+    assert seq.last_block_num_tokens == 1
+
+
+def test_prompt_only_sequence_survives_pickle_roundtrip():
+    seq = Sequence([7, 8, 9], SamplingParams(max_tokens=3, top_k=8, top_p=0.9))
+    seq.num_computed_tokens = 2
+    r = pickle.loads(pickle.dumps(seq))
+    assert r.seq_id == seq.seq_id and r.token_ids == [7, 8, 9] and r.num_prompt_tokens == 3
+    assert r.num_completion_tokens == 0 and r.num_computed_tokens == 2 and r.top_k == 8 and r.top_p == 0.9
+
+
+def test_decode_sequence_survives_pickle_roundtrip():
+    seq = Sequence([7, 8, 9], SamplingParams(max_tokens=3, top_k=4, top_p=0.7))
+    seq.status = SequenceStatus.RUNNING
+    seq.num_computed_tokens = 3
+    seq.append_token(10)
+    r = pickle.loads(pickle.dumps(seq))
+    assert r.seq_id == seq.seq_id and r.last_token == 10 and r.num_tokens == 4
+    assert r.num_prompt_tokens == 3 and r.num_completion_tokens == 1 and r.top_k == 4 and r.top_p == 0.7
+
+
+def test_sequence_exposes_prefill_progress():
+    seq = Sequence([1, 2, 3, 4], SamplingParams(max_tokens=3))
+    seq.num_computed_tokens = 3
+    assert seq.num_prompt_tokens_remaining == 1
+    assert seq.num_uncomputed_tokens == 1
+    assert seq.is_prefill_done is False
+
+
+def test_scheduler_rejects_shrinking_with_live_decode_slots():
+    s = Scheduler.__new__(Scheduler)
+    s.running, s.max_num_seqs = set(), 2
+    s.decode_slots, s.free_slot_indices, s.persistent_batch_size = [object(), None], [1], 2
+    with pytest.raises(AssertionError):
+        s._maybe_shrink_batch()
+
+
+def test_scheduler_shrinks_trailing_padding_slots():
+    s = Scheduler.__new__(Scheduler)
+    s.running, s.max_num_seqs = {object()}, 4
+    s.decode_slots, s.free_slot_indices, s.persistent_batch_size = [object(), None, None, None], [1, 2, 3], 4
+    s._maybe_shrink_batch()
+    assert s.persistent_batch_size == 1
+
+
+def test_scheduler_reuses_lowest_free_slot():
+    s = Scheduler.__new__(Scheduler)
+    s.decode_slots, s.free_slot_indices, s.persistent_batch_size = [None, None, None], [0, 2, 1], 0
+    seq = Sequence([1], SamplingParams())
+    s._assign_decode_slot(seq)
+    assert seq.decode_slot_index == 0 and s.persistent_batch_size == 1
+
+
+def test_scheduler_compacts_internal_decode_hole():
+    s = Scheduler.__new__(Scheduler)
+    s.decode_slots, s.free_slot_indices, s.persistent_batch_size = [None, None, None], [], 3
+    a, b, c = Sequence([1], SamplingParams()), Sequence([2], SamplingParams()), Sequence([3], SamplingParams())
+    s.running = {a, c}
+    a.decode_slot_index, b.decode_slot_index, c.decode_slot_index = 0, 1, 2
+    s.decode_slots[:] = [a, b, c]
+    s._free_decode_slot(b)
+    s._maybe_shrink_batch()
+    assert b.decode_slot_index == -1 and c.decode_slot_index == 1
+    assert s.decode_slots == [a, c, None] and s.persistent_batch_size == 2 and s.free_slot_indices == [2]
+
+
+def test_sampling_params_validate_top_k_and_top_p():
+    for kw in (dict(top_k=0), dict(top_p=0.0), dict(top_p=1.1)):
+        with pytest.raises(AssertionError):
+            SamplingParams(**kw)
+
+
+def test_sampling_params_rejects_zero_temperature():
+    with pytest.raises(AssertionError):
+        SamplingParams(temperature=0.0)
+
+
+# ---- test_block_manager.py (block size 2)
+def test_allocate_reuses_cached_full_prefix_block():
+    Sequence.block_size = 2
+    m = BlockManager(num_blocks=4, block_size=2)
+    s1, s2 = Sequence([1, 2, 3]), Sequence([1, 2, 9])
+    m.allocate(s1)
+    m.allocate(s2)
+    shared = s1.block_table[0]
+    assert s2.block_table[0] == shared and s2.num_cached_tokens == 2 and m.blocks[shared].ref_count == 2
+
+
+def test_deallocate_returns_blocks_to_free_pool():
+    Sequence.block_size = 2
+    m = BlockManager(num_blocks=3, block_size=2)
+    seq = Sequence([1, 2, 3])
+    m.allocate(seq)
+    assert len(m.free_block_ids) == 1
+    m.deallocate(seq)
+    assert len(m.free_block_ids) == 3 and m.used_block_ids == set() and seq.block_table == [] and seq.num_cached_tokens == 0
+
+
+# ---- test_scheduler.py (block size 2)
+def test_prefill_moves_waiting_sequences_to_running():
+    Sequence.block_size = 2
+    s = Scheduler(make_config())
+    a, b = Sequence([10, 11], SamplingParams(max_tokens=4)), Sequence([20], SamplingParams(max_tokens=4))
+    s.add(a)
+    s.add(b)
+    sched, pre = s.schedule()
+    s.postprocess(sched, [1, 2], pre)
+    assert pre is True and list(s.waiting) == [] and s.running == {a, b}
+    assert a.status is SequenceStatus.RUNNING and b.status is SequenceStatus.RUNNING
+
+
+def test_postprocess_marks_finished_sequence_on_eos():
+    Sequence.block_size = 2
+    s = Scheduler(make_config())
+    seq = Sequence([1, 2], SamplingParams(max_tokens=4))
+    s.add(seq)
+    sched, pre = s.schedule()
+    s.postprocess(sched, [99], pre)
+    assert seq.status is SequenceStatus.FINISHED and list(s.running) == [] and seq.block_table == []
+
+
+def test_chunked_prefill_rotates_partial_sequence_to_waiting_tail():
+    Sequence.block_size = 2
+    s = Scheduler(make_config(max_num_seqs=1, max_num_batched_tokens=4, chunked_prefill_size=2))
+    long_seq = Sequence([10, 11, 12, 13, 14, 15], SamplingParams(max_tokens=4))
+    short_seq = Sequence([20, 21], SamplingParams(max_tokens=4))
+    s.add(long_seq)
+    s.add(short_seq)
+    sched, pre = s.schedule()
+    s.postprocess(sched, [None], pre)
+    assert pre is True and long_seq.num_computed_tokens == 4
+    assert list(s.waiting) == [short_seq, long_seq] and list(s.running) == []
+
+
+def test_decode_runs_between_prefill_chunks_when_running_queue_is_non_empty():
+    Sequence.block_size = 2
+    s = Scheduler(make_config(max_num_batched_tokens=4, chunked_prefill_size=2))
+    d = Sequence([1, 2], SamplingParams(max_tokens=4))
+    s.add(d)
+    w, wp = s.schedule()
+    s.postprocess(w, [42], wp)
+    waiting = Sequence([10, 11, 12, 13], SamplingParams(max_tokens=4))
+    s.add(waiting)
+    s.last_step_was_prefill = False
+    f, fp = s.schedule()
+    s.postprocess(f, [None], fp)
+    sec, sp = s.schedule()
+    assert fp is True and sp is False and sec[0].seq is d
+
+
+@pytest.mark.xfail(reason="stale in the reference too: prefer-decode (scheduler.py:257-277) returns decode here",
+                   strict=True)
+def test_prefill_respects_running_sequences_when_counting_max_num_seqs():
+    Sequence.block_size = 2
+    s = Scheduler(make_config(max_num_seqs=2, max_num_batched_tokens=8))
+    r = Sequence([1, 2], SamplingParams(max_tokens=4))
+    s.add(r)
+    sched, pre = s.schedule()
+    s.postprocess(sched, [42], pre)
+    w1, w2 = Sequence([10, 11], SamplingParams(max_tokens=4)), Sequence([20, 21], SamplingParams(max_tokens=4))
+    s.add(w1)
+    s.add(w2)
+    nxt, npre = s.schedule()
+    assert npre is True and [x.seq for x in nxt] == [w1]
+
+
+# ---- test_sampler.py
+def test_top_k_masks_out_lower_ranked_logits():
+    logits = torch.tensor([[5.0, 4.0, 3.0, 2.0]])
+    m = Sampler._apply_top_k(logits.clone(), torch.tensor([2], dtype=torch.int32))
+    assert torch.isneginf(m[0, 2]) and torch.isneginf(m[0, 3]) and m[0, 0] == 5.0 and m[0, 1] == 4.0
+
+
+def test_top_p_masks_tail_outside_probability_mass():
+    logits = torch.log(torch.tensor([[0.5, 0.3, 0.15, 0.05]]))
+    m = Sampler._apply_top_p(logits.clone(), torch.tensor([0.81]))
+    assert not torch.isneginf(m[0, 0]) and not torch.isneginf(m[0, 1])
+    assert torch.isneginf(m[0, 2]) and torch.isneginf(m[0, 3])
+
+
+def test_top_p_uses_strict_boundary():
+    logits = torch.log(torch.tensor([[0.5, 0.3, 0.15, 0.05]]))
+    m = Sampler._apply_top_p(logits.clone(), torch.tensor([0.8]))
+    assert not torch.isneginf(m[0, 0])
+    assert torch.isneginf(m[0, 1]) and torch.isneginf(m[0, 2]) and torch.isneginf(m[0, 3])
