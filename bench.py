@@ -56,6 +56,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--profile", default="", choices=["", "decode-kernel", "decode-steps"],
+                    help="run a short profiling case instead of the benchmark: the CUDA profiler range "
+                         "(cudaProfilerStart/Stop, for ncu --profile-from-start off) covers --steps "
+                         "launches of the decode kernel alone (decode-kernel) or --steps engine decode "
+                         "steps at the job's mid context (decode-steps)")
     return ap.parse_args()
 
 
@@ -322,8 +327,71 @@ def run_ours(args):
     llm.exit()
 
 
+def run_profile(args):
+    """Short, self-contained cases for ncu (one GPU)."""
+    import torch
+
+    from hilda_vllm_b200 import LLM, SamplingParams, kernels
+
+    torch.cuda.set_device(0)
+    g = torch.Generator().manual_seed(args.seed)
+    if args.profile == "decode-kernel":
+        # Config-2 shapes at mid-job: 256 sequences, contexts U[65, 1087] (mean ~576), Hq 16 / Hk 8.
+        b, hq, hk, d, bs = NUM_SEQS, 16, 8, 128, 256
+        lens = torch.randint(PROMPT_LEN + 1, PROMPT_LEN + OUTPUT_LEN, (b,), generator=g)
+        nblk = [-(-int(n) // bs) for n in lens]
+        perm = torch.randperm(sum(nblk), generator=g).tolist()
+        mb = max(nblk)
+        tables, off = [], 0
+        for n in nblk:
+            tables.append(perm[off:off + n] + [-1] * (mb - n))
+            off += n
+        dev = torch.device("cuda", 0)
+        kc = torch.randn(sum(nblk), bs, hk, d, device=dev, dtype=torch.bfloat16)
+        vc = torch.randn_like(kc)
+        q = torch.randn(b, hq, d, device=dev, dtype=torch.bfloat16)
+        bt = torch.tensor(tables, dtype=torch.int32, device=dev)
+        ln = lens.to(torch.int32).to(dev)
+        out = torch.empty_like(q)
+        ws = kernels.make_decode_workspace(b, hq, d, mb, bs, dev)
+        for _ in range(3):
+            kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        for _ in range(args.steps):
+            kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        nbytes = int(lens.sum()) * hk * d * 2 * 2 + b * hq * d * 4
+        print(json.dumps({"profile": "decode-kernel", "launches": args.steps, "bytes_per_launch": nbytes,
+                          "cache_gb": round(2 * kc.numel() * 2 / 1e9, 2)}))
+        return
+    # decode-steps: the engine at the job's mid context (prompts of 576 tokens, 256 sequences).
+    ctx = PROMPT_LEN + OUTPUT_LEN // 2
+    prompts = [torch.randint(0, 151936, (ctx,), generator=g).tolist() for _ in range(NUM_SEQS)]
+    llm = LLM(str(CFG_DIR), load_format="random", seed=args.seed, max_num_seqs=NUM_SEQS, max_model_len=MAX_MODEL_LEN,
+              max_num_batched_tokens=16384, gpu_memory_utilization=0.85)
+    sp = SamplingParams(greedy=True, max_tokens=args.steps + 3, ignore_eos=True)
+    for p in prompts:
+        llm.add_request(p, sp)
+    while llm.scheduler.waiting:
+        llm.step()
+    llm.step()  # first decode step outside the range (full packet)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    for _ in range(args.steps):
+        llm.step()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print(json.dumps({"profile": "decode-steps", "steps": args.steps, "context": ctx + 1}))
+    llm.exit()
+
+
 def main():
     args = parse()
+    if args.profile:
+        run_profile(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args)
         return

@@ -8,6 +8,8 @@ step() returns the reference's 13-tuple; the speculative-decoding fields are alw
 from __future__ import annotations
 
 import atexit
+import os
+import socket
 from dataclasses import fields
 from time import perf_counter
 
@@ -21,6 +23,12 @@ from hilda_vllm_b200.sampling_params import SamplingParams
 from hilda_vllm_b200.utils.tokenizer import load_tokenizer
 
 
+def _free_port() -> int:
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        return sock.getsockname()[1]
+
+
 class LLMEngine:
 
     def __init__(self, model, **kwargs):
@@ -29,6 +37,9 @@ class LLMEngine:
         self.config = config
         self.ps = []
         self.events = []
+        if config.tensor_parallel_size > 1 and config.distributed_executor == "spawn" \
+                and "MINI_VLLM_DIST_PORT" not in os.environ:
+            os.environ["MINI_VLLM_DIST_PORT"] = str(_free_port())  # inherited by the spawned ranks
         if config.distributed_executor == "external" and config.tensor_parallel_size > 1:
             import torch.distributed as dist
             rank = dist.get_rank()

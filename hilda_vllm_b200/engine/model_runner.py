@@ -103,9 +103,10 @@ class ModelRunner:
         self.external = getattr(config, "distributed_executor", "spawn") == "external"
         self.io_bytes = {"h2d": 0, "d2h": 0}
         self.recording: list[torch.Tensor] | None = None
-        if not dist.is_initialized():
+        if self.world_size > 1 and not dist.is_initialized():
             port = int(os.getenv("MINI_VLLM_DIST_PORT", "2333"))
-            dist.init_process_group("nccl", f"tcp://127.0.0.1:{port}", world_size=self.world_size, rank=rank)
+            dist.init_process_group("nccl", f"tcp://127.0.0.1:{port}", world_size=self.world_size, rank=rank,
+                                    device_id=torch.device("cuda", int(os.getenv("LOCAL_RANK", rank))))
         self.rpc_group = None
         if self.world_size > 1 and self.external:
             # Ranks launched by torchrun: the control plane is a gloo group (object broadcast
@@ -156,7 +157,7 @@ class ModelRunner:
         self.graphs = {}
         self.graph_pool = None
         torch.cuda.synchronize()
-        if dist.is_initialized():
+        if self.world_size > 1 and dist.is_initialized():
             dist.destroy_process_group()
 
     def loop(self):
@@ -292,7 +293,6 @@ class ModelRunner:
             slot_mapping=torch.full((max_bs,), -1, dtype=torch.int32, device=dev),
             context_lens=torch.zeros(max_bs, dtype=torch.int32, device=dev),
             block_tables=torch.full((max_bs, mb), -1, dtype=torch.int32, device=dev),
-            outputs=torch.zeros(max_bs, hf.hidden_size, dtype=torch.bfloat16, device=dev),
             next_tokens=torch.zeros(max_bs, dtype=torch.int64, device=dev),
             slot_seq_ids=torch.full((max_bs,), -1, dtype=torch.int64, device=dev),
             slot_bt_lens=torch.zeros(max_bs, dtype=torch.int32, device=dev),
@@ -362,7 +362,6 @@ class ModelRunner:
                                   gv["context_lens"], gv["block_tables"])
         self._set_decode_context(n)
         hidden = self.model(gv["input_ids"][:n], gv["positions"][:n])
-        gv["outputs"][:n] = hidden
         logits = self.logits_buf[:n]
         torch.matmul(hidden, self.model.lm_head.weight.t(), out=logits)
         if greedy and self.world_size == 1:
@@ -503,6 +502,7 @@ class ModelRunner:
         self.recorded_packets = rec
         return rec
 
+    @torch.inference_mode()
     def reset_decode_state(self):
         """Forget every decode slot (device buffers and the host mirror)."""
         gv = self.graph_vars

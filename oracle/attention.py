@@ -21,7 +21,7 @@ import torch
 
 def _gather_pages(cache, table_row, length, block_size):
     n_pages = -(-length // block_size)
-    pages = torch.as_tensor(table_row[:n_pages], dtype=torch.long)
+    pages = torch.as_tensor(table_row[:n_pages], dtype=torch.long, device=cache.device)
     return cache[pages].reshape(-1, cache.shape[2], cache.shape[3])[:length]
 
 
@@ -46,7 +46,7 @@ def paged_decode(q, k_cache, v_cache, block_tables, context_lens, scale, k_scale
 
     b, hq, d = q.shape
     bs = k_cache.shape[1]
-    out = torch.zeros(b, hq, d, dtype=torch.float32)
+    out = torch.zeros(b, hq, d, dtype=torch.float32, device=q.device)
     for i in range(b):
         length = int(context_lens[i])
         if length <= 0:
@@ -63,7 +63,7 @@ def paged_decode(q, k_cache, v_cache, block_tables, context_lens, scale, k_scale
 
 def varlen_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, scale, block_table=None):
     tq, hq, d = q.shape
-    out = torch.zeros(tq, hq, d, dtype=torch.float32)
+    out = torch.zeros(tq, hq, d, dtype=torch.float32, device=q.device)
     cq = cu_seqlens_q.tolist()
     ck = cu_seqlens_k.tolist()
     for s in range(len(cq) - 1):
@@ -77,8 +77,8 @@ def varlen_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, scale, block_table=None)
             vv = _gather_pages(v, block_table[s].tolist(), lk, bs)
         else:
             kk, vv = k[ck[s]:ck[s + 1]], v[ck[s]:ck[s + 1]]
-        i = torch.arange(lq).unsqueeze(1)
-        j = torch.arange(lk).unsqueeze(0)
+        i = torch.arange(lq, device=q.device).unsqueeze(1)
+        j = torch.arange(lk, device=q.device).unsqueeze(0)
         mask = j <= i + (lk - lq)
         out[q0:q1] = _attend(q[q0:q1].float(), kk.float(), vv.float(), scale, mask)
     return out

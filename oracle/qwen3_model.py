@@ -86,7 +86,7 @@ class Qwen3Oracle:
         if ctx["is_prefill"]:
             if ctx.get("block_tables") is not None:
                 o = oattn.varlen_prefill(q, self.k_cache[layer], self.v_cache[layer], ctx["cu_seqlens_q"],
-                                         ctx["cu_seqlens_k"], scale, block_table=ctx["block_tables"])
+                                         ctx["cu_seqlens_k"], scale, block_table=ctx["block_tables"].cpu())
             else:
                 o = oattn.varlen_prefill(q, k, v, ctx["cu_seqlens_q"], ctx["cu_seqlens_k"], scale)
         else:
