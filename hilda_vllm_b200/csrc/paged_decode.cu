@@ -21,6 +21,9 @@
 // ticket in the workspace); sequences that fit in one split write the output directly.
 #include "hl_common.cuh"
 
+#include <atomic>
+#include <mutex>
+
 namespace hl {
 namespace {
 
@@ -569,4 +572,91 @@ extern "C" int hl_paged_decode_read_errors(const void* workspace, int32_t* error
     return HL_ERR_CUDA;
   }
   return HL_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free variant of the decode entry point.
+//
+// Some callers cannot hand us a workspace: hosts that bind this library through a foreign-
+// function interface and have no device allocator of their own, serving loops whose memory
+// is fully carved out up front and that must not call cudaMalloc (it synchronises the device
+// and can fail under memory pressure), and plugins that may only touch the buffers their
+// host passes in.  For them the split-K scratch lives in this file-scope device array, which
+// every GPU that loads the library reserves once, until the process exits.
+// ------------------------------------------------------------------------------------------
+namespace hl {
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = int64_t(32) << 20;  // 32 MiB per GPU
+static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::atomic<uint8_t*> g_scratch_ptr[kMaxDevices];
+std::mutex g_scratch_mutex;
+
+// Device address of g_decode_scratch on the current device (host code only holds a host-side
+// stand-in for the symbol, so the address must be looked up per device).
+int scratch_for_current_device(uint8_t** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("hl_paged_decode_noalloc: no usable current device (%s)", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
+  uint8_t* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    p = g_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      void* addr = nullptr;
+      e = cudaGetSymbolAddress(&addr, g_decode_scratch);
+      if (e != cudaSuccess || addr == nullptr) {
+        set_error("hl_paged_decode_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        return HL_ERR_CUDA;
+      }
+      p = static_cast<uint8_t*>(addr);
+      g_scratch_ptr[dev].store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
+  return HL_OK;
+}
+
+}  // namespace
+}  // namespace hl
+
+extern "C" int64_t hl_paged_decode_noalloc_capacity(void) { return hl::kNoAllocScratchBytes; }
+
+extern "C" int hl_paged_decode_noalloc(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+                                       int kv_dtype, const float* k_scale, const float* v_scale,
+                                       const int32_t* block_tables, int64_t bt_stride, int max_blocks_per_seq,
+                                       const int32_t* context_lens, int batch, int num_q_heads, int num_kv_heads,
+                                       int head_dim, int block_size, int64_t num_blocks, float softmax_scale,
+                                       void* out, int64_t out_row_stride, void* stream) {
+  clear_error();
+  HL_CHECK_ARG(batch >= 0, "hl_paged_decode_noalloc: batch < 0");
+  if (batch == 0) return HL_OK;
+  HL_CHECK_ARG(num_q_heads > 0 && head_dim > 0 && max_blocks_per_seq > 0 && block_size > 0,
+               "hl_paged_decode_noalloc: bad shape");
+  const int64_t need =
+      hl_paged_decode_workspace_size(batch, num_q_heads, head_dim, max_blocks_per_seq, block_size);
+  if (need < 0 || need > kNoAllocScratchBytes) {
+    set_error("hl_paged_decode_noalloc: this shape needs %lld bytes of scratch, more than the built-in %lld "
+              "(use hl_paged_decode with a caller-provided workspace)",
+              (long long)need, (long long)kNoAllocScratchBytes);
+    return HL_ERR_UNSUPPORTED;
+  }
+  uint8_t* scratch = nullptr;
+  int rc = scratch_for_current_device(&scratch);
+  if (rc != HL_OK) return rc;
+  // The array keeps whatever the previous call left: zero the error word and the tickets,
+  // which the kernel expects to find at zero (the partials are always written before read).
+  cudaError_t e = cudaMemsetAsync(scratch, 0, size_t(kWsMlOff), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("hl_paged_decode_noalloc: cudaMemsetAsync failed: %s", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
+  return hl_paged_decode(q, q_row_stride, k_cache, v_cache, kv_dtype, k_scale, v_scale, block_tables, bt_stride,
+                         max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, head_dim, block_size,
+                         num_blocks, softmax_scale, out, out_row_stride, scratch, kNoAllocScratchBytes, stream);
 }

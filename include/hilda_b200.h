@@ -113,6 +113,29 @@ int hl_paged_decode(const void* q, int64_t q_row_stride,
                     void* out, int64_t out_row_stride,
                     void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of hl_paged_decode (no counterpart in the reference).  For callers
+ * that cannot allocate device memory themselves — a host binding this library through an FFI
+ * with no device allocator, or a serving loop whose memory is all reserved up front and must not
+ * call cudaMalloc (it synchronises the device and can fail under memory pressure) — the split-K
+ * scratch is a file-scope device array of hl_paged_decode_noalloc_capacity() bytes (32 MiB),
+ * reserved on every GPU that loads the library until the process exits.  Shapes whose
+ * hl_paged_decode_workspace_size exceeds it are rejected with HL_ERR_UNSUPPORTED.  The first call
+ * on a device looks up the array's device address (make it before any stream capture); each call
+ * then clears the array's ticket region on `stream` and launches the same kernel as
+ * hl_paged_decode.  All calls share the one array: calls that overlap on the GPU (other streams,
+ * other threads) race and must be serialised by the caller.  Allocates nothing. */
+int hl_paged_decode_noalloc(const void* q, int64_t q_row_stride,
+                            const void* k_cache, const void* v_cache, int kv_dtype,
+                            const float* k_scale, const float* v_scale,
+                            const int32_t* block_tables, int64_t bt_stride, int max_blocks_per_seq,
+                            const int32_t* context_lens, int batch,
+                            int num_q_heads, int num_kv_heads, int head_dim,
+                            int block_size, int64_t num_blocks, float softmax_scale,
+                            void* out, int64_t out_row_stride, void* stream);
+
+/* Size in bytes of the scratch array behind hl_paged_decode_noalloc. */
+int64_t hl_paged_decode_noalloc_capacity(void);
+
 /* Reads the error word the decode kernel keeps in its workspace (bit 0: an mbarrier wait
  * timed out; bit 1: a block id was out of range).  Synchronous: copies 4 bytes to host. */
 int hl_paged_decode_read_errors(const void* workspace, int32_t* errors_out, void* stream);
