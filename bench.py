@@ -226,7 +226,8 @@ def run_ours(args):
               max_model_len=MAX_MODEL_LEN, max_num_batched_tokens=16384, tensor_parallel_size=world,
               gpu_memory_utilization=0.85, distributed_executor="external" if world > 1 else "spawn")
     if getattr(llm, "is_worker", False):
-        dist.destroy_process_group()
+        if dist.is_initialized():
+            dist.destroy_process_group()
         return  # worker ranks served rank 0's calls inside LLM(...) until it exited
     runner = llm.model_runner
     hf = llm.config.hf_config

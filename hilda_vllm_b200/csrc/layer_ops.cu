@@ -186,7 +186,7 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloa
 // One CTA per row; writes the token both to out_tokens[row] and, when given, to
 // next_tokens[slot_of_row[row]] so the next decode step can read it on the device.
 __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int vocab,
-                              int64_t* __restrict__ out_tokens) {
+                              int64_t index_offset, int64_t* __restrict__ out_tokens, float* __restrict__ out_values) {
   const int row = blockIdx.x;
   const __nv_bfloat16* x = logits + int64_t(row) * row_stride;
   float best = -INFINITY;
@@ -228,7 +228,10 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
         bi = oi;
       }
     }
-    if (lane == 0) out_tokens[row] = (bi == 0x7fffffff) ? 0 : bi;
+    if (lane == 0) {
+      out_tokens[row] = index_offset + ((bi == 0x7fffffff) ? 0 : bi);
+      if (out_values) out_values[row] = best;
+    }
   }
 }
 
@@ -313,7 +316,18 @@ extern "C" int hl_argmax(const void* logits, int64_t row_stride, int rows, int v
   if (rows == 0) return HL_OK;
   HL_CHECK_ARG(logits && out_tokens && rows > 0 && vocab > 0, "hl_argmax: bad arguments");
   argmax_kernel<<<rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>((const __nv_bfloat16*)logits, row_stride, vocab,
-                                                                       out_tokens);
+                                                                       0, out_tokens, nullptr);
   HL_CHECK_LAUNCH("hl_argmax");
+  return HL_OK;
+}
+
+extern "C" int hl_argmax_shard(const void* logits, int64_t row_stride, int rows, int vocab, int64_t index_offset,
+                               int64_t* out_tokens, float* out_values, void* stream) {
+  clear_error();
+  if (rows == 0) return HL_OK;
+  HL_CHECK_ARG(logits && out_tokens && out_values && rows > 0 && vocab > 0, "hl_argmax_shard: bad arguments");
+  argmax_kernel<<<rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>((const __nv_bfloat16*)logits, row_stride, vocab,
+                                                                       index_offset, out_tokens, out_values);
+  HL_CHECK_LAUNCH("hl_argmax_shard");
   return HL_OK;
 }

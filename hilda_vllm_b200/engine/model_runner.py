@@ -36,6 +36,27 @@ MODEL_REGISTRY = {"qwen3": Qwen3ForCausalLM}
 MAX_GRAPH_BS = 512
 
 
+def rpc_send(group, method: str, *args) -> None:
+    """Rank 0 side of the torchrun-mode control plane: broadcast (method, args) to all ranks
+    over a gloo group (the spawn mode uses the reference's shared memory + events instead)."""
+    dist.broadcast_object_list([[method, *args]], src=0, group=group)
+
+
+def rpc_recv(group):
+    box = [None]
+    dist.broadcast_object_list(box, src=0, group=group)
+    method, *args = box[0]
+    return method, args
+
+
+def merge_shard_argmax(all_val: torch.Tensor, all_idx: torch.Tensor) -> torch.Tensor:
+    """Global greedy token from per-shard (max value, global index) pairs, shards ordered by
+    vocabulary range ([tp, n] each): the first shard holding the maximum wins, which is the
+    lowest vocabulary id among equal maxima, as a single argmax over all logits would pick."""
+    best = all_val.argmax(0, keepdim=True)
+    return all_idx.gather(0, best).squeeze(0)
+
+
 def graph_batch_sizes(max_bs: int) -> list[int]:
     max_bs = min(max_bs, MAX_GRAPH_BS)
     return [b for b in (1, 2, 4, 8) if b <= max_bs] + list(range(16, max_bs + 1, 16))
@@ -170,10 +191,7 @@ class ModelRunner:
     def read_shm(self):
         assert self.world_size > 1 and self.rank > 0
         if self.external:
-            box = [None]
-            dist.broadcast_object_list(box, src=0, group=self.rpc_group)
-            method, *args = box[0]
-            return method, args
+            return rpc_recv(self.rpc_group)
         self.event.wait()
         n = int.from_bytes(self.shm.buf[0:4], "little")
         method, *args = pickle.loads(self.shm.buf[4:n + 4])
@@ -183,7 +201,7 @@ class ModelRunner:
     def write_shm(self, method, *args):
         assert self.world_size > 1 and self.rank == 0
         if self.external:
-            dist.broadcast_object_list([[method, *args]], src=0, group=self.rpc_group)
+            rpc_send(self.rpc_group, method, *args)
             return
         data = pickle.dumps([method, *args])
         self.shm.buf[0:4] = len(data).to_bytes(4, "little")
@@ -235,6 +253,10 @@ class ModelRunner:
         num_blocks = budget // self.kv_block_bytes()
         if config.kvcache_block_cap > 0:
             num_blocks = min(num_blocks, config.kvcache_block_cap)
+        if self.world_size > 1:  # rank 0 schedules for every rank: use the smallest pool
+            t = torch.tensor([num_blocks], dtype=torch.int64, device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            num_blocks = int(t.item())
         config.num_kvcache_blocks = int(num_blocks)
         assert config.num_kvcache_blocks > 0, "no memory left for the KV cache"
         hk = hf.num_key_value_heads // self.world_size
@@ -307,6 +329,12 @@ class ModelRunner:
         hq = hf.num_attention_heads // self.world_size
         d = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
         self.decode_workspace = kernels.make_decode_workspace(max_bs, hq, d, mb, self.block_size, dev)
+        # Per-rank greedy reduction buffers (tensor parallelism).
+        tp = self.world_size
+        self.tp_idx = torch.zeros(max_bs, dtype=torch.int64, device=dev)
+        self.tp_val = torch.zeros(max_bs, dtype=torch.float32, device=dev)
+        self.tp_all_idx = torch.zeros(tp, max_bs, dtype=torch.int64, device=dev)
+        self.tp_all_val = torch.zeros(tp, max_bs, dtype=torch.float32, device=dev)
         for module in self.attention_layers():
             module.decode_workspace = self.decode_workspace
         self.logits_buf = None
@@ -364,9 +392,28 @@ class ModelRunner:
         hidden = self.model(gv["input_ids"][:n], gv["positions"][:n])
         logits = self.logits_buf[:n]
         torch.matmul(hidden, self.model.lm_head.weight.t(), out=logits)
-        if greedy and self.world_size == 1:
-            kernels.argmax(logits, gv["next_tokens"][:n])
+        if greedy:
+            self._greedy_tokens(logits, gv["next_tokens"][:n])
         return logits
+
+    def _greedy_tokens(self, logits: torch.Tensor, out: torch.Tensor):
+        """Argmax over the full vocabulary into `out` (device), on every rank.  Under tensor
+        parallelism each rank reduces its vocabulary shard to (max, index) and the ranks
+        all-gather those pairs (2 x 12 bytes per row instead of the logits); the lowest rank
+        wins ties, which is the lowest global index because shards are ordered."""
+        if self.world_size == 1:
+            kernels.argmax(logits, out)
+            return
+        n = logits.shape[0]
+        head = self.model.lm_head
+        idx = self.tp_idx[:n]
+        val = self.tp_val[:n]
+        kernels.argmax_shard(logits, head.vocab_start_idx, idx, val)
+        all_val = self.tp_all_val.view(-1)[: self.world_size * n].view(self.world_size, n)
+        all_idx = self.tp_all_idx.view(-1)[: self.world_size * n].view(self.world_size, n)
+        dist.all_gather_into_tensor(all_val, val)
+        dist.all_gather_into_tensor(all_idx, idx)
+        out.copy_(merge_shard_argmax(all_val, all_idx))
 
     def _ensure_logits_buf(self, rows: int):
         vocab_local = self.model.lm_head.num_embeddings_per_partition
@@ -429,17 +476,20 @@ class ModelRunner:
         real_seqs = [scheduled_seqs[i].seq for i in real]
         greedy = all(s.greedy for s in real_seqs)
         gv = self.graph_vars
-        if graph_bs in self.graphs and greedy and self.world_size == 1:
-            self.graphs[graph_bs].replay()
-            logits = None
-        else:
-            n = graph_bs
+        if greedy:
+            # Tokens are picked on the device (in the graph when there is one) on every rank.
             if graph_bs in self.graphs:
                 self.graphs[graph_bs].replay()
-                logits = self.logits_buf[:n]
             else:
-                self._ensure_logits_buf(n)
-                logits = self._decode_body(n, greedy=False)
+                self._ensure_logits_buf(graph_bs)
+                self._decode_body(graph_bs, greedy=True)
+        else:
+            if graph_bs in self.graphs:
+                self.graphs[graph_bs].replay()
+                logits = self.logits_buf[:graph_bs]
+            else:
+                self._ensure_logits_buf(graph_bs)
+                logits = self._decode_body(graph_bs, greedy=False)
             logits = self._gather_logits(logits)
             if self.rank == 0 and real:
                 sub = logits[real].contiguous()
@@ -467,7 +517,7 @@ class ModelRunner:
     @torch.inference_mode()
     def capture_cudagraph(self):
         self.graph_bs = graph_batch_sizes(self.config.max_num_seqs)
-        greedy = self.world_size == 1
+        greedy = True
         self._ensure_logits_buf(self.graph_bs[-1])
         # The packet is all zeros during capture: batch 0, every slot padding.
         self.packet_dev.zero_()

@@ -310,3 +310,14 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     check(lib.hl_argmax(logits.data_ptr(), logits.stride(0), rows, vocab, out.data_ptr(), _stream(logits)),
           "hl_argmax")
     return out
+
+
+def argmax_shard(logits: torch.Tensor, index_offset: int, out_tokens: torch.Tensor, out_values: torch.Tensor):
+    """Per-row (max value, index + index_offset) of one vocabulary shard (hl_argmax_shard)."""
+    _cuda(logits, out_tokens, out_values)
+    rows, vocab = logits.shape
+    assert logits.dtype == torch.bfloat16 and logits.stride(1) == 1
+    assert out_tokens.dtype == torch.int64 and out_values.dtype == torch.float32
+    lib = _lib.load()
+    check(lib.hl_argmax_shard(logits.data_ptr(), logits.stride(0), rows, vocab, int(index_offset),
+                              out_tokens.data_ptr(), out_values.data_ptr(), _stream(logits)), "hl_argmax_shard")

@@ -246,6 +246,13 @@ int hl_silu_mul(const void* in, int64_t in_stride, void* out, int64_t out_stride
 int hl_argmax(const void* logits, int64_t row_stride, int rows, int vocab, int64_t* out_tokens,
               void* stream);
 
+/* Greedy token of one vocabulary shard under tensor parallelism: per row the index of the
+ * maximum plus index_offset (the shard's first vocabulary id) and the maximum itself, so ranks
+ * can all-gather (value, index) pairs instead of the logits that the reference gathers to rank 0
+ * (mini_vllm/layers/embed_head.py:56-66). */
+int hl_argmax_shard(const void* logits, int64_t row_stride, int rows, int vocab, int64_t index_offset,
+                    int64_t* out_tokens, float* out_values, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -128,3 +128,23 @@ def test_fp8_kv_engine_runs_and_tracks_bf16(tmp_path, golden_dir):
     assert res["fp8"][0] == res["fp8"][1]
     agree = sum(a[:4] == b[:4] for a, b in zip(res["auto"][0], res["fp8"][0]))
     assert agree >= 2
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tensor_parallel_2_matches_oracle(tmp_path, golden_dir):
+    """TP=2 (KV heads sharded, all-reduce after o_proj/down_proj, greedy via per-shard
+    (max, index) all-gather inside the graph), spawn mode as the reference launches ranks."""
+    from transformers import AutoConfig
+
+    hf = AutoConfig.from_pretrained(CFG_06B)
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, hf.vocab_size, (n,), generator=g).tolist() for n in (64, 64, 200, 17)]
+    steps = 32
+    llm = LLM(str(CFG_06B), load_format="random", seed=0, max_num_seqs=8, max_model_len=1344,
+              max_num_batched_tokens=16384, kvcache_block_cap=128, gpu_memory_utilization=0.5,
+              tensor_parallel_size=2)
+    outs = llm.generate(prompts, SamplingParams(greedy=True, max_tokens=steps + 1, ignore_eos=True), use_tqdm=False)
+    llm.exit()
+    checked, exact, ties = check_against_oracle(hf, 0, prompts, [o["token_ids"] for o in outs])
+    print(f"TP=2 greedy: {exact}/{checked} exact argmax matches, {len(ties)} bf16 ties")
+    assert checked == len(prompts) * (steps + 1) and exact >= 0.9 * checked
