@@ -358,14 +358,20 @@ def run_profile(args):
         for _ in range(3):
             kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws)
         torch.cuda.synchronize()
+        stream = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.profiler.start()
+        e0.record(stream)
         for _ in range(args.steps):
             kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws)
+        e1.record(stream)
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
         nbytes = int(lens.sum()) * hk * d * 2 * 2 + b * hq * d * 4
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
         print(json.dumps({"profile": "decode-kernel", "launches": args.steps, "bytes_per_launch": nbytes,
-                          "cache_gb": round(2 * kc.numel() * 2 / 1e9, 2)}))
+                          "cache_gb": round(2 * kc.numel() * 2 / 1e9, 2), "us_per_launch": round(us, 2),
+                          "gb_per_s": round(nbytes / us / 1e3, 1)}))
         return
     # decode-steps: the engine at the job's mid context (prompts of 576 tokens, 256 sequences).
     ctx = PROMPT_LEN + OUTPUT_LEN // 2

@@ -31,7 +31,7 @@ constexpr int kDecodeThreads = 256;
 constexpr int kHeadDim = 128;
 constexpr int kSplit = 128;            // tokens per CTA (divides every supported block size)
 constexpr int kTileBytes = 16384;      // bytes per K (and per V) pipeline stage
-constexpr int kStages = 3;
+constexpr int kStages = 2;
 constexpr int kMaxBatch = 4096;        // capacity of the ticket array in the workspace
 constexpr int64_t kWsErrOff = 0;       // int32 error word(s)
 constexpr int64_t kWsTicketOff = 256;  // int32 tickets[kMaxBatch]
@@ -74,29 +74,59 @@ struct Traits {
   static_assert(kTPH >= 1, "tile too small");
 };
 
-// Load 8 consecutive K or V elements (this lane's D-slice) from shared memory as floats.
+// Load this lane's 8 consecutive K or V elements (its D-slice) from shared memory as four
+// float2 pairs of adjacent dimensions, ready for the packed fp32x2 FMA of sm_100.
 template <bool FP8>
-__device__ __forceinline__ void load8(const uint8_t* p, float (&x)[8]) {
+__device__ __forceinline__ void load8x2(const uint8_t* p, float2 (&x)[4]) {
   if constexpr (FP8) {
     const uint2 v = *reinterpret_cast<const uint2*>(p);
-    const uint32_t w[2] = {v.x, v.y};
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float2 a = e4m3x2_to_float2(static_cast<uint16_t>(w[i] & 0xffffu));
-      const float2 b = e4m3x2_to_float2(static_cast<uint16_t>(w[i] >> 16));
-      x[4 * i + 0] = a.x;
-      x[4 * i + 1] = a.y;
-      x[4 * i + 2] = b.x;
-      x[4 * i + 3] = b.y;
-    }
+    x[0] = e4m3x2_to_float2(static_cast<uint16_t>(v.x & 0xffffu));
+    x[1] = e4m3x2_to_float2(static_cast<uint16_t>(v.x >> 16));
+    x[2] = e4m3x2_to_float2(static_cast<uint16_t>(v.y & 0xffffu));
+    x[3] = e4m3x2_to_float2(static_cast<uint16_t>(v.y >> 16));
   } else {
     const uint4 v = *reinterpret_cast<const uint4*>(p);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    x[0] = make_float2(bf16lo(v.x), bf16hi(v.x));
+    x[1] = make_float2(bf16lo(v.y), bf16hi(v.y));
+    x[2] = make_float2(bf16lo(v.z), bf16hi(v.z));
+    x[3] = make_float2(bf16lo(v.w), bf16hi(v.w));
+  }
+}
+
+// Sums NV per-lane partial values over the 16 lanes of each half-warp so that every lane ends
+// with all NV totals.  A butterfly reduce-scatter (each level halves the values a lane keeps,
+// exchanging the other half with its partner) followed by an all-gather costs about
+// 3*NV + log2(16) shuffles and adds instead of 4*NV for NV independent shuffle trees.
+template <int NV>
+__device__ __forceinline__ void halfwarp_allreduce(float (&v)[NV], int ln, int hw) {
+  if constexpr (NV > 16) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      x[2 * i] = bf16lo(w[i]);
-      x[2 * i + 1] = bf16hi(w[i]);
+    for (int off = 8; off >= 1; off >>= 1)
+#pragma unroll
+      for (int k = 0; k < NV; ++k) v[k] += __shfl_xor_sync(0xffffffffu, v[k], off);
+  } else {
+#pragma unroll
+    for (int lvl = 0; lvl < 4; ++lvl) {
+      const int off = 8 >> lvl;
+      const int cur = NV >> lvl;  // values still held before this level (compile-time after unrolling)
+      if (cur >= 2) {
+        const bool upper = (ln & off) != 0;
+#pragma unroll
+        for (int k = 0; k < (NV >> (lvl + 1)); ++k) {
+          const float lo = v[k], hi = v[k + (NV >> (lvl + 1))];
+          const float send = upper ? lo : hi;
+          const float keep = upper ? hi : lo;
+          v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      } else {
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+      }
     }
+    // Lane ln now holds total number (ln >> (4 - log2 NV)); gather all of them.
+    constexpr int kShift = NV == 1 ? 4 : NV == 2 ? 3 : NV == 4 ? 2 : NV == 8 ? 1 : 0;
+    const float mine = v[0];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) v[k] = __shfl_sync(0xffffffffu, mine, hw * 16 + (k << kShift));
   }
 }
 
@@ -112,8 +142,8 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float (&x)[8]) {
 
 // Merge softmax state (m2, l2, a2) into (m, l, a).  m == -inf means "empty".
 template <int G>
-__device__ __forceinline__ void merge_state(float (&m)[G], float (&l)[G], float (&a)[G][8], const float (&m2)[G],
-                                            const float (&l2)[G], const float (&a2)[G][8]) {
+__device__ __forceinline__ void merge_state(float (&m)[G], float (&l)[G], float2 (&a)[G][4], const float (&m2)[G],
+                                            const float (&l2)[G], const float2 (&a2)[G][4]) {
 #pragma unroll
   for (int j = 0; j < G; ++j) {
     const float mn = fmaxf(m[j], m2[j]);
@@ -122,13 +152,15 @@ __device__ __forceinline__ void merge_state(float (&m)[G], float (&l)[G], float 
     const float c2 = exp2f(m2[j] - mn);
     l[j] = l[j] * c1 + l2[j] * c2;
 #pragma unroll
-    for (int d = 0; d < 8; ++d) a[j][d] = a[j][d] * c1 + a2[j][d] * c2;
+    for (int c = 0; c < 4; ++c)
+      a[j][c] = __ffma2_rn(a[j][c], make_float2(c1, c1), __fmul2_rn(a2[j][c], make_float2(c2, c2)));
     m[j] = mn;
   }
 }
 
 template <bool FP8, int G, int HK>
-__global__ void __launch_bounds__(kDecodeThreads, (G <= 4 ? 2 : 1)) paged_decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kDecodeThreads, (G <= 2 ? 3 : (G <= 4 ? 2 : 1)))
+paged_decode_kernel(const DecodeParams p) {
   using Tr = Traits<FP8, HK>;
   constexpr int kT = Tr::kT;
   constexpr int kRow = Tr::kRowBytes;
@@ -200,29 +232,29 @@ __global__ void __launch_bounds__(kDecodeThreads, (G <= 4 ? 2 : 1)) paged_decode
 
   // Query slice of the G query heads that share KV head h, pre-scaled so that the
   // softmax runs in base 2 (and, for FP8, with k_scale folded in).
-  float qs[G][8];
+  float2 qs[G][4];
   {
     const float ks = (FP8 && p.k_scale) ? p.k_scale[h] : 1.0f;
+    const float f = p.scale_log2 * ks;
     const __nv_bfloat16* qb = p.q + int64_t(b) * p.q_row_stride;
 #pragma unroll
     for (int j = 0; j < G; ++j) {
       const uint4 v = *reinterpret_cast<const uint4*>(qb + (h * G + j) * kHeadDim + 8 * ln);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        qs[j][2 * i] = bf16lo(w[i]) * p.scale_log2 * ks;
-        qs[j][2 * i + 1] = bf16hi(w[i]) * p.scale_log2 * ks;
-      }
+      qs[j][0] = make_float2(bf16lo(v.x) * f, bf16hi(v.x) * f);
+      qs[j][1] = make_float2(bf16lo(v.y) * f, bf16hi(v.y) * f);
+      qs[j][2] = make_float2(bf16lo(v.z) * f, bf16hi(v.z) * f);
+      qs[j][3] = make_float2(bf16lo(v.w) * f, bf16hi(v.w) * f);
     }
   }
 
-  float m[G], l[G], acc[G][8];
+  float m[G], l[G];
+  float2 acc[G][4];
 #pragma unroll
   for (int j = 0; j < G; ++j) {
     m[j] = -INFINITY;
     l[j] = 0.f;
 #pragma unroll
-    for (int d = 0; d < 8; ++d) acc[j][d] = 0.f;
+    for (int c = 0; c < 4; ++c) acc[j][c] = make_float2(0.f, 0.f);
   }
 
   bool timed_out = false;
@@ -237,30 +269,25 @@ __global__ void __launch_bounds__(kDecodeThreads, (G <= 4 ? 2 : 1)) paged_decode
       const uint8_t* Vs = Ks + kTileBytes;
       const int tile_tok0 = tok0 + t * kT;
 
-      float sc[G][kTPH];
+      // Partial q.k over this lane's 8 dimensions, packed fp32x2 FMAs; sc[j * kTPH + i].
+      float sc[G * kTPH];
       bool valid[kTPH];
 #pragma unroll
       for (int i = 0; i < kTPH; ++i) {
         const int tt = phase * kTPW + 2 * i + hw;
         valid[i] = tile_tok0 + tt < tok1;
-        float kx[8];
-        load8<FP8>(Ks + tt * kRow + (h * kHeadDim + 8 * ln) * Tr::kElem, kx);
+        float2 kx[4];
+        load8x2<FP8>(Ks + tt * kRow + (h * kHeadDim + 8 * ln) * Tr::kElem, kx);
 #pragma unroll
         for (int j = 0; j < G; ++j) {
-          float s = 0.f;
-#pragma unroll
-          for (int d = 0; d < 8; ++d) s = fmaf(qs[j][d], kx[d], s);
-          sc[j][i] = s;
+          float2 a = __fmul2_rn(qs[j][0], kx[0]);
+          a = __ffma2_rn(qs[j][1], kx[1], a);
+          a = __ffma2_rn(qs[j][2], kx[2], a);
+          a = __ffma2_rn(qs[j][3], kx[3], a);
+          sc[j * kTPH + i] = a.x + a.y;
         }
       }
-      // Sum the 16 partial dot products of each half-warp.
-#pragma unroll
-      for (int off = 8; off >= 1; off >>= 1) {
-#pragma unroll
-        for (int j = 0; j < G; ++j)
-#pragma unroll
-          for (int i = 0; i < kTPH; ++i) sc[j][i] += __shfl_xor_sync(0xffffffffu, sc[j][i], off);
-      }
+      halfwarp_allreduce<G * kTPH>(sc, ln, hw);
 
       float pr[G][kTPH];
 #pragma unroll
@@ -268,7 +295,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (G <= 4 ? 2 : 1)) paged_decode
         float mt = -INFINITY;
 #pragma unroll
         for (int i = 0; i < kTPH; ++i)
-          if (valid[i]) mt = fmaxf(mt, sc[j][i]);
+          if (valid[i]) mt = fmaxf(mt, sc[j * kTPH + i]);
         const float mn = fmaxf(m[j], mt);
         if (mn == -INFINITY) {
 #pragma unroll
@@ -279,24 +306,27 @@ __global__ void __launch_bounds__(kDecodeThreads, (G <= 4 ? 2 : 1)) paged_decode
         float ps = 0.f;
 #pragma unroll
         for (int i = 0; i < kTPH; ++i) {
-          pr[j][i] = valid[i] ? exp2f(sc[j][i] - mn) : 0.f;
+          pr[j][i] = valid[i] ? exp2f(sc[j * kTPH + i] - mn) : 0.f;
           ps += pr[j][i];
         }
         l[j] = l[j] * corr + ps;
+        const float2 c2 = make_float2(corr, corr);
 #pragma unroll
-        for (int d = 0; d < 8; ++d) acc[j][d] *= corr;
+        for (int c = 0; c < 4; ++c) acc[j][c] = __fmul2_rn(acc[j][c], c2);
         m[j] = mn;
       }
 #pragma unroll
       for (int i = 0; i < kTPH; ++i) {
         if (!valid[i]) continue;  // never touch V rows past the context (may hold NaN bits)
         const int tt = phase * kTPW + 2 * i + hw;
-        float vx[8];
-        load8<FP8>(Vs + tt * kRow + (h * kHeadDim + 8 * ln) * Tr::kElem, vx);
+        float2 vx[4];
+        load8x2<FP8>(Vs + tt * kRow + (h * kHeadDim + 8 * ln) * Tr::kElem, vx);
 #pragma unroll
-        for (int j = 0; j < G; ++j)
+        for (int j = 0; j < G; ++j) {
+          const float2 p2 = make_float2(pr[j][i], pr[j][i]);
 #pragma unroll
-          for (int d = 0; d < 8; ++d) acc[j][d] = fmaf(pr[j][i], vx[d], acc[j][d]);
+          for (int c = 0; c < 4; ++c) acc[j][c] = __ffma2_rn(p2, vx[c], acc[j][c]);
+        }
       }
 
       }  // ok
@@ -326,13 +356,16 @@ __global__ void __launch_bounds__(kDecodeThreads, (G <= 4 ? 2 : 1)) paged_decode
 
   // Merge the two half-warps (they hold disjoint token subsets of the same D-slice).
   {
-    float m2[G], l2[G], a2[G][8];
+    float m2[G], l2[G];
+    float2 a2[G][4];
 #pragma unroll
     for (int j = 0; j < G; ++j) {
       m2[j] = __shfl_xor_sync(0xffffffffu, m[j], 16);
       l2[j] = __shfl_xor_sync(0xffffffffu, l[j], 16);
 #pragma unroll
-      for (int d = 0; d < 8; ++d) a2[j][d] = __shfl_xor_sync(0xffffffffu, acc[j][d], 16);
+      for (int c = 0; c < 4; ++c)
+        a2[j][c] = make_float2(__shfl_xor_sync(0xffffffffu, acc[j][c].x, 16),
+                               __shfl_xor_sync(0xffffffffu, acc[j][c].y, 16));
     }
     merge_state<G>(m, l, acc, m2, l2, a2);
   }
@@ -349,21 +382,25 @@ __global__ void __launch_bounds__(kDecodeThreads, (G <= 4 ? 2 : 1)) paged_decode
         e[0] = m[j];
         e[1] = l[j];
 #pragma unroll
-        for (int d = 0; d < 8; ++d) e[2 + d] = acc[j][d];
+        for (int c = 0; c < 4; ++c) {
+          e[2 + 2 * c] = acc[j][c].x;
+          e[3 + 2 * c] = acc[j][c].y;
+        }
       }
     }
     __syncthreads();
     if (phase == 0) {
       for (int ph = 1; ph < Tr::kPhases; ++ph) {
         const int w2 = ph * HK + h;
-        float m2[G], l2[G], a2[G][8];
+        float m2[G], l2[G];
+        float2 a2[G][4];
 #pragma unroll
         for (int j = 0; j < G; ++j) {
           const float* e = scr + ((w2 * G + j) * 16 + ln) * 10;
           m2[j] = e[0];
           l2[j] = e[1];
 #pragma unroll
-          for (int d = 0; d < 8; ++d) a2[j][d] = e[2 + d];
+          for (int c = 0; c < 4; ++c) a2[j][c] = make_float2(e[2 + 2 * c], e[3 + 2 * c]);
         }
         merge_state<G>(m, l, acc, m2, l2, a2);
       }
@@ -378,7 +415,10 @@ __global__ void __launch_bounds__(kDecodeThreads, (G <= 4 ? 2 : 1)) paged_decode
         const float inv = l[j] > 0.f ? vs / l[j] : 0.f;
         float o[8];
 #pragma unroll
-        for (int d = 0; d < 8; ++d) o[d] = acc[j][d] * inv;
+        for (int c = 0; c < 4; ++c) {
+          o[2 * c] = acc[j][c].x * inv;
+          o[2 * c + 1] = acc[j][c].y * inv;
+        }
         *reinterpret_cast<uint4*>(out_b + (h * G + j) * kHeadDim + 8 * ln) = pack_bf16x8(o);
       }
     }
@@ -392,8 +432,10 @@ __global__ void __launch_bounds__(kDecodeThreads, (G <= 4 ? 2 : 1)) paged_decode
       const int hq = h * G + j;
       const int64_t row = (int64_t(b) * p.max_splits + split) * kHq + hq;
       float* o = ws_o + row * kHeadDim + 8 * ln;
-      reinterpret_cast<float4*>(o)[0] = make_float4(acc[j][0] * vs, acc[j][1] * vs, acc[j][2] * vs, acc[j][3] * vs);
-      reinterpret_cast<float4*>(o)[1] = make_float4(acc[j][4] * vs, acc[j][5] * vs, acc[j][6] * vs, acc[j][7] * vs);
+      reinterpret_cast<float4*>(o)[0] =
+          make_float4(acc[j][0].x * vs, acc[j][0].y * vs, acc[j][1].x * vs, acc[j][1].y * vs);
+      reinterpret_cast<float4*>(o)[1] =
+          make_float4(acc[j][2].x * vs, acc[j][2].y * vs, acc[j][3].x * vs, acc[j][3].y * vs);
       if (ln == 0) ws_ml[row] = make_float2(m[j], l[j]);
     }
   }
