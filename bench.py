@@ -56,7 +56,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--profile", default="", choices=["", "decode-kernel", "decode-steps"],
+    ap.add_argument("--profile", default="", choices=["", "decode-kernel", "decode-steps", "prefill-kernel"],
                     help="run a short profiling case instead of the benchmark: the CUDA profiler range "
                          "(cudaProfilerStart/Stop, for ncu --profile-from-start off) covers --steps "
                          "launches of the decode kernel alone (decode-kernel) or --steps engine decode "
@@ -372,6 +372,55 @@ def run_profile(args):
         print(json.dumps({"profile": "decode-kernel", "launches": args.steps, "bytes_per_launch": nbytes,
                           "cache_gb": round(2 * kc.numel() * 2 / 1e9, 2), "us_per_launch": round(us, 2),
                           "gb_per_s": round(nbytes / us / 1e3, 1)}))
+        return
+    if args.profile == "prefill-kernel":
+        # BASELINE config-4 prefill shape: 8 sequences of 4096..8192 new tokens over a 2048-token
+        # cached prefix (paged), Hq 16 / Hk 8, causal; FLOPs = 4 * Hq * D * sum_i visible_keys(i).
+        hq, hk, d, bs = 16, 8, 128, 256
+        dev = torch.device("cuda", 0)
+        chunks = [int(x) for x in torch.randint(4096, 8193, (8,), generator=g)]
+        prefix = 2048
+        kl = [prefix + c for c in chunks]
+        nblk = [-(-n // bs) for n in kl]
+        perm = torch.randperm(sum(nblk), generator=g).tolist()
+        mb = max(nblk)
+        tables, off = [], 0
+        for n in nblk:
+            tables.append(perm[off:off + n] + [-1] * (mb - n))
+            off += n
+        kc = torch.randn(sum(nblk), bs, hk, d, device=dev, dtype=torch.bfloat16)
+        vc = torch.randn_like(kc)
+        tq = sum(chunks)
+        q = torch.randn(tq, hq, d, device=dev, dtype=torch.bfloat16)
+        cuq = torch.tensor([0] + list(__import__("itertools").accumulate(chunks)), dtype=torch.int32, device=dev)
+        cuk = torch.tensor([0] + list(__import__("itertools").accumulate(kl)), dtype=torch.int32, device=dev)
+        bt = torch.tensor(tables, dtype=torch.int32, device=dev)
+        flops = sum(4 * hq * d * (c * prefix + c * (c + 1) // 2) for c in chunks)
+        res = {"profile": "prefill-kernel", "tokens": tq, "gflop": round(flops / 1e9, 1)}
+        variants = {"tc_precise": lambda: kernels.varlen_prefill(q, kc, vc, cuq, cuk, max(chunks), max(kl), d ** -0.5,
+                                                                 block_table=bt, precise_p=True),
+                    "tc_bf16p": lambda: kernels.varlen_prefill(q, kc, vc, cuq, cuk, max(chunks), max(kl), d ** -0.5,
+                                                               block_table=bt, precise_p=False),
+                    "simt": lambda: kernels.varlen_prefill_simt(q, kc, vc, cuq, cuk, max(chunks), max(kl), d ** -0.5,
+                                                                block_table=bt)}
+        stream = torch.cuda.current_stream()
+        for name, fn in variants.items():
+            fn()
+            torch.cuda.synchronize()
+            reps = args.steps if name != "simt" else 1
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if name == "tc_precise":
+                torch.cuda.profiler.start()
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if name == "tc_precise":
+                torch.cuda.profiler.stop()
+            ms = e0.elapsed_time(e1) / reps
+            res[name] = {"ms": round(ms, 3), "tflops": round(flops / ms / 1e9, 1)}
+        print(json.dumps(res))
         return
     # decode-steps: the engine at the job's mid context (prompts of 576 tokens, 256 sequences).
     ctx = PROMPT_LEN + OUTPUT_LEN // 2

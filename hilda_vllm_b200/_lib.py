@@ -83,6 +83,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hl_varlen_prefill": (
         c_int,
         [
+            c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_int, c_int,
+            c_int, c_int, c_int, c_int, c_i64, c_f32, c_vp, c_i64, c_int, c_vp,
+        ],
+    ),
+    "hl_varlen_prefill_read_errors": (c_int, [c_vp]),
+    "hl_varlen_prefill_simt": (
+        c_int,
+        [
             c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_int,
             c_int, c_int, c_int, c_int, c_i64, c_f32, c_vp, c_i64, c_vp,
         ],

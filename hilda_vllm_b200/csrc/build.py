@@ -26,6 +26,7 @@ SOURCES = [
     "store_kv.cu",
     "paged_decode.cu",
     "varlen_prefill.cu",
+    "prefill_tc.cu",
     "pack_decode.cu",
     "layer_ops.cu",
 ]

@@ -1,4 +1,5 @@
-// Varlen causal prefill attention (CUDA-core path).
+// Varlen causal prefill attention on CUDA cores (hl_varlen_prefill_simt; the engine uses the
+// tensor-core kernel in prefill_tc.cu).
 //
 // Semantics (mini_vllm/layers/attention.py:120-131,149-160: flash_attn_varlen_func with
 // causal=True and, when a prefix is cached or the prompt is chunked, block_table set so K/V
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(kThreads) varlen_prefill_simt_kernel(const Pre
 
 using namespace hl;
 
-extern "C" int hl_varlen_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v,
+extern "C" int hl_varlen_prefill_simt(const void* q, int64_t q_row_stride, const void* k, const void* v,
                                  int64_t k_row_stride, int64_t v_row_stride, const int32_t* cu_seqlens_q,
                                  const int32_t* cu_seqlens_k, const int32_t* block_tables, int64_t bt_stride,
                                  int num_seqs, int max_seqlen_q, int max_seqlen_k, int num_q_heads,
@@ -210,26 +211,26 @@ extern "C" int hl_varlen_prefill(const void* q, int64_t q_row_stride, const void
                                  float softmax_scale, void* out, int64_t out_row_stride, void* stream) {
   clear_error();
   (void)max_seqlen_k;
-  HL_CHECK_ARG(num_seqs >= 0 && max_seqlen_q >= 0, "hl_varlen_prefill: negative size");
+  HL_CHECK_ARG(num_seqs >= 0 && max_seqlen_q >= 0, "hl_varlen_prefill_simt: negative size");
   if (num_seqs == 0 || max_seqlen_q == 0) return HL_OK;
-  HL_CHECK_ARG(q && k && v && cu_seqlens_q && cu_seqlens_k && out, "hl_varlen_prefill: null pointer");
-  HL_CHECK_ARG(head_dim == kD, "hl_varlen_prefill: head_dim %d != 128", head_dim);
-  HL_CHECK_ARG(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "hl_varlen_prefill: Hq %% Hk != 0");
-  HL_CHECK_ARG(num_seqs <= 65535 && num_q_heads <= 65535, "hl_varlen_prefill: grid too large");
+  HL_CHECK_ARG(q && k && v && cu_seqlens_q && cu_seqlens_k && out, "hl_varlen_prefill_simt: null pointer");
+  HL_CHECK_ARG(head_dim == kD, "hl_varlen_prefill_simt: head_dim %d != 128", head_dim);
+  HL_CHECK_ARG(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "hl_varlen_prefill_simt: Hq %% Hk != 0");
+  HL_CHECK_ARG(num_seqs <= 65535 && num_q_heads <= 65535, "hl_varlen_prefill_simt: grid too large");
   HL_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out) && q_row_stride % 8 == 0 &&
                    out_row_stride % 8 == 0,
-               "hl_varlen_prefill: q/k/v/out must be 16-byte aligned with row strides %% 8 == 0");
+               "hl_varlen_prefill_simt: q/k/v/out must be 16-byte aligned with row strides %% 8 == 0");
   PrefillParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.q_row_stride = q_row_stride;
   p.k = static_cast<const __nv_bfloat16*>(k);
   p.v = static_cast<const __nv_bfloat16*>(v);
   if (block_tables) {
-    HL_CHECK_ARG(block_size > 0 && bt_stride > 0, "hl_varlen_prefill: bad block table");
+    HL_CHECK_ARG(block_size > 0 && bt_stride > 0, "hl_varlen_prefill_simt: bad block table");
     p.k_row_stride = int64_t(num_kv_heads) * head_dim;
     p.v_row_stride = int64_t(num_kv_heads) * head_dim;
   } else {
-    HL_CHECK_ARG(k_row_stride % 8 == 0 && v_row_stride % 8 == 0, "hl_varlen_prefill: k/v row stride %% 8 != 0");
+    HL_CHECK_ARG(k_row_stride % 8 == 0 && v_row_stride % 8 == 0, "hl_varlen_prefill_simt: k/v row stride %% 8 != 0");
     p.k_row_stride = k_row_stride;
     p.v_row_stride = v_row_stride;
   }
@@ -246,6 +247,6 @@ extern "C" int hl_varlen_prefill(const void* q, int64_t q_row_stride, const void
   p.out_row_stride = out_row_stride;
   dim3 grid((max_seqlen_q + kRows - 1) / kRows, num_q_heads, num_seqs);
   varlen_prefill_simt_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  HL_CHECK_LAUNCH("hl_varlen_prefill");
+  HL_CHECK_LAUNCH("hl_varlen_prefill_simt");
   return HL_OK;
 }

@@ -264,12 +264,12 @@ class ModelRunner:
         shape = (2, hf.num_hidden_layers, config.num_kvcache_blocks, self.block_size, hk, d)
         layers = self.attention_layers()
         if self.use_fp8_kv_cache:
-            self.prefill_kv_cache = torch.empty(shape, dtype=torch.bfloat16)
-            self.decode_kv_cache = torch.empty(shape, dtype=torch.float8_e4m3fn)
+            self.prefill_kv_cache = torch.zeros(shape, dtype=torch.bfloat16)
+            self.decode_kv_cache = torch.zeros(shape, dtype=torch.float8_e4m3fn)
             self.kv_scales = torch.full((2, hf.num_hidden_layers, hk), float(config.kv_cache_scale),
                                         dtype=torch.float32)
         else:
-            self.kv_cache = torch.empty(shape, dtype=torch.bfloat16)
+            self.kv_cache = torch.zeros(shape, dtype=torch.bfloat16)
         for layer_id, module in enumerate(layers):
             module.kv_cache_dtype = config.kv_cache_dtype
             if self.use_fp8_kv_cache:

@@ -194,10 +194,11 @@ def decode_errors(workspace: torch.Tensor) -> int:
 
 
 # ------------------------------------------------------------------------ prefill attention
-def varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
-                   cu_seqlens_k: torch.Tensor, max_seqlen_q: int, max_seqlen_k: int, softmax_scale: float,
-                   block_table: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Causal varlen attention with a bottom-right-aligned mask.
+def varlen_prefill_simt(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                        cu_seqlens_k: torch.Tensor, max_seqlen_q: int, max_seqlen_k: int, softmax_scale: float,
+                        block_table: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal varlen attention with a bottom-right-aligned mask, on the CUDA-core kernel
+    (hl_varlen_prefill_simt; kept for comparison — the engine uses varlen_prefill).
 
     Same arguments as the reference's flash_attn_varlen_func call
     (mini_vllm/layers/attention.py:149-160): q [Tq, Hq, D]; with block_table, k/v are the paged
@@ -224,11 +225,55 @@ def varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens
     if num_seqs <= 0 or tq == 0:
         return out
     lib = _lib.load()
-    check(lib.hl_varlen_prefill(q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k_rs, v_rs,
+    check(lib.hl_varlen_prefill_simt(q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k_rs, v_rs,
                                 cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), bt_ptr, bt_stride, num_seqs,
                                 int(max_seqlen_q), int(max_seqlen_k), hq, hk, hd, bsz, nb, float(softmax_scale),
-                                out.data_ptr(), out.stride(0), _stream(q)), "hl_varlen_prefill")
+                                out.data_ptr(), out.stride(0), _stream(q)), "hl_varlen_prefill_simt")
     return out
+
+
+def varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                   cu_seqlens_k: torch.Tensor, max_seqlen_q: int, max_seqlen_k: int, softmax_scale: float,
+                   block_table: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                   precise_p: bool = True) -> torch.Tensor:
+    """Causal varlen attention with a bottom-right-aligned mask on the tcgen05/TMEM kernel.
+
+    Same arguments as the reference's flash_attn_varlen_func call
+    (mini_vllm/layers/attention.py:149-160): q [Tq, Hq, D]; with block_table, k/v are the paged
+    caches [NB, BS, Hk, D]; without, k/v are [Tk, Hk, D].  Returns [Tq, Hq, D] bf16.
+    precise_p feeds P to the P.V MMA as bf16 hi + lo terms (see hl_varlen_prefill)."""
+    _cuda(q, k, v, cu_seqlens_q, cu_seqlens_k, block_table, out)
+    tq, hq, hd = q.shape
+    assert q.stride(2) == 1 and q.stride(1) == hd
+    assert cu_seqlens_q.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32
+    num_seqs = cu_seqlens_q.numel() - 1
+    if block_table is not None:
+        nb, bsz, hk, _ = k.shape
+        assert k.is_contiguous() and v.is_contiguous()
+        assert block_table.dtype == torch.int32 and block_table.stride(1) == 1
+        bt_ptr, bt_stride, k_rs, v_rs, total_k = block_table.data_ptr(), block_table.stride(0), 0, 0, 0
+    else:
+        total_k, hk, _ = k.shape
+        assert k.stride(2) == 1 and k.stride(1) == hd and v.stride(2) == 1 and v.stride(1) == hd
+        nb, bsz = 0, 0
+        bt_ptr, bt_stride, k_rs, v_rs = None, 0, k.stride(0), v.stride(0)
+    if out is None:
+        out = torch.empty(tq, hq, hd, dtype=torch.bfloat16, device=q.device)
+    if num_seqs <= 0 or tq == 0:
+        return out
+    lib = _lib.load()
+    check(lib.hl_varlen_prefill(q.data_ptr(), q.stride(0), tq, k.data_ptr(), v.data_ptr(), k_rs, v_rs, total_k,
+                                   cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), bt_ptr, bt_stride, num_seqs,
+                                   int(max_seqlen_q), hq, hk, hd, bsz, nb, float(softmax_scale), out.data_ptr(),
+                                   out.stride(0), 1 if precise_p else 0, _stream(q)), "hl_varlen_prefill")
+    return out
+
+
+def prefill_errors() -> int:
+    """Error bits of the tensor-core prefill kernel (synchronous)."""
+    val = ctypes.c_int32(0)
+    check(_lib.load().hl_varlen_prefill_read_errors(ctypes.addressof(val)), "hl_varlen_prefill_read_errors")
+    return int(val.value)
 
 
 # ------------------------------------------------------------------------ decode packing

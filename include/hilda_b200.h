@@ -142,24 +142,45 @@ int hl_paged_decode_read_errors(const void* workspace, int32_t* errors_out, void
 
 /* ------------------------------------------------------------------------------------
  * Varlen causal prefill attention (bottom-right aligned causal mask), optionally reading
- * K/V (prefix + chunk) from the paged cache through block_tables.
+ * K/V (prefix + chunk) from the paged cache through block_tables, on the 5th-generation tensor
+ * cores: tcgen05.mma with TMEM accumulators, Q/K/V tiles brought in by TMA (3-D tensor maps,
+ * 128-byte swizzle), S and O resident in TMEM.
  * Replaces flash_attn_varlen_func(q, k|k_cache, v|v_cache, cu_seqlens_q, cu_seqlens_k,
  * max_seqlen_q, max_seqlen_k, softmax_scale, causal=True, block_table),
  * mini_vllm/layers/attention.py:120-131,149-160.
- *   q:   [Tq, Hq, D] bf16 (row stride q_row_stride), out [Tq, Hq, D] (row stride out_row_stride)
- *   paged (block_tables != NULL): k/v are the caches [num_blocks, block_size, Hk, D];
- *   contiguous (block_tables == NULL): k/v are [Tk, Hk, D] with row strides k_row_stride,
+ *   q:   [total_q, Hq, D] bf16 (row stride q_row_stride), out [total_q, Hq, D] (out_row_stride)
+ *   paged (block_tables != NULL): k/v are the caches [num_blocks, block_size, Hk, D],
+ *   block_size % 128 == 0;
+ *   contiguous (block_tables == NULL): k/v are [total_k, Hk, D] with row strides k_row_stride,
  *   v_row_stride, and sequence s's keys are rows cu_seqlens_k[s] .. cu_seqlens_k[s+1]-1.
- * Requires head_dim == 128 and Hq % Hk == 0.
+ * precise_p != 0 feeds the probabilities to the P.V product as two bf16 terms (hi + lo, ~16
+ * significant bits; one extra MMA group per tile) instead of one bf16-rounded term, which keeps
+ * outputs within an fp32 reference's rtol 2e-2 / atol 2e-3 where heavy cancellation defeats
+ * bf16 P (bf16 P alone is what flash-attn does).  Requires head_dim == 128 and Hq % Hk == 0.
  * ---------------------------------------------------------------------------------- */
-int hl_varlen_prefill(const void* q, int64_t q_row_stride,
+int hl_varlen_prefill(const void* q, int64_t q_row_stride, int64_t total_q,
                       const void* k, const void* v, int64_t k_row_stride, int64_t v_row_stride,
-                      const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                      int64_t total_k, const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
                       const int32_t* block_tables, int64_t bt_stride,
-                      int num_seqs, int max_seqlen_q, int max_seqlen_k,
+                      int num_seqs, int max_seqlen_q,
                       int num_q_heads, int num_kv_heads, int head_dim,
                       int block_size, int64_t num_blocks, float softmax_scale,
-                      void* out, int64_t out_row_stride, void* stream);
+                      void* out, int64_t out_row_stride, int precise_p, void* stream);
+
+/* Error bits of the tensor-core prefill kernel (bit 0: an mbarrier wait timed out).  Synchronous. */
+int hl_varlen_prefill_read_errors(int32_t* errors_out);
+
+/* The same prefill on CUDA cores (fp32 FMA, one CTA per 64 query rows x head x sequence):
+ * the small reference implementation kept for comparison; same semantics and arguments as
+ * hl_varlen_prefill minus total_q / total_k / precise_p. */
+int hl_varlen_prefill_simt(const void* q, int64_t q_row_stride,
+                           const void* k, const void* v, int64_t k_row_stride, int64_t v_row_stride,
+                           const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                           const int32_t* block_tables, int64_t bt_stride,
+                           int num_seqs, int max_seqlen_q, int max_seqlen_k,
+                           int num_q_heads, int num_kv_heads, int head_dim,
+                           int block_size, int64_t num_blocks, float softmax_scale,
+                           void* out, int64_t out_row_stride, void* stream);
 
 /* ------------------------------------------------------------------------------------
  * Decode-batch packing on the GPU.

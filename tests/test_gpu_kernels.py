@@ -226,7 +226,7 @@ def test_decode_fp8(hq, hk, scaled):
 
 # ----------------------------------------------------------------------------- prefill
 @pytest.mark.parametrize("hq,hk", [(16, 8), (32, 8), (8, 1)])
-def test_prefill_contiguous(hq, hk):
+def test_prefill_simt_contiguous(hq, hk):
     g = torch.Generator().manual_seed(11 + hq)
     lens = [1, 5, 64, 64, 130, 257, 31]
     cu = torch.tensor([0] + np.cumsum(lens).tolist(), dtype=torch.int32)
@@ -236,14 +236,15 @@ def test_prefill_contiguous(hq, hk):
     k = qkv[:, hq * 128:(hq + hk) * 128].view(t, hk, 128)
     v = qkv[:, (hq + hk) * 128:].view(t, hk, 128)
     qd = qkv.to(DEV)
-    out = kernels.varlen_prefill(qd[:, :hq * 128].view(t, hq, 128), qd[:, hq * 128:(hq + hk) * 128].view(t, hk, 128),
-                                 qd[:, (hq + hk) * 128:].view(t, hk, 128), cu.to(DEV), cu.to(DEV), max(lens),
-                                 max(lens), 128 ** -0.5)
+    out = kernels.varlen_prefill_simt(qd[:, :hq * 128].view(t, hq, 128),
+                                      qd[:, hq * 128:(hq + hk) * 128].view(t, hk, 128),
+                                      qd[:, (hq + hk) * 128:].view(t, hk, 128), cu.to(DEV), cu.to(DEV), max(lens),
+                                      max(lens), 128 ** -0.5)
     want = oattn.varlen_prefill(q, k, v, cu, cu, 128 ** -0.5)
-    assert_close(out, want, **BF16_TOL, what="prefill contiguous")
+    assert_close(out, want, **BF16_TOL, what="prefill contiguous (CUDA cores)")
 
 
-def test_prefill_paged_with_prefix_chunks():
+def test_prefill_simt_paged_with_prefix_chunks():
     """Chunked prefill over cached prefixes: queries are the chunk, keys = prefix + chunk
     from the paged cache (block_table set), bottom-right causal mask."""
     g = torch.Generator().manual_seed(12)
@@ -255,10 +256,10 @@ def test_prefill_paged_with_prefix_chunks():
     cuq = torch.tensor([0] + np.cumsum(chunks).tolist(), dtype=torch.int32)
     cuk = torch.tensor([0] + np.cumsum(kl).tolist(), dtype=torch.int32)
     q = torch.randn(int(cuq[-1]), hq, 128, generator=g).bfloat16()
-    out = kernels.varlen_prefill(q.to(DEV), k.to(DEV), v.to(DEV), cuq.to(DEV), cuk.to(DEV), max(chunks), max(kl),
-                                 128 ** -0.5, block_table=bt.to(DEV))
+    out = kernels.varlen_prefill_simt(q.to(DEV), k.to(DEV), v.to(DEV), cuq.to(DEV), cuk.to(DEV), max(chunks),
+                                      max(kl), 128 ** -0.5, block_table=bt.to(DEV))
     want = oattn.varlen_prefill(q, k, v, cuq, cuk, 128 ** -0.5, block_table=bt)
-    assert_close(out, want, **BF16_TOL, what="prefill paged")
+    assert_close(out, want, **BF16_TOL, what="prefill paged (CUDA cores)")
 
 
 # ----------------------------------------------------------------------------- packing
@@ -406,3 +407,46 @@ def test_oracle_and_kernels_agree_with_flash_attn_when_it_runs():
                   block_table=bt2.to(DEV))
     want2 = oattn.varlen_prefill(q2, k2, v2, cuq, cuk, 128 ** -0.5, block_table=bt2)
     assert_close(ref2, want2, **BF16_TOL, what="flash-attn varlen vs oracle")
+
+
+# ----------------------------------------------------------------------------- tcgen05 prefill
+@pytest.mark.parametrize("hq,hk,lens", [
+    (16, 8, [1, 5, 64, 64, 130, 257, 31]),
+    (16, 8, [128, 256, 1000]),
+    (32, 8, [300, 7]),
+    (8, 1, [513]),
+])
+def test_prefill_tensor_core_contiguous(hq, hk, lens):
+    g = torch.Generator().manual_seed(31 + hq + len(lens))
+    cu = torch.tensor([0] + np.cumsum(lens).tolist(), dtype=torch.int32)
+    t = int(cu[-1])
+    qkv = torch.randn(t, (hq + 2 * hk) * 128, generator=g).bfloat16()
+    q = qkv[:, :hq * 128].view(t, hq, 128)
+    k = qkv[:, hq * 128:(hq + hk) * 128].view(t, hk, 128)
+    v = qkv[:, (hq + hk) * 128:].view(t, hk, 128)
+    qd = qkv.to(DEV)
+    out = kernels.varlen_prefill(qd[:, :hq * 128].view(t, hq, 128), qd[:, hq * 128:(hq + hk) * 128].view(t, hk, 128),
+                                    qd[:, (hq + hk) * 128:].view(t, hk, 128), cu.to(DEV), cu.to(DEV), max(lens),
+                                    max(lens), 128 ** -0.5)
+    torch.cuda.synchronize()
+    assert kernels.prefill_errors() == 0
+    want = oattn.varlen_prefill(q, k, v, cu, cu, 128 ** -0.5)
+    assert_close(out, want, **BF16_TOL, what="tcgen05 prefill contiguous")
+
+
+def test_prefill_tensor_core_paged_with_prefix_chunks():
+    g = torch.Generator().manual_seed(41)
+    hq, hk, bs, nb = 16, 8, 256, 40
+    starts = [0, 256, 100, 512, 2048, 3]
+    chunks = [64, 128, 1, 300, 512, 700]
+    kl = [s + c for s, c in zip(starts, chunks)]
+    k, v, bt, _ = make_paged(g, len(kl), hk, 128, nb, bs, kl)
+    cuq = torch.tensor([0] + np.cumsum(chunks).tolist(), dtype=torch.int32)
+    cuk = torch.tensor([0] + np.cumsum(kl).tolist(), dtype=torch.int32)
+    q = torch.randn(int(cuq[-1]), hq, 128, generator=g).bfloat16()
+    out = kernels.varlen_prefill(q.to(DEV), k.to(DEV), v.to(DEV), cuq.to(DEV), cuk.to(DEV), max(chunks), max(kl),
+                                    128 ** -0.5, block_table=bt.to(DEV))
+    torch.cuda.synchronize()
+    assert kernels.prefill_errors() == 0
+    want = oattn.varlen_prefill(q, k, v, cuq, cuk, 128 ** -0.5, block_table=bt)
+    assert_close(out, want, **BF16_TOL, what="tcgen05 prefill paged")
