@@ -56,6 +56,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"],
+                    help="c2 (default, the headline): BASELINE configs[1]; c3: FP8 KV with a capped pool; "
+                         "c4: mixed chunked prefill + decode with shared prefixes; c5: Qwen3-8B (TP over --gpus)")
+    ap.add_argument("--kv", default="auto", choices=["auto", "fp8"], help="KV cache dtype for c5")
     ap.add_argument("--profile", default="", choices=["", "decode-kernel", "decode-steps", "prefill-kernel"],
                     help="run a short profiling case instead of the benchmark: the CUDA profiler range "
                          "(cudaProfilerStart/Stop, for ncu --profile-from-start off) covers --steps "
@@ -443,10 +447,127 @@ def run_profile(args):
     llm.exit()
 
 
+# ----------------------------------------------------------------------------- other workloads
+def _engine_e2e(args, model_dir, prompts, params, **llm_kwargs):
+    """One warm-up job, then the timed job, through LLM.generate; returns (line fields, llm)."""
+    import torch
+    import torch.distributed as dist
+
+    from hilda_vllm_b200 import LLM
+
+    world = args.gpus
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    llm = LLM(str(model_dir), load_format="random", seed=args.seed, tensor_parallel_size=world,
+              distributed_executor="external" if world > 1 else "spawn", **llm_kwargs)
+    if getattr(llm, "is_worker", False):
+        if dist.is_initialized():
+            dist.destroy_process_group()
+        return None, None
+    from hilda_vllm_b200.engine.scheduler import Scheduler
+
+    warm = [p[:64] for p in prompts[:8]]
+    llm.generate(warm, params[:8], use_tqdm=False)
+    llm.scheduler = Scheduler(llm.config)
+    llm.model_runner.call("reset_decode_state")
+    llm.model_runner.io_bytes = {"h2d": 0, "d2h": 0}
+    sampler = ClockSampler(local)
+    sampler.start()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    outs = llm.generate(prompts, params, use_tqdm=False)
+    wall = time.perf_counter() - t0
+    clocks = sampler.stop()
+    st = llm.last_generate_stats
+    n_out = sum(len(o["token_ids"]) for o in outs)
+    steps = st["decode_steps"] + 1
+    fields = {"e2e": {"value": round(n_out / wall, 1), "unit": "tok/s",
+                      "h2d_bytes_per_step": int(llm.model_runner.io_bytes["h2d"] / steps),
+                      "d2h_bytes_per_step": int(llm.model_runner.io_bytes["d2h"] / steps),
+                      "wall_s": round(wall, 3), "output_tokens": n_out,
+                      "prompt_tokens": st["prompt_tokens"], "prefill_tokens": st["prefill_tokens"],
+                      "prefill_s": round(st["prefill_time_s"], 3), "decode_s": round(st["decode_time_s"], 3),
+                      "prefill_tok_s": round(st["prefill_throughput_toks"], 1),
+                      "decode_tok_s": round(st["decode_throughput_toks"], 1),
+                      "decode_steps": st["decode_steps"], "avg_decode_active_bs": round(st["avg_decode_active_bs"], 2),
+                      "min_free_blocks": st["min_free_blocks_observed"], "kv_blocks": st["kv_num_blocks"],
+                      "prefill_blocked_steps": st["prefill_allocation_blocked_steps"]},
+              "clocks": clocks}
+    return fields, llm
+
+
+def run_workload(args):
+    """BASELINE configs 3, 4 and 5 through the public API (e2e); value = output tok/s."""
+    import torch
+
+    from hilda_vllm_b200 import SamplingParams
+
+    g = torch.Generator().manual_seed(args.seed)
+    vocab = 151936
+    if args.workload == "c3":
+        # FP8 e4m3 KV with per-head scales (unit scales, the reference-compatible setting), 256 seqs,
+        # prompts U[32,128], 512 greedy tokens, pool capped at 512 blocks (< 768 needed at the
+        # peak) so the scheduler preempts, re-prefills and compacts the decode batch.
+        prompts = [torch.randint(0, vocab, (int(torch.randint(32, 129, (1,), generator=g)),), generator=g).tolist()
+                   for _ in range(256)]
+        params = [SamplingParams(greedy=True, max_tokens=512, ignore_eos=True)] * 256
+        kw = dict(max_num_seqs=256, max_model_len=64 + 512 + 256 + 128, max_num_batched_tokens=16384,
+                  kv_cache_dtype="fp8", kvcache_block_cap=512, gpu_memory_utilization=0.85)
+        cfg, desc = CFG_DIR, "qwen3-0.6b FP8 KV, 256 seqs, prompt U[32,128], 512 greedy, pool capped at 512 blocks"
+    elif args.workload == "c4":
+        # 64 long prompts U[4096,8192] in 8 groups sharing a 2048-token prefix (max_tokens 1, as the
+        # reference's jitter benchmark), plus 128 decode sequences of prompt 64 / output 256; prefill
+        # chunk budget 8192; max_model_len = max_num_batched_tokens = 8448 (config.py:40).
+        prompts, params = [], []
+        for grp in range(8):
+            prefix = torch.randint(0, vocab, (2048,), generator=g).tolist()
+            for _ in range(8):
+                n = int(torch.randint(4096, 8193, (1,), generator=g))
+                prompts.append(prefix + torch.randint(0, vocab, (n - 2048,), generator=g).tolist())
+                params.append(SamplingParams(greedy=True, max_tokens=1, ignore_eos=True))
+        for _ in range(128):
+            prompts.append(torch.randint(0, vocab, (64,), generator=g).tolist())
+            params.append(SamplingParams(greedy=True, max_tokens=256, ignore_eos=True))
+        order = torch.randperm(len(prompts), generator=g).tolist()
+        prompts = [prompts[i] for i in order]
+        params = [params[i] for i in order]
+        kw = dict(max_num_seqs=256, max_model_len=8448, max_num_batched_tokens=8448, chunked_prefill_size=8192,
+                  gpu_memory_utilization=0.85)
+        cfg, desc = CFG_DIR, "qwen3-0.6b mixed: 64 x U[4096,8192] prompts (8 groups sharing 2048-token prefixes) + 128 x (64 -> 256)"
+    else:
+        # Qwen3-8B shape, 256 seqs, prompts U[256,1024], 512 greedy tokens, TP over --gpus.
+        prompts = [torch.randint(0, vocab, (int(torch.randint(256, 1025, (1,), generator=g)),), generator=g).tolist()
+                   for _ in range(256)]
+        params = [SamplingParams(greedy=True, max_tokens=512, ignore_eos=True)] * 256
+        kw = dict(max_num_seqs=256, max_model_len=1024 + 512 + 256, max_num_batched_tokens=16384,
+                  kv_cache_dtype=args.kv, gpu_memory_utilization=0.85)
+        cfg = ROOT / "hilda_vllm_b200" / "model_configs" / "qwen3-8b"
+        desc = f"qwen3-8b, 256 seqs, prompt U[256,1024], 512 greedy, {args.kv} KV, tp{args.gpus}"
+    fields, llm = _engine_e2e(args, cfg, prompts, params, **kw)
+    if fields is None:
+        return
+    e2e = fields["e2e"]
+    line = {"metric": f"{desc}: output tok/s", "value": e2e["value"], "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": 1, "warmup": 1, "ms_per_step": round(e2e["wall_s"] * 1e3, 1), "higher_is_better": True,
+            "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": {"workload": args.workload, "desc": desc,
+                                                             "parallelism": f"tp{args.gpus}"},
+            **fields}
+    print(json.dumps(line), flush=True)
+    llm.exit()
+
+
 def main():
     args = parse()
     if args.profile:
         run_profile(args)
+        return
+    if args.workload != "c2" and args.impl == "ours":
+        run_workload(args)
         return
     if args.impl == "reference":
         run_reference_arm(args)

@@ -287,15 +287,20 @@ class ModelRunner:
 
     @torch.inference_mode()
     def convert_prefill_to_decode_cache(self, seqs: list[Sequence]):
-        """FP8 mode: quantise the BF16 prefill-cache rows of every prompt token of `seqs` into
-        the FP8 decode cache, all layers in one launch (model_runner.py:483-502)."""
+        """FP8 mode: quantise the BF16 prefill-cache rows of every cached token of `seqs` into
+        the FP8 decode cache, all layers in one launch (model_runner.py:483-502).
+
+        Departure from the reference, on purpose: it copies positions [0, num_prompt_tokens)
+        (model_runner.py:488-491), which after a preemption misses the completion tokens that
+        the re-prefill recomputed into the BF16 cache; here every position whose KV the prefill
+        wrote, [0, num_computed_tokens), is copied (identical for sequences never preempted)."""
         if not self.use_fp8_kv_cache or not seqs:
             return
         bs = self.block_size
         slots = []
         for seq in seqs:
             table = np.asarray(seq.block_table, dtype=np.int64)
-            pos = np.arange(seq.num_prompt_tokens, dtype=np.int64)
+            pos = np.arange(seq.num_computed_tokens, dtype=np.int64)
             slots.append(table[pos // bs] * bs + pos % bs)
         slot_mapping = torch.from_numpy(np.concatenate(slots).astype(np.int32)).to(self.device, non_blocking=True)
         kernels.copy_kvcache_fp8_layers(self.prefill_kv_cache[0], self.prefill_kv_cache[1],
