@@ -85,7 +85,7 @@ class LLMEngine:
         seqs, is_prefill = self.scheduler.schedule()
         if not seqs:
             return [], False, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0
-        token_ids = self.model_runner.call("run", seqs, is_prefill)
+        token_ids = self.model_runner.run(seqs, is_prefill)
         self.last_step_diagnostics = {
             "running": len(self.scheduler.running),
             "waiting": len(self.scheduler.waiting),
@@ -96,7 +96,7 @@ class LLMEngine:
             ready = [s.seq for s in seqs if not s.is_padding and s.seq.is_prefill_done and not s.seq.is_finished
                      and not s.seq.decode_cache_ready]
             if ready:
-                self.model_runner.call("convert_prefill_to_decode_cache", ready)
+                self.model_runner.convert_prefill_to_decode_cache(ready)
                 for seq in ready:
                     seq.decode_cache_ready = True
         outputs = [(s.seq.seq_id, s.seq.completion_token_ids) for s in seqs if not s.is_padding and s.seq.is_finished]

@@ -49,6 +49,14 @@ def rpc_recv(group):
     return method, args
 
 
+def sampling_settings(seqs: list[Sequence]):
+    """None when every sequence samples greedily, else the per-row sampler inputs."""
+    if all(getattr(s, "greedy", False) for s in seqs):
+        return None
+    return ([s.temperature for s in seqs], [s.top_k for s in seqs], [s.top_p for s in seqs],
+            [bool(getattr(s, "greedy", False)) for s in seqs])
+
+
 def merge_shard_argmax(all_val: torch.Tensor, all_idx: torch.Tensor) -> torch.Tensor:
     """Global greedy token from per-shard (max value, global index) pairs, shards ordered by
     vocabulary range ([tp, n] each): the first shard holding the maximum wins, which is the
@@ -285,10 +293,10 @@ class ModelRunner:
                 module.k_cache = self.kv_cache[0, layer_id]
                 module.v_cache = self.kv_cache[1, layer_id]
 
-    @torch.inference_mode()
     def convert_prefill_to_decode_cache(self, seqs: list[Sequence]):
-        """FP8 mode: quantise the BF16 prefill-cache rows of every cached token of `seqs` into
-        the FP8 decode cache, all layers in one launch (model_runner.py:483-502).
+        """FP8 mode (rank 0): quantise the BF16 prefill-cache rows of every cached token of
+        `seqs` into the FP8 decode cache on all ranks, all layers in one launch
+        (model_runner.py:483-502).
 
         Departure from the reference, on purpose: it copies positions [0, num_prompt_tokens)
         (model_runner.py:488-491), which after a preemption misses the completion tokens that
@@ -302,7 +310,11 @@ class ModelRunner:
             table = np.asarray(seq.block_table, dtype=np.int64)
             pos = np.arange(seq.num_computed_tokens, dtype=np.int64)
             slots.append(table[pos // bs] * bs + pos % bs)
-        slot_mapping = torch.from_numpy(np.concatenate(slots).astype(np.int32)).to(self.device, non_blocking=True)
+        self.call("copy_to_decode_cache", np.concatenate(slots).astype(np.int32))
+
+    @torch.inference_mode()
+    def copy_to_decode_cache(self, slots: np.ndarray):
+        slot_mapping = torch.from_numpy(slots).pin_memory().to(self.device, non_blocking=True)
         kernels.copy_kvcache_fp8_layers(self.prefill_kv_cache[0], self.prefill_kv_cache[1],
                                         self.decode_kv_cache[0], self.decode_kv_cache[1], slot_mapping,
                                         self.kv_scales[0], self.kv_scales[1])
@@ -347,7 +359,9 @@ class ModelRunner:
     # ------------------------------------------------------------------ batch preparation
     def prepare_prefill(self, seqs: list[ScheduledSequence]):
         """Varlen metadata for the scheduled prefill chunks (model_runner.py:614-650)."""
-        meta = prefill_metadata(seqs, self.block_size)
+        return self._upload_prefill(prefill_metadata(seqs, self.block_size))
+
+    def _upload_prefill(self, meta: dict):
         dev = self.device
 
         def h2d(arr):
@@ -365,22 +379,6 @@ class ModelRunner:
         if self.enforce_eager or bs > MAX_GRAPH_BS:
             return bs
         return next(g for g in self.graph_bs if g >= bs)
-
-    @torch.inference_mode()
-    def prepare_decode(self, scheduled_seqs: list[ScheduledSequence]) -> int:
-        """Builds this step's packet on the host and copies it to the device; returns the
-        graph batch size.  The graph (or the eager path) then runs the pack kernel."""
-        bs = len(scheduled_seqs)
-        graph_bs = self._decode_graph_batch_size(bs)
-        nbytes = self.packer.build(scheduled_seqs, graph_bs)
-        self.packet_dev[:nbytes].copy_(self.packet_host[:nbytes], non_blocking=True)
-        self.io_bytes["h2d"] += nbytes
-        if self.recording is not None:
-            self.recording.append(self.packet_dev[:nbytes].clone())
-        active = sum(1 for s in scheduled_seqs if not s.is_padding)
-        self.last_decode_batch_info = {"scheduled_bs": bs, "graph_bs": graph_bs, "active_seqs": active,
-                                       "padded_slots": bs - active, "pack_events": self.packer.last_num_events}
-        return graph_bs
 
     def _set_decode_context(self, n: int):
         gv = self.graph_vars
@@ -425,28 +423,45 @@ class ModelRunner:
         if self.logits_buf is None or self.logits_buf.shape[0] < rows:
             self.logits_buf = torch.zeros(rows, vocab_local, dtype=torch.bfloat16, device=self.device)
 
-    def prepare_sample(self, seqs: list[Sequence]):
-        temps = torch.tensor([s.temperature for s in seqs], dtype=torch.float32).pin_memory()
-        ks = torch.tensor([s.top_k for s in seqs], dtype=torch.int32).pin_memory()
-        ps = torch.tensor([s.top_p for s in seqs], dtype=torch.float32).pin_memory()
-        return (temps.to(self.device, non_blocking=True), ks.to(self.device, non_blocking=True),
-                ps.to(self.device, non_blocking=True))
-
     # ------------------------------------------------------------------ running
+    # Rank 0 turns the scheduler's decision into small arrays — the prefill metadata, or the
+    # decode packet — plus the sampling settings, and only those cross to the other ranks
+    # (the reference pickles every scheduled Sequence to every rank each step,
+    # model_runner.py:117-124); every rank then executes the same step.
     @torch.inference_mode()
-    def run(self, scheduled_seqs: list[ScheduledSequence], is_prefill: bool) -> list[int | None] | None:
+    def run(self, scheduled_seqs: list[ScheduledSequence], is_prefill: bool) -> list[int | None]:
         if is_prefill:
-            return self._run_prefill(scheduled_seqs)
-        return self._run_decode(scheduled_seqs)
+            meta = prefill_metadata(scheduled_seqs, self.block_size)
+            rows = [i for i, s in enumerate(scheduled_seqs) if s.requires_sampling]
+            samp = sampling_settings([scheduled_seqs[i].seq for i in rows])
+            return self.call("execute_prefill", meta, len(scheduled_seqs), rows, samp)
+        bs = len(scheduled_seqs)
+        graph_bs = self._decode_graph_batch_size(bs)
+        nbytes = self.packer.build(scheduled_seqs, graph_bs)
+        real = [i for i, s in enumerate(scheduled_seqs) if not s.is_padding]
+        samp = sampling_settings([scheduled_seqs[i].seq for i in real])
+        self.last_decode_batch_info = {"scheduled_bs": bs, "graph_bs": graph_bs, "active_seqs": len(real),
+                                       "padded_slots": bs - len(real), "pack_events": self.packer.last_num_events}
+        packet = self.packet_host[:nbytes].numpy()
+        tokens = self.call("execute_decode", packet, bs, graph_bs,
+                           real, samp)
+        self.packer.note_sampled(bs, tokens)
+        out: list[int | None] = [None] * bs
+        for i in real:
+            out[i] = tokens[i]
+        return out
 
-    def _sample_rows(self, logits: torch.Tensor, seqs: list[Sequence]) -> list[int]:
-        if all(s.greedy for s in seqs):
+    def _sample_rows(self, logits: torch.Tensor, samp) -> list[int]:
+        if samp is None:
             return kernels.argmax(logits).tolist()
-        temps, ks, ps = self.prepare_sample(seqs)
-        sampled = self.sampler(logits, temps, ks, ps)
-        greedy_rows = [i for i, s in enumerate(seqs) if s.greedy]
+        temps, ks, ps, greedy = samp
+        dev = self.device
+        sampled = self.sampler(logits, torch.tensor(temps, dtype=torch.float32, device=dev),
+                               torch.tensor(ks, dtype=torch.int32, device=dev),
+                               torch.tensor(ps, dtype=torch.float32, device=dev))
+        greedy_rows = [i for i, g in enumerate(greedy) if g]
         if greedy_rows:
-            idx = torch.tensor(greedy_rows, device=self.device)
+            idx = torch.tensor(greedy_rows, device=dev)
             sampled[idx] = kernels.argmax(logits[idx].contiguous())
         return sampled.tolist()
 
@@ -457,32 +472,35 @@ class ModelRunner:
         dist.gather(logits, parts, 0)
         return torch.cat(parts, -1) if self.rank == 0 else None
 
-    def _run_prefill(self, scheduled_seqs):
-        seqs = [s.seq for s in scheduled_seqs]
-        input_ids, positions = self.prepare_prefill(scheduled_seqs)
+    @torch.inference_mode()
+    def execute_prefill(self, meta: dict, n_sched: int, rows: list[int], samp):
+        input_ids, positions = self._upload_prefill(meta)
         hidden = self.model(input_ids, positions)
         logits = self._gather_logits(self.model.lm_head.local_logits(hidden))
         token_ids = None
         if self.rank == 0:
-            token_ids = [None] * len(scheduled_seqs)
-            rows = [i for i, s in enumerate(scheduled_seqs) if s.requires_sampling]
+            token_ids = [None] * n_sched
             if rows:
                 sub = logits[rows] if len(rows) != logits.shape[0] else logits
-                sampled = self._sample_rows(sub.contiguous(), [seqs[i] for i in rows])
-                for i, t in zip(rows, sampled):
+                for i, t in zip(rows, self._sample_rows(sub.contiguous(), samp)):
                     token_ids[i] = t
         reset_context()
         return token_ids
 
-    def _run_decode(self, scheduled_seqs):
-        bs = len(scheduled_seqs)
-        graph_bs = self.prepare_decode(scheduled_seqs)
-        real = [i for i, s in enumerate(scheduled_seqs) if not s.is_padding]
-        real_seqs = [scheduled_seqs[i].seq for i in real]
-        greedy = all(s.greedy for s in real_seqs)
+    @torch.inference_mode()
+    def execute_decode(self, packet: np.ndarray, bs: int, graph_bs: int, real: list[int], samp):
+        nbytes = packet.nbytes
+        host = self.packet_host.numpy()
+        if packet.ctypes.data != host.ctypes.data:
+            host[:nbytes] = packet
+        self.packet_dev[:nbytes].copy_(self.packet_host[:nbytes], non_blocking=True)
+        self.io_bytes["h2d"] += nbytes
+        if self.recording is not None:
+            self.recording.append(self.packet_dev[:nbytes].clone())
         gv = self.graph_vars
-        if greedy:
-            # Tokens are picked on the device (in the graph when there is one) on every rank.
+        if samp is None:
+            # Greedy: tokens are picked on the device (inside the graph when there is one) on
+            # every rank, so nothing but the packet crossed the host.
             if graph_bs in self.graphs:
                 self.graphs[graph_bs].replay()
             else:
@@ -497,8 +515,7 @@ class ModelRunner:
                 logits = self._decode_body(graph_bs, greedy=False)
             logits = self._gather_logits(logits)
             if self.rank == 0 and real:
-                sub = logits[real].contiguous()
-                sampled = torch.tensor(self._sample_rows(sub, real_seqs), dtype=torch.int64)
+                sampled = torch.tensor(self._sample_rows(logits[real].contiguous(), samp), dtype=torch.int64)
                 toks = torch.zeros(bs, dtype=torch.int64)
                 toks[real] = sampled
                 gv["next_tokens"][:bs].copy_(toks.pin_memory(), non_blocking=True)
@@ -509,15 +526,8 @@ class ModelRunner:
         self.io_bytes["d2h"] += 8 * bs
         self.copy_done.record()
         self.copy_done.synchronize()
-        tokens = self.tokens_host[:bs].tolist()
-        self.packer.note_sampled(bs, tokens)
         reset_context()
-        if self.rank != 0:
-            return None
-        out = [None] * bs
-        for i in real:
-            out[i] = tokens[i]
-        return out
+        return self.tokens_host[:bs].tolist()
 
     @torch.inference_mode()
     def capture_cudagraph(self):

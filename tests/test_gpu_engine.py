@@ -96,6 +96,31 @@ def test_tiny_model_greedy_matches_oracle_graph_and_eager(tmp_path, golden_dir):
     assert checked == len(prompts) * (steps + 1) and exact >= 0.9 * checked
 
 
+def test_sampled_rows_low_temperature_match_oracle(tmp_path, golden_dir):
+    """Sampled decode (the host-side sampler path, graph replay for the logits) mixed with
+    greedy rows in one batch: at temperature 1e-3 the sampler must pick the oracle's argmax
+    (or a bf16 tie), and a temperature-1 request still yields in-vocabulary tokens."""
+    from transformers import AutoConfig
+
+    d = tiny_dir(tmp_path, golden_dir)
+    hf = AutoConfig.from_pretrained(d)
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, hf.vocab_size, (n,), generator=g).tolist() for n in (9, 70, 130, 3)]
+    steps = 24
+    llm = LLM(str(d), load_format="random", seed=7, max_num_seqs=8, max_model_len=1024,
+              max_num_batched_tokens=4096, kvcache_block_cap=64, gpu_memory_utilization=0.5)
+    sps = [SamplingParams(temperature=1e-3, max_tokens=steps + 1, ignore_eos=True),
+           SamplingParams(greedy=True, max_tokens=steps + 1, ignore_eos=True),
+           SamplingParams(temperature=1e-3, top_k=5, top_p=0.9, max_tokens=steps + 1, ignore_eos=True),
+           SamplingParams(greedy=True, max_tokens=steps + 1, ignore_eos=True)]
+    outs = llm.generate(prompts, sps, use_tqdm=False)
+    hot = llm.generate([prompts[0]], SamplingParams(temperature=1.0, max_tokens=16, ignore_eos=True), use_tqdm=False)
+    llm.exit()
+    assert all(0 <= t < hf.vocab_size for t in hot[0]["token_ids"]) and len(hot[0]["token_ids"]) == 16
+    checked, exact, ties = check_against_oracle(hf, 7, prompts, [o["token_ids"] for o in outs])
+    assert checked == len(prompts) * (steps + 1) and exact >= 0.9 * checked
+
+
 def test_qwen3_0_6b_greedy_32_steps_matches_oracle():
     from transformers import AutoConfig
 
@@ -144,7 +169,13 @@ def test_tensor_parallel_2_matches_oracle(tmp_path, golden_dir):
               max_num_batched_tokens=16384, kvcache_block_cap=128, gpu_memory_utilization=0.5,
               tensor_parallel_size=2)
     outs = llm.generate(prompts, SamplingParams(greedy=True, max_tokens=steps + 1, ignore_eos=True), use_tqdm=False)
+    # Sampled rows: logits gathered to rank 0, tokens broadcast back to the other rank.
+    cold = llm.generate(prompts[:2], SamplingParams(temperature=1e-3, max_tokens=8, ignore_eos=True), use_tqdm=False)
     llm.exit()
+    for c, o in zip(cold, outs):
+        assert len(c["token_ids"]) == 8 and all(0 <= t < hf.vocab_size for t in c["token_ids"])
+    checked, exact, ties = check_against_oracle(hf, 0, prompts[:2], [c["token_ids"] for c in cold])
+    assert exact >= 0.9 * checked
     checked, exact, ties = check_against_oracle(hf, 0, prompts, [o["token_ids"] for o in outs])
     print(f"TP=2 greedy: {exact}/{checked} exact argmax matches, {len(ties)} bf16 ties")
     assert checked == len(prompts) * (steps + 1) and exact >= 0.9 * checked
