@@ -101,6 +101,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "hl_rmsnorm": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_f32, c_vp]),
     "hl_qk_norm_rope": (c_int, [c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_f32, c_vp]),
+    "hl_qk_norm_rope_store": (c_int, [c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_f32, c_vp,
+                                      c_vp, c_int, c_vp, c_i64, c_vp, c_vp, c_vp]),
     "hl_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_vp]),
     "hl_argmax": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp]),
     "hl_argmax_shard": (c_int, [c_vp, c_i64, c_int, c_int, c_i64, c_vp, c_vp, c_vp]),

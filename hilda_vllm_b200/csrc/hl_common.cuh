@@ -127,4 +127,18 @@ __device__ __forceinline__ uint8_t float_to_e4m3_sat(float x) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
 }
 
+// 8 bf16 (one 16-byte vector) -> 8 e4m3 bytes (one 8-byte store), all divided by `scale`.
+// IEEE division (not a reciprocal multiply) so the bytes match x / scale exactly.
+__device__ __forceinline__ uint2 quant8_e4m3(uint4 v, float scale) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t out[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t qa = float_to_e4m3_sat(__fdiv_rn(bf16lo(w[i]), scale));
+    const uint32_t qb = float_to_e4m3_sat(__fdiv_rn(bf16hi(w[i]), scale));
+    out[i >> 1] |= (qa | (qb << 8)) << ((i & 1) * 16);
+  }
+  return make_uint2(out[0], out[1]);
+}
+
 }  // namespace hl

@@ -87,11 +87,25 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat
 // qkv rows: qkv[t] = [q (Hq*128) | k (Hk*128) | v (Hk*128)].  One half-warp per (token,
 // head); lane ln owns dims [8ln, 8ln+8) and its RoPE partner dims live in lane ln ^ 8.
 // cos_sin[pos] = [cos(pos*f_0..63) | sin(pos*f_0..63)] fp32 (the reference's cos_sin_cache).
+//
+// KV != kNoStore also fuses the KV-cache store (store_kvcache, mini_vllm/layers/attention.py:
+// 59-90, and its FP8 twin): the (token, head) space then covers the v heads too, and for a
+// token whose slot is in range the post-RoPE k head and the v head are written to row `slot`
+// of the paged cache, as bf16 bytes (kStoreBf16) or as e4m3 of x / scale[h] (kStoreFp8) —
+// the same bytes the separate store kernels write from the rotated qkv rows.
+constexpr int kNoStore = 0;
+constexpr int kStoreBf16 = 1;
+constexpr int kStoreFp8 = 2;
+
+template <int KV>
 __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row_stride, int num_tokens,
                                     int num_q_heads, int num_kv_heads, const __nv_bfloat16* __restrict__ qw,
                                     const __nv_bfloat16* __restrict__ kw, const float* __restrict__ cos_sin,
-                                    const int64_t* __restrict__ positions, float eps) {
-  const int heads = num_q_heads + num_kv_heads;
+                                    const int64_t* __restrict__ positions, float eps, void* __restrict__ k_cache,
+                                    void* __restrict__ v_cache, const int32_t* __restrict__ slot_mapping,
+                                    int64_t num_slots, const float* __restrict__ k_scale,
+                                    const float* __restrict__ v_scale) {
+  const int heads = num_q_heads + (KV == kNoStore ? 1 : 2) * num_kv_heads;
   const int64_t gid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;  // (token, head) index
   const int ln = threadIdx.x & 15;
   const bool active = gid < int64_t(num_tokens) * heads;
@@ -99,6 +113,24 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row
   const int hh = active ? int(gid % heads) : 0;
   const bool is_q = hh < num_q_heads;
   __nv_bfloat16* x = qkv + tok * row_stride + int64_t(hh) * 128 + 8 * ln;
+  const int row_elems = num_kv_heads * 128;
+  if constexpr (KV != kNoStore) {
+    // v heads: a copy into the cache; the half-warp is uniform in hh, so it leaves together.
+    if (hh >= num_q_heads + num_kv_heads) {
+      if (!active) return;
+      const int64_t slot = slot_mapping[tok];
+      if (slot < 0 || slot >= num_slots) return;
+      const int hv = hh - num_q_heads - num_kv_heads;
+      const uint4 a = *reinterpret_cast<const uint4*>(x);
+      const int64_t off = slot * row_elems + hv * 128 + 8 * ln;
+      if constexpr (KV == kStoreBf16) {
+        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(v_cache) + off) = a;
+      } else {
+        *reinterpret_cast<uint2*>(static_cast<uint8_t*>(v_cache) + off) = quant8_e4m3(a, v_scale ? v_scale[hv] : 1.f);
+      }
+      return;
+    }
+  }
   float v[8];
   {
     const uint4 a = active ? *reinterpret_cast<const uint4*>(x) : make_uint4(0, 0, 0, 0);
@@ -150,7 +182,22 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row
     __nv_bfloat162 h2 = __floats2bfloat162_rn(r[0], r[1]);
     o[t] = *reinterpret_cast<uint32_t*>(&h2);
   }
-  *reinterpret_cast<uint4*>(x) = make_uint4(o[0], o[1], o[2], o[3]);
+  const uint4 rot = make_uint4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<uint4*>(x) = rot;
+  if constexpr (KV != kNoStore) {
+    if (!is_q) {
+      const int64_t slot = slot_mapping[tok];
+      if (slot >= 0 && slot < num_slots) {
+        const int hk = hh - num_q_heads;
+        const int64_t off = slot * row_elems + hk * 128 + 8 * ln;
+        if constexpr (KV == kStoreBf16) {
+          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(k_cache) + off) = rot;
+        } else {
+          *reinterpret_cast<uint2*>(static_cast<uint8_t*>(k_cache) + off) = quant8_e4m3(rot, k_scale ? k_scale[hk] : 1.f);
+        }
+      }
+    }
+  }
 }
 
 // out[t, i] = bf16(bf16(silu(x[t, i])) * y[t, i]) with x = in[t, :I], y = in[t, I:2I].
@@ -279,18 +326,50 @@ extern "C" int hl_rmsnorm(const void* in, int64_t in_stride, void* residual, con
 extern "C" int hl_qk_norm_rope(void* qkv, int64_t row_stride, int num_tokens, int num_q_heads, int num_kv_heads,
                                int head_dim, const void* q_weight, const void* k_weight, const float* cos_sin,
                                const int64_t* positions, float eps, void* stream) {
+  return hl_qk_norm_rope_store(qkv, row_stride, num_tokens, num_q_heads, num_kv_heads, head_dim, q_weight, k_weight,
+                               cos_sin, positions, eps, nullptr, nullptr, 0, nullptr, 0, nullptr, nullptr, stream);
+}
+
+extern "C" int hl_qk_norm_rope_store(void* qkv, int64_t row_stride, int num_tokens, int num_q_heads,
+                                     int num_kv_heads, int head_dim, const void* q_weight, const void* k_weight,
+                                     const float* cos_sin, const int64_t* positions, float eps, void* k_cache,
+                                     void* v_cache, int kv_dtype, const int32_t* slot_mapping, int64_t num_slots,
+                                     const float* k_scale, const float* v_scale, void* stream) {
   clear_error();
   if (num_tokens == 0) return HL_OK;
   HL_CHECK_ARG(qkv && q_weight && k_weight && cos_sin && positions && num_tokens > 0, "hl_qk_norm_rope: bad args");
   HL_CHECK_ARG(head_dim == 128, "hl_qk_norm_rope: head_dim must be 128");
   HL_CHECK_ARG(aligned16(qkv) && row_stride % 8 == 0, "hl_qk_norm_rope: 16-byte alignment required");
-  const int64_t groups = int64_t(num_tokens) * (num_q_heads + num_kv_heads);
+  const bool store = k_cache != nullptr;
+  if (store) {
+    HL_CHECK_ARG(v_cache && slot_mapping && num_slots > 0, "hl_qk_norm_rope_store: cache arguments missing");
+    HL_CHECK_ARG(kv_dtype == HL_KV_BF16 || kv_dtype == HL_KV_FP8_E4M3, "hl_qk_norm_rope_store: bad kv_dtype");
+    HL_CHECK_ARG(aligned16(k_cache) && aligned16(v_cache), "hl_qk_norm_rope_store: 16-byte aligned caches required");
+  } else {
+    HL_CHECK_ARG(!v_cache, "hl_qk_norm_rope_store: v_cache without k_cache");
+  }
+  const int heads = num_q_heads + (store ? 2 : 1) * num_kv_heads;
+  const int64_t groups = int64_t(num_tokens) * heads;
   const int threads = 256;
   const int64_t blocks = (groups * 16 + threads - 1) / threads;
   HL_CHECK_ARG(blocks < (1ll << 31), "hl_qk_norm_rope: grid too large");
-  qk_norm_rope_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      (__nv_bfloat16*)qkv, row_stride, num_tokens, num_q_heads, num_kv_heads, (const __nv_bfloat16*)q_weight,
-      (const __nv_bfloat16*)k_weight, cos_sin, positions, eps);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto q = (__nv_bfloat16*)qkv;
+  auto qwt = (const __nv_bfloat16*)q_weight;
+  auto kwt = (const __nv_bfloat16*)k_weight;
+  if (!store) {
+    qk_norm_rope_kernel<kNoStore><<<(unsigned)blocks, threads, 0, s>>>(
+        q, row_stride, num_tokens, num_q_heads, num_kv_heads, qwt, kwt, cos_sin, positions, eps, nullptr, nullptr,
+        nullptr, 0, nullptr, nullptr);
+  } else if (kv_dtype == HL_KV_BF16) {
+    qk_norm_rope_kernel<kStoreBf16><<<(unsigned)blocks, threads, 0, s>>>(
+        q, row_stride, num_tokens, num_q_heads, num_kv_heads, qwt, kwt, cos_sin, positions, eps, k_cache, v_cache,
+        slot_mapping, num_slots, nullptr, nullptr);
+  } else {
+    qk_norm_rope_kernel<kStoreFp8><<<(unsigned)blocks, threads, 0, s>>>(
+        q, row_stride, num_tokens, num_q_heads, num_kv_heads, qwt, kwt, cos_sin, positions, eps, k_cache, v_cache,
+        slot_mapping, num_slots, k_scale, v_scale);
+  }
   HL_CHECK_LAUNCH("hl_qk_norm_rope");
   return HL_OK;
 }

@@ -54,22 +54,6 @@ __global__ void __launch_bounds__(kStoreThreads) store_kv_bf16_scalar(
 }
 
 // ------------------------------------------------------------------ FP8 quantisation
-// 8 bf16 (one 16-byte vector) -> 8 e4m3 bytes (one 8-byte store), all in head h.
-__device__ __forceinline__ uint2 quant8(uint4 v, float scale) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  uint32_t out[2] = {0u, 0u};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    // IEEE division (not a reciprocal multiply) so the bytes match x / scale exactly.
-    const float a = __fdiv_rn(bf16lo(w[i]), scale);
-    const float b = __fdiv_rn(bf16hi(w[i]), scale);
-    const uint32_t qa = float_to_e4m3_sat(a);
-    const uint32_t qb = float_to_e4m3_sat(b);
-    out[i >> 1] |= (qa | (qb << 8)) << ((i & 1) * 16);
-  }
-  return make_uint2(out[0], out[1]);
-}
-
 __global__ void __launch_bounds__(kStoreThreads) store_kv_fp8_vec(
     const __nv_bfloat16* __restrict__ key, const __nv_bfloat16* __restrict__ value, int64_t key_stride,
     int64_t value_stride, uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
@@ -87,8 +71,8 @@ __global__ void __launch_bounds__(kStoreThreads) store_kv_fp8_vec(
     const int h = (i * 8) / head_dim;
     const float sk = k_scale ? k_scale[h] : 1.0f;
     const float sv = v_scale ? v_scale[h] : 1.0f;
-    kd[i] = quant8(__ldg(ks + i), sk);
-    vd[i] = quant8(__ldg(vs + i), sv);
+    kd[i] = quant8_e4m3(__ldg(ks + i), sk);
+    vd[i] = quant8_e4m3(__ldg(vs + i), sv);
   }
 }
 
@@ -131,8 +115,8 @@ __global__ void __launch_bounds__(kStoreThreads) copy_kv_bf16_to_fp8_kernel(
   const float* vsc = v_scale ? v_scale + layer * scale_layer_stride : nullptr;
   for (int i = threadIdx.x; i < nvec; i += kStoreThreads) {
     const int h = (i * 8) / head_dim;
-    kd[i] = quant8(__ldg(ks + i), ksc ? ksc[h] : 1.0f);
-    vd[i] = quant8(__ldg(vs + i), vsc ? vsc[h] : 1.0f);
+    kd[i] = quant8_e4m3(__ldg(ks + i), ksc ? ksc[h] : 1.0f);
+    vd[i] = quant8_e4m3(__ldg(vs + i), vsc ? vsc[h] : 1.0f);
   }
 }
 

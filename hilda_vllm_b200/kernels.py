@@ -332,6 +332,35 @@ def qk_norm_rope(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, head_di
                               float(eps), _stream(qkv)), "hl_qk_norm_rope")
 
 
+def qk_norm_rope_store(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                       q_weight: torch.Tensor, k_weight: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Tensor,
+                       eps: float, k_cache: torch.Tensor, v_cache: torch.Tensor, slot_mapping: torch.Tensor,
+                       k_scale: torch.Tensor | None = None, v_scale: torch.Tensor | None = None) -> None:
+    """qk_norm_rope plus the KV-cache store of the rotated k heads and the v heads, in one
+    launch.  Caches are [NB, BS, Hk, D] bf16 (store_kvcache) or float8_e4m3fn (the FP8 store,
+    per-head scales optional); slot -1 skips a token."""
+    _cuda(qkv, q_weight, k_weight, cos_sin, positions, k_cache, v_cache, slot_mapping, k_scale, v_scale)
+    assert qkv.stride(1) == 1 and cos_sin.dtype == torch.float32 and cos_sin.is_contiguous()
+    assert positions.dtype == torch.int64 and positions.is_contiguous()
+    assert slot_mapping.dtype == torch.int32 and slot_mapping.is_contiguous() and slot_mapping.numel() >= qkv.shape[0]
+    assert k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.shape == v_cache.shape
+    assert k_cache.dtype == v_cache.dtype and k_cache.shape[-2:] == (num_kv_heads, head_dim)
+    if k_cache.dtype == torch.bfloat16:
+        kv_dtype = 0
+    else:
+        assert k_cache.dtype == torch.float8_e4m3fn
+        kv_dtype = 1
+    for sc in (k_scale, v_scale):
+        assert sc is None or (sc.dtype == torch.float32 and sc.is_contiguous() and sc.numel() == num_kv_heads)
+    num_slots = k_cache.numel() // (num_kv_heads * head_dim)
+    lib = _lib.load()
+    check(lib.hl_qk_norm_rope_store(qkv.data_ptr(), qkv.stride(0), qkv.shape[0], num_q_heads, num_kv_heads, head_dim,
+                                    q_weight.data_ptr(), k_weight.data_ptr(), cos_sin.data_ptr(), positions.data_ptr(),
+                                    float(eps), k_cache.data_ptr(), v_cache.data_ptr(), kv_dtype,
+                                    slot_mapping.data_ptr(), num_slots, _p(k_scale), _p(v_scale), _stream(qkv)),
+          "hl_qk_norm_rope_store")
+
+
 def silu_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     _cuda(x, out)
     rows, two_i = x.shape

@@ -45,6 +45,32 @@ class Attention(nn.Module):
         self.v_scale: torch.Tensor | None = None
         self.decode_workspace: torch.Tensor | None = None
 
+    def _store_target(self, context):
+        """(k_cache, v_cache, k_scale, v_scale) this step's new K/V go to, or None before the
+        KV pool exists (the reference's forward skips the store then, attention.py:146)."""
+        if self.kv_cache_dtype == "fp8" and self.prefill_k_cache.numel() and self.decode_k_cache.numel():
+            if context.is_prefill:
+                return self.prefill_k_cache, self.prefill_v_cache, None, None
+            return self.decode_k_cache, self.decode_v_cache, self.k_scale, self.v_scale
+        if self.k_cache.numel() and self.v_cache.numel():
+            return self.k_cache, self.v_cache, None, None
+        return None
+
+    def rotate_and_store(self, qkv, q_weight, k_weight, cos_sin, positions, eps) -> bool:
+        """The attention prologue in one launch: QK-RMSNorm + RoPE in place on the qkv rows
+        (mini_vllm/models/qwen3.py:82-85) fused with the KV-cache store that forward() would
+        do.  Returns True when the store happened, so the caller passes kv_stored=True."""
+        context = get_context()
+        target = self._store_target(context)
+        if target is None or context.slot_mapping is None:
+            kernels.qk_norm_rope(qkv, self.num_heads, self.num_kv_heads, self.head_dim, q_weight, k_weight, cos_sin,
+                                 positions, eps)
+            return False
+        k_cache, v_cache, k_scale, v_scale = target
+        kernels.qk_norm_rope_store(qkv, self.num_heads, self.num_kv_heads, self.head_dim, q_weight, k_weight, cos_sin,
+                                   positions, eps, k_cache, v_cache, context.slot_mapping, k_scale, v_scale)
+        return True
+
     def _prefill(self, q, k, v, k_cache, v_cache, context):
         if context.block_tables is not None:
             k, v = k_cache, v_cache
@@ -56,18 +82,21 @@ class Attention(nn.Module):
                                    workspace=self.decode_workspace, k_scale=k_scale, v_scale=v_scale)
         return out.unsqueeze(1)
 
-    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_stored: bool = False):
+        """kv_stored=True: rotate_and_store already wrote k/v into the cache this step."""
         context = get_context()
         if self.kv_cache_dtype == "fp8" and self.prefill_k_cache.numel() and self.decode_k_cache.numel():
             if context.is_prefill:
-                store_kvcache(k, v, self.prefill_k_cache, self.prefill_v_cache, context.slot_mapping)
+                if not kv_stored:
+                    store_kvcache(k, v, self.prefill_k_cache, self.prefill_v_cache, context.slot_mapping)
                 return self._prefill(q, k, v, self.prefill_k_cache, self.prefill_v_cache, context)
-            store_kvcache_fp8(k, v, self.decode_k_cache, self.decode_v_cache, context.slot_mapping,
-                              self.k_scale, self.v_scale)
+            if not kv_stored:
+                store_kvcache_fp8(k, v, self.decode_k_cache, self.decode_v_cache, context.slot_mapping,
+                                  self.k_scale, self.v_scale)
             return self._decode(q, self.decode_k_cache, self.decode_v_cache, context, self.k_scale, self.v_scale)
 
         k_cache, v_cache = self.k_cache, self.v_cache
-        if k_cache.numel() and v_cache.numel():
+        if k_cache.numel() and v_cache.numel() and not kv_stored:
             store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
         if context.is_prefill:
             return self._prefill(q, k, v, k_cache, v_cache, context)

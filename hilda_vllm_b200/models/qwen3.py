@@ -2,14 +2,13 @@
 
 Module names and parameter names match the reference (and Hugging Face checkpoints), so the
 reference's weight loader mapping works unchanged.  Per layer of a decode step the GPU runs:
-add+RMSNorm, qkv GEMM, fused QK-RMSNorm+RoPE (in place on the qkv rows), KV store + paged
+add+RMSNorm, qkv GEMM, fused QK-RMSNorm+RoPE+KV store (in place on the qkv rows), paged
 decode attention, o_proj GEMM (+ all-reduce under TP), add+RMSNorm, gate_up GEMM, SiLU*mul,
 down GEMM (+ all-reduce).
 """
 import torch
 from torch import nn
 
-from hilda_vllm_b200 import kernels
 from hilda_vllm_b200.layers.activation import SiluAndMul
 from hilda_vllm_b200.layers.attention import Attention
 from hilda_vllm_b200.layers.embed_head import ParallelLMHead, VocabParallelEmbedding
@@ -48,13 +47,13 @@ class Qwen3Attention(nn.Module):
 
     def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
         qkv = self.qkv_proj(hidden_states)
-        kernels.qk_norm_rope(qkv, self.num_heads, self.num_kv_heads, self.head_dim, self.q_norm.weight,
-                             self.k_norm.weight, self.rotary_emb.cos_sin_cache, positions, self.rms_norm_eps)
+        stored = self.attn.rotate_and_store(qkv, self.q_norm.weight, self.k_norm.weight,
+                                            self.rotary_emb.cos_sin_cache, positions, self.rms_norm_eps)
         q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
         q = q.view(-1, self.num_heads, self.head_dim)
         k = k.view(-1, self.num_kv_heads, self.head_dim)
         v = v.view(-1, self.num_kv_heads, self.head_dim)
-        o = self.attn(q, k, v)
+        o = self.attn(q, k, v, kv_stored=stored)
         return self.o_proj(o.flatten(1, -1))
 
 

@@ -258,6 +258,19 @@ int hl_qk_norm_rope(void* qkv, int64_t row_stride, int num_tokens, int num_q_hea
                     int head_dim, const void* q_weight, const void* k_weight, const float* cos_sin,
                     const int64_t* positions, float eps, void* stream);
 
+/* hl_qk_norm_rope fused with the KV-cache store: after rotating row t in place, writes the
+ * post-RoPE k heads and the v heads of row t to row slot_mapping[t] of k_cache / v_cache
+ * ([num_slots, Hk*D], kv_dtype HL_KV_BF16 or HL_KV_FP8_E4M3 with optional per-head scales),
+ * skipping slots outside [0, num_slots).  Replaces the qwen3.py:82-85 prologue plus the
+ * store_kvcache / store_kvcache_fp8 calls at mini_vllm/layers/attention.py:133,146 in one
+ * launch; the cache bytes equal those of hl_store_kv_bf16 / hl_store_kv_fp8 applied to the
+ * rotated rows.  k_cache = v_cache = NULL makes it exactly hl_qk_norm_rope. */
+int hl_qk_norm_rope_store(void* qkv, int64_t row_stride, int num_tokens, int num_q_heads, int num_kv_heads,
+                          int head_dim, const void* q_weight, const void* k_weight, const float* cos_sin,
+                          const int64_t* positions, float eps, void* k_cache, void* v_cache, int kv_dtype,
+                          const int32_t* slot_mapping, int64_t num_slots, const float* k_scale,
+                          const float* v_scale, void* stream);
+
 /* out = silu(in[:, :I]) * in[:, I:2I]  (SiluAndMul, mini_vllm/layers/activation.py:12-16). */
 int hl_silu_mul(const void* in, int64_t in_stride, void* out, int64_t out_stride, int rows,
                 int intermediate, void* stream);

@@ -348,6 +348,50 @@ def test_qk_norm_rope_matches_reference_modules(golden_dir):
     assert torch.all(qkv[:, 3 * 128:] == 0)  # v untouched
 
 
+@pytest.mark.parametrize("kv,hq,hk,n", [("bf16", 16, 8, 300), ("fp8", 16, 8, 257), ("fp8s", 8, 2, 64),
+                                        ("bf16", 4, 1, 1)])
+def test_fused_rope_store_equals_rope_then_store(kv, hq, hk, n):
+    """hl_qk_norm_rope_store == hl_qk_norm_rope followed by the store kernel, byte for byte, in
+    the qkv rows and in both caches (strided rows, skipped slots, untouched cache rows)."""
+    from hilda_vllm_b200.layers.rotary_embedding import RotaryEmbedding
+    g = torch.Generator().manual_seed(n + hq)
+    d, nb, bs = 128, 8, 256
+    width = (hq + 2 * hk) * d
+    qkv = (torch.randn(n, width, generator=g) * 2).bfloat16()
+    qw = (torch.rand(d, generator=g) + 0.5).bfloat16().to(DEV)
+    kw = (torch.rand(d, generator=g) + 0.5).bfloat16().to(DEV)
+    pos = torch.randint(0, 4000, (n,), generator=g).to(DEV)
+    slots = torch.randperm(nb * bs, generator=g)[:n].to(torch.int32)
+    slots[::5] = -1
+    slots = slots.to(DEV)
+    cos_sin = RotaryEmbedding(d, d, 4096, 1000000.0).cos_sin_cache.to(DEV).contiguous()
+    fp8 = kv != "bf16"
+    ks = (torch.rand(hk, generator=g) + 0.3).to(DEV) if kv == "fp8s" else None
+    vs = (torch.rand(hk, generator=g) + 0.3).to(DEV) if kv == "fp8s" else None
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    init = torch.randn(nb, bs, hk, d, generator=g).to(dt)
+    caches = [[init.clone().to(DEV), init.clone().to(DEV)] for _ in range(2)]
+    rows = []
+    for _ in range(2):
+        buf = torch.zeros(n, width + 64, dtype=torch.bfloat16, device=DEV)
+        buf[:, :width] = qkv.to(DEV)
+        rows.append(buf[:, :width])
+    # separate: rotate, then store the strided k / v views
+    kernels.qk_norm_rope(rows[0], hq, hk, d, qw, kw, cos_sin, pos, 1e-6)
+    k = rows[0][:, hq * d:(hq + hk) * d].view(n, hk, d)
+    v = rows[0][:, (hq + hk) * d:].view(n, hk, d)
+    if fp8:
+        kernels.store_kvcache_fp8(k, v, caches[0][0], caches[0][1], slots, ks, vs)
+    else:
+        kernels.store_kvcache(k, v, caches[0][0], caches[0][1], slots)
+    kernels.qk_norm_rope_store(rows[1], hq, hk, d, qw, kw, cos_sin, pos, 1e-6, caches[1][0], caches[1][1], slots,
+                               ks, vs)
+    assert rows[1].stride(0) == width + 64
+    assert torch.equal(rows[0].contiguous().view(torch.int16), rows[1].contiguous().view(torch.int16))
+    for a, b in zip(caches[0], caches[1]):
+        assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+
+
 def test_silu_mul_matches_reference_module(golden_dir):
     g = np.load(golden_dir / "layers.npz")
     a = bf(g["silu_in"]).to(DEV)
