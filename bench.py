@@ -405,6 +405,9 @@ def run_profile(args):
                                                                  block_table=bt, precise_p=True),
                     "tc_bf16p": lambda: kernels.varlen_prefill(q, kc, vc, cuq, cuk, max(chunks), max(kl), d ** -0.5,
                                                                block_table=bt, precise_p=False),
+                    "tc_one_head_precise": lambda: kernels.varlen_prefill(q, kc, vc, cuq, cuk, max(chunks), max(kl),
+                                                                          d ** -0.5, block_table=bt,
+                                                                          one_head_per_cta=True),
                     "simt": lambda: kernels.varlen_prefill_simt(q, kc, vc, cuq, cuk, max(chunks), max(kl), d ** -0.5,
                                                                 block_table=bt)}
         stream = torch.cuda.current_stream()

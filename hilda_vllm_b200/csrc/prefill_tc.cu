@@ -429,6 +429,410 @@ __global__ void __launch_bounds__(kThreads, 1) varlen_prefill_tc_kernel(const __
   }
 }
 
+// ---------------------------------------------------------------------------------- head pairs
+// The production kernel when Hq / Hk is even: one CTA = 128 query rows of the TWO query heads
+// 2p and 2p+1, which share one KV head, so every K/V tile brought in by TMA feeds twice the
+// MMAs.  TMEM holds S_a, S_b (128 columns each) and O_a, O_b (128 each) = all 512 columns; the
+// probabilities are written back over their own S columns as bf16 (P_hi in the first 64
+// columns, P_lo in the next 64 with SPLIT_P) and the PV product reads them straight from TMEM
+// as the A operand (tcgen05.mma with [a-tmem]), so P never touches shared memory.
+//   warp 0     TMA producer (both Q tiles once, then K+V tiles into a 2-stage ring)
+//   warp 1     TMEM allocator + MMA issuer, in ping-pong order per key tile j:
+//                PV_a(j), QK_a(j+1), PV_b(j), QK_b(j+1)
+//              so the tensor core works on one head while the other head's softmax runs.
+//   warps 2-5  softmax of head a (thread = query row = TMEM lane; warp w reads TMEM lanes
+//              32 * (w % 4) ..), warps 6-9 softmax of head b.
+// O is rescaled lazily: the running reference max only moves when a tile's max exceeds it by
+// more than kRescaleLog2 (probabilities then stay <= 2^kRescaleLog2, exact in bf16 range),
+// which skips almost every O read-modify-write of TMEM.  Since tcgen05.commit tracks every
+// earlier MMA of the issuing thread, "S_a(j) is ready" also means PV_a(j-1) has finished, so
+// the softmax warps may touch O_a then.  CTAs run heaviest query tile first (blockIdx.z is
+// the reversed tile index) to shorten the causal tail.
+constexpr int kThreads2 = 320;
+constexpr int kOff2Qa = 0;
+constexpr int kOff2Qb = kTile;
+constexpr int kOff2K = 2 * kTile;                        // + stage * 2 * kTile; V at + kTile
+constexpr int kOff2Bar = kOff2K + kStages * 2 * kTile;   // 192 KiB
+constexpr int kSmem2Bytes = kOff2Bar + 256 + 1024;
+constexpr float kRescaleLog2 = 8.f;
+
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                             uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+// 2^x on the MUFU unit (ex2.approx.ftz: 2^-inf = +0, relative error ~2^-22).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Bounded mbarrier wait that also gives up as soon as another role has raised the abort flag.
+__device__ __forceinline__ bool wait2(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < kMaxWaitPolls; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 63u) == 63u && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  atomicOr(&g_prefill_errors, 1);
+  return false;
+}
+
+template <bool SPLIT_P>
+__global__ void __launch_bounds__(kThreads2, 1) varlen_prefill_pair_kernel(const __grid_constant__ TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOff2Bar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2] stages
+  uint64_t* kv_empty = bars + 3;  // [2] stages
+  uint64_t* s_full = bars + 5;    // [2] heads
+  uint64_t* p_full = bars + 7;    // [2] heads
+  uint64_t* o_done = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13);
+
+  const int pair = blockIdx.x;
+  const int s = blockIdx.y;
+  const int tile = gridDim.z - 1 - blockIdx.z;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = p.num_q_heads / p.num_kv_heads;
+  const int hq0 = 2 * pair;
+  const int hk = hq0 / G;
+
+  const int q_begin = p.cu_q[s];
+  const int Lq = p.cu_q[s + 1] - q_begin;
+  const int k_begin = p.cu_k[s];
+  const int Lk = p.cu_k[s + 1] - k_begin;
+  const int q0 = tile * kBM;
+  if (q0 >= Lq) return;  // uniform per CTA
+  const int shift = Lk - Lq;
+  int k_needed = min(Lk, q0 + kBM + shift);
+  if (k_needed < 0) k_needed = 0;
+  const int n_tiles = (k_needed + kBN - 1) / kBN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);    // producer arrive.expect_tx + TMA bytes
+      mbar_init(&kv_empty[i], 1);   // tcgen05.commit after the tile's last MMA
+      mbar_init(&s_full[i], 1);     // tcgen05.commit after QK of head i
+      mbar_init(&p_full[i], 128);   // every softmax thread of head i wrote its P row
+    }
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0 && n_tiles > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * kTile);
+      tma_load_3d(sbase + kOff2Qa, &p.tq, 0, hq0, q_begin + q0, smem_u32(q_full));
+      tma_load_3d(sbase + kOff2Qa + kHalf, &p.tq, 64, hq0, q_begin + q0, smem_u32(q_full));
+      tma_load_3d(sbase + kOff2Qb, &p.tq, 0, hq0 + 1, q_begin + q0, smem_u32(q_full));
+      tma_load_3d(sbase + kOff2Qb + kHalf, &p.tq, 64, hq0 + 1, q_begin + q0, smem_u32(q_full));
+      int issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !wait2(&kv_empty[st], ((j - 2) >> 1) & 1, abort_flag)) break;
+        const int kj = j * kBN;
+        int row;
+        if (p.paged) {
+          const int blk = p.block_tables[int64_t(s) * p.bt_stride + kj / p.block_size];
+          row = blk * p.block_size + (kj % p.block_size);  // a bad (-1) block reads zeros (out of range)
+        } else {
+          row = k_begin + kj;
+        }
+        const uint32_t kdst = sbase + kOff2K + st * 2 * kTile;
+        const uint32_t vdst = kdst + kTile;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+        tma_load_3d(kdst, &p.tk, 0, hk, row, smem_u32(&kv_full[st]));
+        tma_load_3d(kdst + kHalf, &p.tk, 64, hk, row, smem_u32(&kv_full[st]));
+        tma_load_3d(vdst, &p.tv, 0, hk, row, smem_u32(&kv_full[st]));
+        tma_load_3d(vdst + kHalf, &p.tv, 64, hk, row, smem_u32(&kv_full[st]));
+        issued = j + 1;
+      }
+      // Drain: no copy into this CTA's shared memory may still be in flight at exit (the
+      // normal path returns at once, every tile having been consumed).
+      mbar_wait(q_full, 0);
+      for (int t = issued >= 2 ? issued - 2 : 0; t < issued; ++t) mbar_wait(&kv_full[t & 1], (t >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (n_tiles > 0) {
+      auto qk = [&](int j, int h) {
+        const uint32_t qbase = sbase + (h ? kOff2Qb : kOff2Qa);
+        const uint32_t kbase = sbase + kOff2K + (j & 1) * 2 * kTile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t a = smem_desc(qbase + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+          const uint64_t b = smem_desc(kbase + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+          umma_bf16(tmem + h * 128, a, b, kIdescS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(smem_u32(&s_full[h]));
+      };
+      auto pv = [&](int j, int h) {
+        const uint32_t vbase = sbase + kOff2K + (j & 1) * 2 * kTile + kTile;
+        const uint32_t pcol = tmem + h * 128;
+        const uint32_t ocol = tmem + kColO + h * 128;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t b = smem_desc(vbase + kk * 16 * 128, kHalf, 1024);
+          umma_bf16_ts(ocol, pcol + kk * 8, b, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        if constexpr (SPLIT_P) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t b = smem_desc(vbase + kk * 16 * 128, kHalf, 1024);
+            umma_bf16_ts(ocol, pcol + 64 + kk * 8, b, kIdescPV, 1u);
+          }
+        }
+      };
+      bool ok = __all_sync(0xffffffffu, wait2(q_full, 0, abort_flag) && wait2(&kv_full[0], 0, abort_flag));
+      if (ok && lane == 0) {
+        tc_fence_after();
+        qk(0, 0);
+        qk(0, 1);
+      }
+      __syncwarp();
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int st = j & 1;
+        ok = __all_sync(0xffffffffu, wait2(&p_full[0], j & 1, abort_flag));
+        if (!ok) break;
+        const int j0 = j * kBN;
+        if (j0 + kBN > Lk) {
+          // Last, partial tile: zero the V rows past the sequence so that P = 0 never meets a
+          // non-finite cache value inside the MMA (the tile's TMA landed before its QK).
+          uint8_t* vs = smem + kOff2K + st * 2 * kTile + kTile;
+          for (int rr = max(Lk - j0, 0) + lane; rr < kBN; rr += 32) {
+            uint4* v0 = reinterpret_cast<uint4*>(vs + rr * 128);
+            uint4* v1 = reinterpret_cast<uint4*>(vs + kHalf + rr * 128);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+        if (lane == 0) {
+          tc_fence_after();
+          pv(j, 0);
+        }
+        if (j + 1 < n_tiles) {
+          ok = __all_sync(0xffffffffu, wait2(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag));
+          if (!ok) break;
+          if (lane == 0) qk(j + 1, 0);
+        }
+        ok = __all_sync(0xffffffffu, wait2(&p_full[1], j & 1, abort_flag));
+        if (!ok) break;
+        if (lane == 0) {
+          tc_fence_after();
+          pv(j, 1);
+          umma_commit(smem_u32(&kv_empty[st]));
+          if (j + 1 < n_tiles) qk(j + 1, 1);
+        }
+        __syncwarp();
+      }
+      if (lane == 0) {
+        umma_commit(smem_u32(o_done));
+        if (!ok) mbar_wait(o_done, 0);  // let issued MMAs finish before TMEM is freed
+      }
+      __syncwarp();
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int h = (warp - 2) >> 2;   // 0: head a, 1: head b
+    const int quarter = warp & 3;    // TMEM lanes [32 * quarter, +32) belong to this warp
+    const int r = quarter * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+    const uint32_t s_col = lane_base + h * 128;
+    const uint32_t o_col = lane_base + kColO + h * 128;
+    const int limit = qi + shift;  // keys j <= limit are visible (and j < Lk)
+    const float sc = p.scale_log2;
+    float m_ref = -INFINITY, l = 0.f;
+    bool alive = n_tiles > 0;
+    for (int j = 0; alive && j < n_tiles; ++j) {
+      if (!__all_sync(0xffffffffu, wait2(&s_full[h], j & 1, abort_flag))) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t raw[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32_async(s_col + c * 32, raw[c]);
+      tmem_wait_ld();
+      float sv[kBN];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(raw[c][i]);
+      const int j0 = j * kBN;
+      // Rows of this tile see every key of it unless the tile reaches the diagonal or Lk.
+      if (j0 + kBN - 1 > q0 + shift || j0 + kBN > Lk) {
+        const int lim = min(limit, Lk - 1) - j0;  // visible columns c <= lim
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) sv[c] = c <= lim ? sv[c] : -INFINITY;
+      }
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < kBN; c += 4) {
+        mx[0] = fmaxf(mx[0], sv[c]);
+        mx[1] = fmaxf(mx[1], sv[c + 1]);
+        mx[2] = fmaxf(mx[2], sv[c + 2]);
+        mx[3] = fmaxf(mx[3], sv[c + 3]);
+      }
+      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sc;
+      float corr = 1.f;
+      if (mt > m_ref + kRescaleLog2) {
+        if (m_ref != -INFINITY) corr = ex2(m_ref - mt);
+        m_ref = mt;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+        // PV_h(j-1) has completed (it was issued before QK_h(j), whose commit we waited for).
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          uint32_t o[16];
+          tmem_ld16_async(o_col + c * 16, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+          tmem_st16(o_col + c * 16, o);
+        }
+      }
+      l *= corr;
+      // p = 2^(s * scale_log2 - m_ref); masked keys (-inf) give 0; a row with nothing visible
+      // yet (m_ref = -inf) gives all zeros.
+      const float msub = m_ref == -INFINITY ? 0.f : m_ref;
+      const float2 sc2 = make_float2(sc, sc);
+      const float2 nm2 = make_float2(-msub, -msub);
+      float2 rs = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float2 x = __ffma2_rn(make_float2(sv[ch * 16 + 2 * t], sv[ch * 16 + 2 * t + 1]), sc2, nm2);
+          const float2 e = make_float2(ex2(x.x), ex2(x.y));
+          rs = __fadd2_rn(rs, e);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(e.x, e.y);
+          hi[t] = *reinterpret_cast<uint32_t*>(&h2);
+          if constexpr (SPLIT_P) {
+            const float2 hf = __bfloat1622float2(h2);
+            __nv_bfloat162 l2 = __floats2bfloat162_rn(e.x - hf.x, e.y - hf.y);
+            lo[t] = *reinterpret_cast<uint32_t*>(&l2);
+          }
+        }
+        tmem_st8(s_col + ch * 8, hi);
+        if constexpr (SPLIT_P) tmem_st8(s_col + 64 + ch * 8, lo);
+      }
+      l += rs.x + rs.y;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[h]);
+    }
+    // Epilogue: O / l -> bf16 rows of the output (rows past the sequence load but do not store).
+    const bool have_o = __all_sync(0xffffffffu, alive && n_tiles > 0 && wait2(o_done, 0, abort_flag));
+    if (have_o) tc_fence_after();
+    __nv_bfloat16* orow = p.out + int64_t(q_begin + qi) * p.out_row_stride + (hq0 + h) * kD;
+    const float inv = (have_o && l > 0.f) ? 1.f / l : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t o[32];
+      if (have_o) {
+        tmem_ld32_async(o_col + c * 32, o);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0u;
+      }
+      if (qi < Lq) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint32_t w[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(o[v * 8 + 2 * t]) * inv,
+                                                      __uint_as_float(o[v * 8 + 2 * t + 1]) * inv);
+            w[t] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+          *reinterpret_cast<uint4*>(orow + c * 32 + v * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // ---------------------------------------------------------------------------------- host
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -464,6 +868,24 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t heads, uint64_t rows,
 }  // namespace hl
 
 using namespace hl;
+
+template <bool SPLIT_P>
+int launch_pair(const TcParams& prm, int max_seqlen_q, int num_q_heads, int num_seqs, cudaStream_t stream) {
+  static bool configured = false;  // first call happens before any graph capture
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(varlen_prefill_pair_kernel<SPLIT_P>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2Bytes);
+    if (e != cudaSuccess) {
+      set_error("hl_varlen_prefill: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return HL_ERR_CUDA;
+    }
+    configured = true;
+  }
+  dim3 grid(num_q_heads / 2, num_seqs, (max_seqlen_q + kBM - 1) / kBM);
+  varlen_prefill_pair_kernel<SPLIT_P><<<grid, kThreads2, kSmem2Bytes, stream>>>(prm);
+  HL_CHECK_LAUNCH("hl_varlen_prefill");
+  return HL_OK;
+}
 
 template <bool SPLIT_P>
 int launch_tc(const TcParams& prm, int max_seqlen_q, int num_q_heads, int num_seqs, cudaStream_t stream) {
@@ -534,7 +956,14 @@ extern "C" int hl_varlen_prefill(const void* q, int64_t q_row_stride, int64_t to
   prm.out = static_cast<__nv_bfloat16*>(out);
   prm.out_row_stride = out_row_stride;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (precise_p) return launch_tc<true>(prm, max_seqlen_q, num_q_heads, num_seqs, st);
+  const bool split = (precise_p & 1) != 0;
+  const bool pairs = (num_q_heads / num_kv_heads) % 2 == 0 && !(precise_p & HL_PREFILL_ONE_HEAD_PER_CTA);
+  HL_CHECK_ARG((max_seqlen_q + kBM - 1) / kBM <= 65535, "hl_varlen_prefill: max_seqlen_q too large");
+  if (pairs) {
+    if (split) return launch_pair<true>(prm, max_seqlen_q, num_q_heads, num_seqs, st);
+    return launch_pair<false>(prm, max_seqlen_q, num_q_heads, num_seqs, st);
+  }
+  if (split) return launch_tc<true>(prm, max_seqlen_q, num_q_heads, num_seqs, st);
   return launch_tc<false>(prm, max_seqlen_q, num_q_heads, num_seqs, st);
 }
 

@@ -235,13 +235,14 @@ def varlen_prefill_simt(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_se
 def varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
                    cu_seqlens_k: torch.Tensor, max_seqlen_q: int, max_seqlen_k: int, softmax_scale: float,
                    block_table: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                   precise_p: bool = True) -> torch.Tensor:
+                   precise_p: bool = True, one_head_per_cta: bool = False) -> torch.Tensor:
     """Causal varlen attention with a bottom-right-aligned mask on the tcgen05/TMEM kernel.
 
     Same arguments as the reference's flash_attn_varlen_func call
     (mini_vllm/layers/attention.py:149-160): q [Tq, Hq, D]; with block_table, k/v are the paged
     caches [NB, BS, Hk, D]; without, k/v are [Tk, Hk, D].  Returns [Tq, Hq, D] bf16.
-    precise_p feeds P to the P.V MMA as bf16 hi + lo terms (see hl_varlen_prefill)."""
+    precise_p feeds P to the P.V MMA as bf16 hi + lo terms (see hl_varlen_prefill);
+    one_head_per_cta forces the one-query-head-per-CTA kernel instead of the head-pair kernel."""
     _cuda(q, k, v, cu_seqlens_q, cu_seqlens_k, block_table, out)
     tq, hq, hd = q.shape
     assert q.stride(2) == 1 and q.stride(1) == hd
@@ -265,7 +266,8 @@ def varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens
     check(lib.hl_varlen_prefill(q.data_ptr(), q.stride(0), tq, k.data_ptr(), v.data_ptr(), k_rs, v_rs, total_k,
                                    cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), bt_ptr, bt_stride, num_seqs,
                                    int(max_seqlen_q), hq, hk, hd, bsz, nb, float(softmax_scale), out.data_ptr(),
-                                   out.stride(0), 1 if precise_p else 0, _stream(q)), "hl_varlen_prefill")
+                                   out.stride(0), (1 if precise_p else 0) | (2 if one_head_per_cta else 0),
+                                   _stream(q)), "hl_varlen_prefill")
     return out
 
 

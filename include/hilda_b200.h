@@ -157,7 +157,11 @@ int hl_paged_decode_read_errors(const void* workspace, int32_t* errors_out, void
  * significant bits; one extra MMA group per tile) instead of one bf16-rounded term, which keeps
  * outputs within an fp32 reference's rtol 2e-2 / atol 2e-3 where heavy cancellation defeats
  * bf16 P (bf16 P alone is what flash-attn does).  Requires head_dim == 128 and Hq % Hk == 0.
+ * When Hq / Hk is even, one CTA computes the two query heads of a KV head together (each
+ * K/V tile feeds both; P kept in TMEM as the A operand of the P.V MMA); otherwise one head per
+ * CTA.  precise_p | HL_PREFILL_ONE_HEAD_PER_CTA forces the one-head kernel (for comparison).
  * ---------------------------------------------------------------------------------- */
+#define HL_PREFILL_ONE_HEAD_PER_CTA 2
 int hl_varlen_prefill(const void* q, int64_t q_row_stride, int64_t total_q,
                       const void* k, const void* v, int64_t k_row_stride, int64_t v_row_stride,
                       int64_t total_k, const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
