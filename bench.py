@@ -60,11 +60,13 @@ def parse():
                     help="c2 (default, the headline): BASELINE configs[1]; c3: FP8 KV with a capped pool; "
                          "c4: mixed chunked prefill + decode with shared prefixes; c5: Qwen3-8B (TP over --gpus)")
     ap.add_argument("--kv", default="auto", choices=["auto", "fp8"], help="KV cache dtype for c5")
-    ap.add_argument("--profile", default="", choices=["", "decode-kernel", "decode-steps", "prefill-kernel"],
+    ap.add_argument("--profile", default="",
+                    choices=["", "decode-kernel", "decode-steps", "prefill-kernel", "small-kernels"],
                     help="run a short profiling case instead of the benchmark: the CUDA profiler range "
                          "(cudaProfilerStart/Stop, for ncu --profile-from-start off) covers --steps "
-                         "launches of the decode kernel alone (decode-kernel) or --steps engine decode "
-                         "steps at the job's mid context (decode-steps)")
+                         "launches of the decode kernel alone (decode-kernel), of the prefill kernel "
+                         "(prefill-kernel), of every other kernel (small-kernels), or --steps engine "
+                         "decode steps at the job's mid context (decode-steps)")
     return ap.parse_args()
 
 
@@ -310,7 +312,25 @@ def run_ours(args):
                "sample": f"{CPU_SAMPLE_SEQS} sequences x 2 decode steps at context {CPU_CTX} "
                          f"({dt:.1f} s), reference arithmetic via the CPU oracle port"}
 
-    launches_per_step = 1 + hf.num_hidden_layers * 6 + 2
+    # Our kernels per decode step: the pack kernel; per layer input add+RMSNorm, fused
+    # QK-norm+RoPE+KV store, paged decode, post-attention add+RMSNorm, SiLU*mul; final norm;
+    # argmax (cuBLAS GEMMs and torch's embedding gather are not counted).
+    launches_per_step = 1 + hf.num_hidden_layers * 5 + 2
+
+    # ---- whole-job roofline: weight bytes + KV bytes every decode step must read, per GPU ----
+    d = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
+    per_layer = hf.hidden_size * (hf.num_attention_heads + 2 * hf.num_key_value_heads) * d \
+        + hf.num_attention_heads * d * hf.hidden_size + 3 * hf.hidden_size * hf.intermediate_size
+    weight_bytes = 2 * (hf.num_hidden_layers * per_layer + hf.vocab_size * hf.hidden_size) / world
+    kv_token_bytes = hf.num_hidden_layers * hf.num_key_value_heads * d * 2 * 2 / world
+    ctx_sum = sum(NUM_SEQS * (PROMPT_LEN + 1 + s) for s in range(steps_per_sweep))
+    job_bytes = steps_per_sweep * weight_bytes + ctx_sum * kv_token_bytes
+    roof_tok_s = tokens_per_sweep / (job_bytes / (hbm_peak * 1e9))
+    job_roofline = {"tok_s": round(roof_tok_s, 1), "bytes_per_gpu": int(job_bytes), "peak_gbs": hbm_peak,
+                    "value_frac": round(value / roof_tok_s, 4),
+                    "e2e_frac": round(e2e["value"] / roof_tok_s, 4) if e2e else None,
+                    "what": "decode tok/s if every step only streamed its weights and KV cache from HBM at the "
+                            "measured copy bandwidth (per GPU under TP)"}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(sweep_s * 1e3, 2), "higher_is_better": True,
@@ -323,6 +343,7 @@ def run_ours(args):
                    "l2": "no flush: per-step KV (0.6-3.2 GB) and weights (1.2 GB) exceed the 126 MB L2"},
         "decode_ms_per_batch_step": round(sweep_s * 1e3 / steps_per_sweep, 4),
         "roofline": roofline,
+        "kv_weight_roofline": job_roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "clocks": clocks,
@@ -330,6 +351,113 @@ def run_ours(args):
     }
     print(json.dumps(line), flush=True)
     llm.exit()
+
+
+def small_kernels(args, g):
+    """Every kernel besides decode and prefill attention, at config-2 shapes, args.steps launches
+    each inside the profiler range, timed with CUDA events: the fused QK-norm+RoPE+KV store
+    (BF16 and FP8, decode batch of 256 and a 16384-token prefill), the standalone BF16 store,
+    the all-layer BF16->FP8 cache copy, the decode pack kernel on a full packet, add+RMSNorm,
+    SiLU*mul and the greedy argmax.  A few GB on the device at most."""
+    import numpy as np
+    import torch
+
+    from hilda_vllm_b200 import kernels
+    from hilda_vllm_b200.engine.decode_packer import DecodePacker
+    from hilda_vllm_b200.engine.scheduler import ScheduledSequence
+    from hilda_vllm_b200.engine.sequence import Sequence, SequenceStatus
+    from hilda_vllm_b200.layers.rotary_embedding import RotaryEmbedding
+
+    dev = torch.device("cuda", 0)
+    hq, hk, d, bs, layers, hidden, inter, vocab = 16, 8, 128, 256, 28, 1024, 3072, 151936
+    nb = 512  # 0.27 GB per BF16 cache
+    cos_sin = RotaryEmbedding(d, d, 40960, 1000000.0).cos_sin_cache.to(dev).contiguous()
+    qw = torch.ones(d, dtype=torch.bfloat16, device=dev)
+    kc = torch.zeros(nb, bs, hk, d, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    kc8 = torch.zeros(nb, bs, hk, d, dtype=torch.float8_e4m3fn, device=dev)
+    vc8 = torch.zeros_like(kc8)
+    scales = torch.rand(hk, device=dev) + 0.5
+    cases = {}
+    # Algorithmic bytes of the fused kernel: every qkv element read, q and k written back in
+    # place, the K and V rows written to the cache (2 bytes per element BF16, 1 FP8).
+    for n in (NUM_SEQS, 16384):
+        qkv = torch.randn(n, (hq + 2 * hk) * d, device=dev, dtype=torch.bfloat16)
+        pos = torch.randint(0, 1088, (n,), device=dev)
+        slots = torch.randperm(nb * bs, device=dev)[:n].to(torch.int32)
+        for kv, (kcache, vcache, sc) in {"bf16": (kc, vc, None), "fp8": (kc8, vc8, scales)}.items():
+            elem = 1 if kv == "fp8" else 2
+            cases[f"qk_norm_rope_store_{kv}_n{n}"] = (
+                lambda qkv=qkv, pos=pos, slots=slots, kcache=kcache, vcache=vcache, sc=sc: kernels.qk_norm_rope_store(
+                    qkv, hq, hk, d, qw, qw, cos_sin, pos, 1e-6, kcache, vcache, slots, sc, sc),
+                n * ((hq + 2 * hk) * d * 2 + (hq + hk) * d * 2 + 2 * hk * d * elem))
+    n = 16384
+    qkv = torch.randn(n, (hq + 2 * hk) * d, device=dev, dtype=torch.bfloat16)
+    slots = torch.randperm(nb * bs, device=dev)[:n].to(torch.int32)
+    key = qkv[:, hq * d:(hq + hk) * d].view(n, hk, d)
+    val = qkv[:, (hq + hk) * d:].view(n, hk, d)
+    cases["store_kv_bf16_n16384"] = (lambda: kernels.store_kvcache(key, val, kc, vc, slots), n * hk * d * 2 * 4)
+    # all-layer BF16 -> FP8 copy (prefill-to-decode cache handoff): 8192 slots x 28 layers
+    nbl = 32
+    src = torch.randn(2, layers, nbl, bs, hk, d, device=dev, dtype=torch.bfloat16)
+    dst = torch.zeros(2, layers, nbl, bs, hk, d, device=dev, dtype=torch.float8_e4m3fn)
+    cslots = torch.randperm(nbl * bs, device=dev)[:8192].to(torch.int32)
+    lsc = torch.rand(layers, hk, device=dev) + 0.5
+    cases["copy_kv_bf16_to_fp8_28layers_n8192"] = (
+        lambda: kernels.copy_kvcache_fp8_layers(src[0], src[1], dst[0], dst[1], cslots, lsc, lsc),
+        8192 * layers * 2 * hk * d * 3)
+    # decode pack kernel on a full packet (every slot a new owner with a 5-block row)
+    mb = -(-MAX_MODEL_LEN // bs)
+    packer = DecodePacker(NUM_SEQS, mb)
+    sched = []
+    for i in range(NUM_SEQS):
+        seq = Sequence(list(range(577)))
+        seq.status = SequenceStatus.RUNNING
+        seq.num_computed_tokens = 576
+        seq.block_table = [(5 * i + j) % nb for j in range(3)]
+        sched.append(ScheduledSequence(seq, 1, i))
+    nbytes = packer.build(sched, NUM_SEQS)
+    packet = torch.from_numpy(packer.buffer[:nbytes].copy()).to(dev)
+    gv = dict(slot_seq_ids=torch.full((NUM_SEQS,), -1, dtype=torch.int64, device=dev),
+              slot_bt_lens=torch.zeros(NUM_SEQS, dtype=torch.int32, device=dev),
+              next_tokens=torch.zeros(NUM_SEQS, dtype=torch.int64, device=dev),
+              input_ids=torch.zeros(NUM_SEQS, dtype=torch.int64, device=dev),
+              positions=torch.zeros(NUM_SEQS, dtype=torch.int64, device=dev),
+              slot_mapping=torch.zeros(NUM_SEQS, dtype=torch.int32, device=dev),
+              context_lens=torch.zeros(NUM_SEQS, dtype=torch.int32, device=dev),
+              block_tables=torch.full((NUM_SEQS, mb), -1, dtype=torch.int32, device=dev))
+    cases["pack_decode_full_packet_b256"] = (
+        lambda: kernels.pack_decode_batch(packet, NUM_SEQS, bs, gv["slot_seq_ids"], gv["slot_bt_lens"],
+                                          gv["next_tokens"], gv["input_ids"], gv["positions"], gv["slot_mapping"],
+                                          gv["context_lens"], gv["block_tables"]),
+        nbytes + NUM_SEQS * (8 + 4 + 8 + 8 + 8 + 4 + 4 + mb * 4))
+    x = torch.randn(NUM_SEQS, hidden, device=dev, dtype=torch.bfloat16)
+    res = torch.randn_like(x)
+    nw = torch.ones(hidden, device=dev, dtype=torch.bfloat16)
+    cases["add_rmsnorm_b256"] = (lambda: kernels.rmsnorm(x, nw, 1e-6, residual=res), NUM_SEQS * hidden * 2 * 4)
+    gu = torch.randn(NUM_SEQS, 2 * inter, device=dev, dtype=torch.bfloat16)
+    cases["silu_mul_b256"] = (lambda: kernels.silu_mul(gu), NUM_SEQS * inter * 2 * 3)
+    logits = torch.randn(NUM_SEQS, vocab, device=dev, dtype=torch.bfloat16)
+    toks = torch.zeros(NUM_SEQS, dtype=torch.int64, device=dev)
+    cases["argmax_b256"] = (lambda: kernels.argmax(logits, toks), NUM_SEQS * vocab * 2)
+
+    out = {"profile": "small-kernels"}
+    stream = torch.cuda.current_stream()
+    for fn, _ in cases.values():
+        fn()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    for name, (fn, nbytes_alg) in cases.items():
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        out[name] = {"us": round(us, 2), "alg_bytes": int(nbytes_alg), "gb_per_s": round(nbytes_alg / us / 1e3, 1)}
+    torch.cuda.profiler.stop()
+    print(json.dumps(out))
 
 
 def run_profile(args):
@@ -428,6 +556,9 @@ def run_profile(args):
             ms = e0.elapsed_time(e1) / reps
             res[name] = {"ms": round(ms, 3), "tflops": round(flops / ms / 1e9, 1)}
         print(json.dumps(res))
+        return
+    if args.profile == "small-kernels":
+        small_kernels(args, g)
         return
     # decode-steps: the engine at the job's mid context (prompts of 576 tokens, 256 sequences).
     ctx = PROMPT_LEN + OUTPUT_LEN // 2

@@ -440,15 +440,20 @@ __global__ void __launch_bounds__(kThreads, 1) varlen_prefill_tc_kernel(const __
 //   warp 1     TMEM allocator + MMA issuer, in ping-pong order per key tile j:
 //                PV_a(j), QK_a(j+1), PV_b(j), QK_b(j+1)
 //              so the tensor core works on one head while the other head's softmax runs.
-//   warps 2-5  softmax of head a (thread = query row = TMEM lane; warp w reads TMEM lanes
-//              32 * (w % 4) ..), warps 6-9 softmax of head b.
+//   warps 2-3  idle
+//   warps 4-7  softmax of head a (thread = query row = TMEM lane; warp w reads TMEM lanes
+//              32 * (w % 4) ..), warps 8-11 softmax of head b.
+// Registers: the kernel launches with 168 per thread (384 x 168 = 64512 of the SM's 65536);
+// warpgroup 0 (warps 0-3) gives back down to 56 with setmaxnreg.dec and the two softmax
+// warpgroups take them with setmaxnreg.inc to 224 (128 x 56 + 256 x 224 = 64512), so a whole
+// 128-key S row stays in registers.
 // O is rescaled lazily: the running reference max only moves when a tile's max exceeds it by
 // more than kRescaleLog2 (probabilities then stay <= 2^kRescaleLog2, exact in bf16 range),
 // which skips almost every O read-modify-write of TMEM.  Since tcgen05.commit tracks every
 // earlier MMA of the issuing thread, "S_a(j) is ready" also means PV_a(j-1) has finished, so
 // the softmax warps may touch O_a then.  CTAs run heaviest query tile first (blockIdx.z is
 // the reversed tile index) to shorten the causal tail.
-constexpr int kThreads2 = 320;
+constexpr int kThreads2 = 384;
 constexpr int kOff2Qa = 0;
 constexpr int kOff2Qb = kTile;
 constexpr int kOff2K = 2 * kTile;                        // + stage * 2 * kTile; V at + kTile
@@ -586,7 +591,9 @@ __global__ void __launch_bounds__(kThreads2, 1) varlen_prefill_pair_kernel(const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+  }
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0 && n_tiles > 0) {
@@ -702,9 +709,10 @@ __global__ void __launch_bounds__(kThreads2, 1) varlen_prefill_pair_kernel(const
       }
       __syncwarp();
     }
-  } else {
+  } else if (warp >= 4) {
     // ---------------------------------------------------------------- softmax + epilogue
-    const int h = (warp - 2) >> 2;   // 0: head a, 1: head b
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;");
+    const int h = (warp - 4) >> 2;   // 0: head a, 1: head b
     const int quarter = warp & 3;    // TMEM lanes [32 * quarter, +32) belong to this warp
     const int r = quarter * 32 + lane;
     const int qi = q0 + r;
