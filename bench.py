@@ -61,7 +61,7 @@ def parse():
                          "c4: mixed chunked prefill + decode with shared prefixes; c5: Qwen3-8B (TP over --gpus)")
     ap.add_argument("--kv", default="auto", choices=["auto", "fp8"], help="KV cache dtype for c5")
     ap.add_argument("--profile", default="",
-                    choices=["", "decode-kernel", "decode-steps", "prefill-kernel", "small-kernels"],
+                    choices=["", "decode-kernel", "decode-steps", "prefill-kernel", "small-kernels", "allreduce"],
                     help="run a short profiling case instead of the benchmark: the CUDA profiler range "
                          "(cudaProfilerStart/Stop, for ncu --profile-from-start off) covers --steps "
                          "launches of the decode kernel alone (decode-kernel), of the prefill kernel "
@@ -460,12 +460,89 @@ def small_kernels(args, g):
     print(json.dumps(out))
 
 
+def allreduce_profile(args):
+    """Under torchrun with --gpus N: the fused NVLink all-reduce + add + RMSNorm against NCCL
+    all_reduce followed by the add + RMSNorm kernel, at decode batches of the 0.6B (hidden 1024)
+    and 8B (hidden 4096) models.  Each variant is captured in a CUDA graph of 56 calls (one
+    decode step's worth) and replayed; CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from hilda_vllm_b200 import kernels
+    from hilda_vllm_b200.layers.nvlink_allreduce import NvlinkAllReduce
+
+    world = args.gpus
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    res_all = {"profile": "allreduce", "n_gpus": world}
+    calls = 56
+    for hidden in (1024, 4096):
+        ar = NvlinkAllReduce(rank, world, 512, hidden, dev, timeout_s=20.0)
+        w = torch.ones(hidden, dtype=torch.bfloat16, device=dev)
+        for rows in (64, 256):
+            res = torch.randn(rows, hidden, dtype=torch.bfloat16, device=dev)
+            part = torch.randn(rows, hidden, dtype=torch.bfloat16, device=dev)
+            out = torch.empty_like(res)
+
+            def fused():
+                for i in range(calls):
+                    ar.output(i % 2, rows).copy_(part)
+                    ar.add_rmsnorm(i % 2, rows, res, w, 1e-6, out)
+
+            def nccl():
+                for i in range(calls):
+                    y = part.clone()
+                    dist.all_reduce(y)
+                    kernels.rmsnorm(y, w, 1e-6, residual=res)
+
+            def copies():
+                for i in range(calls):
+                    ar.output(i % 2, rows).copy_(part)
+                    part.clone()
+
+            for name, fn in (("fused_nvlink", fused), ("nccl_plus_rmsnorm", nccl), ("copies_only", copies)):
+                fn()
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    fn()
+                for _ in range(3):
+                    graph.replay()
+                torch.cuda.synchronize()
+                dist.barrier()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(20):
+                    graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                t = torch.tensor([e0.elapsed_time(e1) * 1e3 / (20 * calls)], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                res_all[f"{name}_h{hidden}_rows{rows}_us_per_call"] = round(float(t.item()), 2)
+                del graph
+        ar.copy_error_word()
+        torch.cuda.synchronize()
+        ar.check_errors()
+        dist.barrier()
+        ar.close()
+    if rank == 0:
+        print(json.dumps(res_all), flush=True)
+    dist.destroy_process_group()
+
+
 def run_profile(args):
     """Short, self-contained cases for ncu (one GPU)."""
     import torch
 
     from hilda_vllm_b200 import LLM, SamplingParams, kernels
 
+    if args.profile == "allreduce":
+        allreduce_profile(args)
+        return
     torch.cuda.set_device(0)
     g = torch.Generator().manual_seed(args.seed)
     if args.profile == "decode-kernel":
@@ -560,6 +637,7 @@ def run_profile(args):
     if args.profile == "small-kernels":
         small_kernels(args, g)
         return
+
     # decode-steps: the engine at the job's mid context (prompts of 576 tokens, 256 sequences).
     ctx = PROMPT_LEN + OUTPUT_LEN // 2
     prompts = [torch.randint(0, 151936, (ctx,), generator=g).tolist() for _ in range(NUM_SEQS)]

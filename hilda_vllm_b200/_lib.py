@@ -103,6 +103,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hl_qk_norm_rope": (c_int, [c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_f32, c_vp]),
     "hl_qk_norm_rope_store": (c_int, [c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_f32, c_vp,
                                       c_vp, c_int, c_vp, c_i64, c_vp, c_vp, c_vp]),
+    "hl_device_alloc": (c_int, [c_i64, c_vp]),
+    "hl_device_free": (c_int, [c_vp]),
+    "hl_ipc_get_handle": (c_int, [c_vp, c_vp]),
+    "hl_ipc_open_handle": (c_int, [c_vp, c_vp]),
+    "hl_ipc_close_handle": (c_int, [c_vp]),
+    "hl_allreduce_signal_bytes": (c_i64, []),
+    "hl_allreduce_add_rmsnorm": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_i64, c_f32,
+                                         c_vp, c_vp, c_i64, c_vp]),
     "hl_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_vp]),
     "hl_argmax": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp]),
     "hl_argmax_shard": (c_int, [c_vp, c_i64, c_int, c_int, c_i64, c_vp, c_vp, c_vp]),

@@ -42,6 +42,9 @@ class Config:
     # "external": every rank is already running (torchrun) and calls LLM(...) itself; rank 0
     # drives, the others serve the model-runner loop inside the constructor (gloo RPC).
     distributed_executor: str = "spawn"
+    # Tensor parallelism: reduce decode-sized o_proj / down_proj outputs with the fused NVLink
+    # all-reduce + add + RMSNorm kernel (False: NCCL all-reduce as the reference does).
+    custom_allreduce: bool = True
 
     def __post_init__(self):
         assert os.path.isdir(self.model)

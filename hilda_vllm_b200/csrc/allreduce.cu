@@ -1,0 +1,303 @@
+// Tensor-parallel all-reduce over NVLink peer memory, fused with the residual add + RMSNorm
+// that follows every all-reduce of the Qwen3 decoder.
+//
+// The reference sums the o_proj and down_proj partial outputs with an NCCL all-reduce
+// (mini_vllm/layers/linear.py:176-178) and then runs add + RMSNorm on the result
+// (post_attention_layernorm / the next layer's input_layernorm / the final norm,
+// mini_vllm/layers/layernorm.py:30-42, models/qwen3.py:150-157).  Here one kernel does both:
+// every rank keeps its partial sums in a buffer that the other ranks mapped through CUDA IPC,
+// a CTA meets the same CTA of every peer at a flag barrier (peer stores, local polling), then
+// reads its rows from all ranks' buffers over NVLink with plain loads, sums them in fp32 in
+// rank order (so every rank computes bit-identical results), rounds to bf16 (the all-reduce
+// result, as NCCL returns it) and applies the reference's add + RMSNorm arithmetic.
+//
+// Reuse: the o_proj and down_proj partials live in two different buffers that alternate, so
+// when a rank is at call k+2 (writing buffer A again with its GEMM), every peer has passed the
+// start barrier of call k+1 and therefore finished reading buffer A of call k (kernels of a
+// stream run in order) — one barrier per call is enough.  Flags carry a per-CTA epoch that
+// grows by one per call (compared with >=, so a peer running one call ahead is harmless).
+//
+// Every wait is bounded by time (globaltimer): on expiry the CTA records HL_AR_TIMEOUT in the
+// rank's error word, skips the peer reads (treats the partial sums as zero) and finishes the
+// add + RMSNorm; the host reads the word.
+// No multicast, no NVLS: peer memory is only touched by ordinary loads and stores.
+#include "hl_common.cuh"
+
+namespace hl {
+namespace {
+
+constexpr int kArMaxRanks = 8;
+constexpr int kArMaxBlocks = 128;
+constexpr int kArThreads = 128;
+
+struct ArParams {
+  const __nv_bfloat16* data[kArMaxRanks];  // rank p's partial sums [rows, hidden]
+  int* signal[kArMaxRanks];                // rank p's flags [kArMaxBlocks][kArMaxRanks]
+  int world;
+  int rank;
+  int rows;
+  int hidden;
+  __nv_bfloat16* residual;  // [rows, hidden], updated in place
+  const __nv_bfloat16* weight;
+  __nv_bfloat16* out;
+  int64_t out_stride;
+  float eps;
+  int* epochs;      // this rank's per-CTA call counters [kArMaxBlocks]
+  int* error_word;  // this rank's error bits
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void store_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int load_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// One warp per row, NV = hidden / 256 16-byte vectors per lane (lane + 32 c), the same layout
+// and summation order as the add + RMSNorm kernel, so one rank reproduces it bit for bit.
+template <int NV>
+__global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(const __grid_constant__ ArParams p) {
+  __shared__ int s_epoch;
+  __shared__ int s_ok;
+  const int blk = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  // ---------------------------------------------------------------- barrier with the peers
+  if (tid == 0) {
+    s_epoch = p.epochs[blk] + 1;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const int epoch = s_epoch;
+  if (tid < p.world && tid != p.rank) {
+    // The partials peers will read were written by an earlier kernel of this stream, so they are
+    // complete in this GPU's memory; the release store orders nothing else.
+    store_release_sys(p.signal[tid] + blk * kArMaxRanks + p.rank, epoch);
+    const int* mine = p.signal[p.rank] + blk * kArMaxRanks + tid;
+    const unsigned long long t0 = global_ns();
+    bool arrived = false;
+    for (uint32_t it = 0;; ++it) {
+      if (load_acquire_sys(mine) >= epoch) {
+        arrived = true;
+        break;
+      }
+      if ((it & 255u) == 255u && global_ns() - t0 > p.timeout_ns) break;
+    }
+    if (!arrived) {
+      s_ok = 0;
+      atomicOr(p.error_word, HL_AR_TIMEOUT);
+    }
+  }
+  __syncthreads();
+  const bool ok = s_ok != 0;
+  if (tid == 0) p.epochs[blk] = epoch;
+
+  // ---------------------------------------------------------------- rows of this CTA
+  constexpr int kRowsPerCta = kArThreads / 32;
+  // Ranks whose rows are loaded together: every load of a group is issued before any is used,
+  // so a group costs one NVLink round trip.
+  constexpr int RG = NV <= 4 ? 4 : (NV <= 8 ? 2 : 1);
+  for (int row = blk * kRowsPerCta + warp; row < p.rows; row += gridDim.x * kRowsPerCta) {
+    const int64_t base = int64_t(row) * p.hidden + 8 * lane;
+    uint4 rv[NV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) rv[c] = *reinterpret_cast<const uint4*>(p.residual + base + 256 * c);
+    float buf[NV][8];
+#pragma unroll
+    for (int c = 0; c < NV; ++c)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) buf[c][t] = 0.f;
+    if (ok) {
+      for (int r0 = 0; r0 < p.world; r0 += RG) {
+        uint4 a[RG][NV];
+#pragma unroll
+        for (int g = 0; g < RG; ++g)
+          if (r0 + g < p.world)
+#pragma unroll
+            for (int c = 0; c < NV; ++c)
+              // Peer partials change between calls at the same addresses: no L1 caching.
+              a[g][c] = __ldcv(reinterpret_cast<const uint4*>(p.data[r0 + g] + base + 256 * c));
+#pragma unroll
+        for (int g = 0; g < RG; ++g)
+          if (r0 + g < p.world)
+#pragma unroll
+            for (int c = 0; c < NV; ++c) {
+              const uint32_t w[4] = {a[g][c].x, a[g][c].y, a[g][c].z, a[g][c].w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                buf[c][2 * t] = __fadd_rn(buf[c][2 * t], bf16lo(w[t]));
+                buf[c][2 * t + 1] = __fadd_rn(buf[c][2 * t + 1], bf16hi(w[t]));
+              }
+            }
+      }
+    }
+    // x = bf16(all-reduce) + residual (fp32), residual := bf16(x)  (add_rms_forward order)
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      const uint32_t rw[4] = {rv[c].x, rv[c].y, rv[c].z, rv[c].w};
+      uint32_t ro[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        buf[c][2 * t] = __fadd_rn(bf16_round(buf[c][2 * t]), bf16lo(rw[t]));
+        buf[c][2 * t + 1] = __fadd_rn(bf16_round(buf[c][2 * t + 1]), bf16hi(rw[t]));
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(buf[c][2 * t], buf[c][2 * t + 1]);
+        ro[t] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      *reinterpret_cast<uint4*>(p.residual + base + 256 * c) = make_uint4(ro[0], ro[1], ro[2], ro[3]);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) ss = fmaf(buf[c][t], buf[c][t], ss);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / float(p.hidden) + p.eps);
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      const int col = 8 * (lane + 32 * c);
+      const uint4 wv = *reinterpret_cast<const uint4*>(p.weight + col);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float a = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t], inv)), bf16lo(ww[t]));
+        const float b = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t + 1], inv)), bf16hi(ww[t]));
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
+        o[t] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      *reinterpret_cast<uint4*>(p.out + int64_t(row) * p.out_stride + col) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace hl
+
+using namespace hl;
+
+extern "C" int hl_device_alloc(int64_t bytes, void** ptr_out) {
+  clear_error();
+  HL_CHECK_ARG(bytes > 0 && ptr_out, "hl_device_alloc: bad arguments");
+  cudaError_t e = cudaMalloc(ptr_out, size_t(bytes));
+  if (e == cudaSuccess) e = cudaMemset(*ptr_out, 0, size_t(bytes));
+  if (e != cudaSuccess) {
+    set_error("hl_device_alloc: %s", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
+  return HL_OK;
+}
+
+extern "C" int hl_device_free(void* ptr) {
+  clear_error();
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) {
+    set_error("hl_device_free: %s", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
+  return HL_OK;
+}
+
+extern "C" int hl_ipc_get_handle(void* dev_ptr, void* handle_out) {
+  clear_error();
+  HL_CHECK_ARG(dev_ptr && handle_out, "hl_ipc_get_handle: bad arguments");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, dev_ptr);
+  if (e != cudaSuccess) {
+    set_error("hl_ipc_get_handle: %s", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
+  memcpy(handle_out, &h, sizeof(h));
+  return HL_OK;
+}
+
+extern "C" int hl_ipc_open_handle(const void* handle, void** dev_ptr_out) {
+  clear_error();
+  HL_CHECK_ARG(handle && dev_ptr_out, "hl_ipc_open_handle: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    set_error("hl_ipc_open_handle: %s", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
+  return HL_OK;
+}
+
+extern "C" int hl_ipc_close_handle(void* dev_ptr) {
+  clear_error();
+  cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  if (e != cudaSuccess) {
+    set_error("hl_ipc_close_handle: %s", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
+  return HL_OK;
+}
+
+extern "C" int64_t hl_allreduce_signal_bytes(void) { return int64_t(kArMaxBlocks) * kArMaxRanks * sizeof(int); }
+
+extern "C" int hl_allreduce_add_rmsnorm(void* const* peer_data, void* const* peer_signal, int world, int rank,
+                                        int rows, int hidden, void* residual, const void* weight, void* out,
+                                        int64_t out_stride, float eps, int* epochs, int* error_word,
+                                        int64_t timeout_ns, void* stream) {
+  clear_error();
+  if (rows == 0) return HL_OK;
+  HL_CHECK_ARG(peer_data && peer_signal && residual && weight && out && epochs && error_word && rows > 0,
+               "hl_allreduce_add_rmsnorm: bad arguments");
+  HL_CHECK_ARG(world >= 1 && world <= kArMaxRanks && rank >= 0 && rank < world,
+               "hl_allreduce_add_rmsnorm: world must be 1..8");
+  HL_CHECK_ARG(hidden % 256 == 0 && hidden <= 8192, "hl_allreduce_add_rmsnorm: hidden must be a multiple of 256, <= 8192");
+  HL_CHECK_ARG(aligned16(residual) && aligned16(weight) && aligned16(out) && out_stride % 8 == 0,
+               "hl_allreduce_add_rmsnorm: 16-byte alignment required");
+  HL_CHECK_ARG(timeout_ns > 0, "hl_allreduce_add_rmsnorm: timeout must be positive");
+  ArParams prm;
+  memset(&prm, 0, sizeof(prm));
+  for (int r = 0; r < world; ++r) {
+    HL_CHECK_ARG(peer_data[r] && peer_signal[r] && aligned16(peer_data[r]),
+                 "hl_allreduce_add_rmsnorm: null or misaligned peer pointer");
+    prm.data[r] = static_cast<const __nv_bfloat16*>(peer_data[r]);
+    prm.signal[r] = static_cast<int*>(peer_signal[r]);
+  }
+  prm.world = world;
+  prm.rank = rank;
+  prm.rows = rows;
+  prm.hidden = hidden;
+  prm.residual = static_cast<__nv_bfloat16*>(residual);
+  prm.weight = static_cast<const __nv_bfloat16*>(weight);
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.out_stride = out_stride;
+  prm.eps = eps;
+  prm.epochs = epochs;
+  prm.error_word = error_word;
+  prm.timeout_ns = static_cast<unsigned long long>(timeout_ns);
+  const int groups = (rows + kArThreads / 32 - 1) / (kArThreads / 32);
+  const int blocks = groups < kArMaxBlocks ? groups : kArMaxBlocks;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define HL_AR_CASE(NV) \
+  case NV:             \
+    ar_add_rmsnorm_kernel<NV><<<blocks, kArThreads, 0, s>>>(prm); \
+    break;
+  switch (hidden / 256) {
+    HL_AR_CASE(1) HL_AR_CASE(2) HL_AR_CASE(3) HL_AR_CASE(4) HL_AR_CASE(5) HL_AR_CASE(6) HL_AR_CASE(8)
+    HL_AR_CASE(10) HL_AR_CASE(12) HL_AR_CASE(14) HL_AR_CASE(16) HL_AR_CASE(20) HL_AR_CASE(24) HL_AR_CASE(28)
+    HL_AR_CASE(32)
+    default:
+      set_error("hl_allreduce_add_rmsnorm: hidden=%d not supported", hidden);
+      return HL_ERR_UNSUPPORTED;
+  }
+#undef HL_AR_CASE
+  HL_CHECK_LAUNCH("hl_allreduce_add_rmsnorm");
+  return HL_OK;
+}

@@ -29,6 +29,7 @@ SOURCES = [
     "prefill_tc.cu",
     "pack_decode.cu",
     "layer_ops.cu",
+    "allreduce.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

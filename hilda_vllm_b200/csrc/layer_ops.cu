@@ -238,7 +238,30 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
   const __nv_bfloat16* x = logits + int64_t(row) * row_stride;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+  // 16-byte loads (8 logits) when the row allows it; each thread walks its indices in
+  // increasing order, so a strict '>' keeps the lowest index among equal values.
+  int head = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    head = vocab & ~7;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    for (int i = threadIdx.x; i < (head >> 3); i += blockDim.x) {
+      const uint4 v = __ldg(xv + i);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float a = bf16lo(w[t]), b = bf16hi(w[t]);
+        if (a > best) {
+          best = a;
+          bi = 8 * i + 2 * t;
+        }
+        if (b > best) {
+          best = b;
+          bi = 8 * i + 2 * t + 1;
+        }
+      }
+    }
+  }
+  for (int i = head + threadIdx.x; i < vocab; i += blockDim.x) {
     const float v = __bfloat162float(x[i]);
     if (v > best || (v == best && i < bi)) {
       best = v;

@@ -26,7 +26,9 @@ from hilda_vllm_b200 import kernels
 from hilda_vllm_b200.engine.decode_packer import DecodePacker, packet_capacity_bytes
 from hilda_vllm_b200.engine.scheduler import ScheduledSequence
 from hilda_vllm_b200.engine.sequence import Sequence
+from hilda_vllm_b200.layers import nvlink_allreduce
 from hilda_vllm_b200.layers.attention import Attention
+from hilda_vllm_b200.layers.nvlink_allreduce import NvlinkAllReduce
 from hilda_vllm_b200.layers.sampler import Sampler
 from hilda_vllm_b200.models.qwen3 import Qwen3ForCausalLM
 from hilda_vllm_b200.utils.context import get_context, reset_context, set_context
@@ -144,6 +146,12 @@ class ModelRunner:
         local = int(os.getenv("LOCAL_RANK", rank))
         torch.cuda.set_device(local)
         self.device = torch.device("cuda", local)
+        self.allreduce = None
+        if self.world_size > 1 and getattr(config, "custom_allreduce", True):
+            # Peer-mapped buffers for the decode batches (up to the largest CUDA-graph batch).
+            max_rows = graph_batch_sizes(config.max_num_seqs)[-1]
+            self.allreduce = NvlinkAllReduce(rank, self.world_size, max_rows, hf.hidden_size, self.device)
+            nvlink_allreduce.set_active(self.allreduce)
         default_dtype = torch.get_default_dtype()
         torch.set_default_dtype(torch.bfloat16)
         torch.set_default_device(self.device)
@@ -186,6 +194,11 @@ class ModelRunner:
         self.graphs = {}
         self.graph_pool = None
         torch.cuda.synchronize()
+        if self.allreduce is not None:
+            nvlink_allreduce.set_active(None)
+            dist.barrier()  # no peer may still read this rank's buffers
+            self.allreduce.close()
+            self.allreduce = None
         if self.world_size > 1 and dist.is_initialized():
             dist.destroy_process_group()
 
@@ -521,11 +534,15 @@ class ModelRunner:
                 gv["next_tokens"][:bs].copy_(toks.pin_memory(), non_blocking=True)
             if self.world_size > 1:
                 dist.broadcast(gv["next_tokens"][:bs], 0)
-        # One device->host copy of the step's tokens.
+        # One device->host copy of the step's tokens (and, under TP, of the all-reduce's error word).
         self.tokens_host[:bs].copy_(gv["next_tokens"][:bs], non_blocking=True)
         self.io_bytes["d2h"] += 8 * bs
+        if self.allreduce is not None:
+            self.allreduce.copy_error_word()
         self.copy_done.record()
         self.copy_done.synchronize()
+        if self.allreduce is not None:
+            self.allreduce.check_errors()
         reset_context()
         return self.tokens_host[:bs].tolist()
 

@@ -1,13 +1,17 @@
 """Tensor-parallel linear layers (mini_vllm/layers/linear.py:21-179).
 
 Same classes, sharding and weight loaders as the reference; the GEMMs are cuBLAS (F.linear).
-RowParallelLinear sums partial outputs with an NCCL all-reduce when tp > 1 — together with
-down_proj these are the only collectives of the decode step.
+RowParallelLinear sums partial outputs across ranks when tp > 1 (o_proj and down_proj: the only
+collectives of the decode step): for decode-sized batches it leaves them in an NVLink
+peer-mapped buffer that the following RMSNorm reduces (layers/nvlink_allreduce.py), otherwise it
+runs the reference's NCCL all-reduce.
 """
 import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 from torch import nn
+
+from hilda_vllm_b200.layers import nvlink_allreduce
 
 
 def divide(numerator, denominator):
@@ -105,7 +109,19 @@ class RowParallelLinear(LinearBase):
         shard = param.data.size(self.tp_dim)
         param.data.copy_(loaded_weight.narrow(self.tp_dim, self.tp_rank * shard, shard))
 
+    # Which NVLink all-reduce buffer this layer's partial output goes to (set by the model:
+    # o_proj 0, down_proj 1); None keeps the NCCL all-reduce.
+    ar_slot: int | None = None
+
     def forward(self, x):
+        if self.tp_size > 1 and self.ar_slot is not None:
+            ar = nvlink_allreduce.active()
+            if ar is not None and x.dim() == 2 and ar.fits(x.shape[0]) and self.bias is None:
+                # Partial sums straight into the peer-mapped buffer; the next RMSNorm reduces
+                # them (hl_allreduce_add_rmsnorm).
+                y = ar.output(self.ar_slot, x.shape[0])
+                torch.matmul(x, self.weight.t(), out=y)
+                return y
         y = F.linear(x, self.weight, self.bias if self.tp_rank == 0 else None)
         if self.tp_size > 1:
             dist.all_reduce(y)

@@ -1,0 +1,151 @@
+"""Tensor-parallel all-reduce over NVLink peer memory, fused with the add + RMSNorm after it.
+
+The reference sums the row-parallel partial outputs (o_proj, down_proj) with
+dist.all_reduce (mini_vllm/layers/linear.py:176-178) and then runs add + RMSNorm
+(layers/layernorm.py:30-42).  With this module active, RowParallelLinear writes its partial
+output straight into a buffer every peer has mapped (CUDA IPC), and the next RMSNorm runs
+hl_allreduce_add_rmsnorm: one kernel that meets the peers at a flag barrier, reads the rows of
+all ranks over NVLink, sums them in rank order and applies the add + RMSNorm.  Two buffers
+alternate (o_proj -> slot 0, down_proj -> slot 1), which is what lets the kernel use a single
+barrier per call.  Batches larger than the buffers (prefill) keep NCCL.
+
+All ranks must make the same calls in the same order; the decision to use the buffers depends
+only on the row count, which is identical on every rank.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from hilda_vllm_b200 import _lib
+from hilda_vllm_b200.kernels import check
+
+_ACTIVE: "NvlinkAllReduce | None" = None
+HANDLE_BYTES = 64  # sizeof(cudaIpcMemHandle_t)
+MAX_BLOCKS = 128   # per-CTA flag slots / call counters in the kernel
+
+
+def active() -> "NvlinkAllReduce | None":
+    return _ACTIVE
+
+
+def set_active(ar: "NvlinkAllReduce | None") -> None:
+    global _ACTIVE
+    _ACTIVE = ar
+
+
+class _DeviceArray:
+    """Exposes a raw device allocation to torch.as_tensor (__cuda_array_interface__ v3)."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
+
+
+class NvlinkAllReduce:
+
+    def __init__(self, rank: int, world: int, max_rows: int, hidden: int, device: torch.device,
+                 group=None, timeout_s: float = 20.0):
+        assert 1 <= world <= 8 and hidden % 256 == 0 and hidden <= 8192
+        self.lib = _lib.load()
+        self.rank, self.world, self.max_rows, self.hidden = rank, world, max_rows, hidden
+        self.device = device
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.stats = {"calls": 0}
+        nbytes = max_rows * hidden * 2
+        sig_bytes = int(self.lib.hl_allreduce_signal_bytes())
+        self._owned: list[int] = []
+        self._opened: list[int] = []
+        own = [self._alloc(nbytes), self._alloc(nbytes), self._alloc(sig_bytes)]
+        self._epochs = self._alloc(MAX_BLOCKS * 4)
+        self._error = self._alloc(256)
+        handles = b""
+        for ptr in own:
+            h = ctypes.create_string_buffer(HANDLE_BYTES)
+            check(self.lib.hl_ipc_get_handle(ctypes.c_void_p(ptr), h), "hl_ipc_get_handle")
+            handles += h.raw
+        gathered: list = [None] * world
+        if world > 1:
+            dist.all_gather_object(gathered, handles, group=group)
+        else:
+            gathered[0] = handles
+        ptrs = [[0] * world for _ in range(3)]  # [data0, data1, signal][rank]
+        for p in range(world):
+            for i in range(3):
+                if p == rank:
+                    ptrs[i][p] = own[i]
+                    continue
+                out = ctypes.c_void_p()
+                blob = gathered[p][i * HANDLE_BYTES:(i + 1) * HANDLE_BYTES]
+                check(self.lib.hl_ipc_open_handle(blob, ctypes.byref(out)), "hl_ipc_open_handle")
+                self._opened.append(out.value)
+                ptrs[i][p] = out.value
+        arr = ctypes.c_void_p * world
+        self._peer_data = [arr(*ptrs[0]), arr(*ptrs[1])]
+        self._peer_signal = arr(*ptrs[2])
+        self._buf_ptrs = own[:2]
+        self.buffers = [torch.as_tensor(_DeviceArray(p, (max_rows, hidden), "<i2"), device=device).view(torch.bfloat16)
+                        for p in own[:2]]
+        self.error_host = torch.zeros(1, dtype=torch.int32, pin_memory=True, device="cpu")
+        self._error_dev = torch.as_tensor(_DeviceArray(self._error, (1,), "<i4"), device=device)
+
+    def _alloc(self, nbytes: int) -> int:
+        ptr = ctypes.c_void_p()
+        check(self.lib.hl_device_alloc(nbytes, ctypes.byref(ptr)), "hl_device_alloc")
+        self._owned.append(ptr.value)
+        return ptr.value
+
+    # ------------------------------------------------------------------ use
+    def fits(self, rows: int) -> bool:
+        return 0 < rows <= self.max_rows
+
+    def output(self, slot: int, rows: int) -> torch.Tensor:
+        """Where the row-parallel GEMM of `slot` writes its partial sums for `rows` rows."""
+        return self.buffers[slot][:rows]
+
+    def slot_of(self, t: torch.Tensor) -> int | None:
+        """The slot whose buffer `t` is (from its first row), else None."""
+        if t.dim() != 2 or not t.is_contiguous():
+            return None
+        ptr = t.data_ptr()
+        for i, base in enumerate(self._buf_ptrs):
+            if ptr == base:
+                return i
+        return None
+
+    def add_rmsnorm(self, slot: int, rows: int, residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                    out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """out = RMSNorm(all_reduce(partials) + residual) with residual updated in place."""
+        assert residual.is_contiguous() and residual.shape == (rows, self.hidden)
+        if out is None:
+            out = torch.empty_like(residual)
+        stream = torch.cuda.current_stream(residual.device).cuda_stream
+        self.stats["calls"] += 1
+        check(self.lib.hl_allreduce_add_rmsnorm(
+            ctypes.addressof(self._peer_data[slot]), ctypes.addressof(self._peer_signal), self.world, self.rank, rows,
+            self.hidden, residual.data_ptr(), weight.data_ptr(), out.data_ptr(), out.stride(0), float(eps),
+            ctypes.c_void_p(self._epochs), ctypes.c_void_p(self._error), self.timeout_ns, stream),
+            "hl_allreduce_add_rmsnorm")
+        return out, residual
+
+    def copy_error_word(self) -> None:
+        """Queues a device->host copy of the error word on the current stream."""
+        self.error_host.copy_(self._error_dev, non_blocking=True)
+
+    def check_errors(self) -> None:
+        """Raises if a previous call timed out waiting for a peer (after copy_error_word and a sync)."""
+        if int(self.error_host[0]):
+            raise RuntimeError("NVLink all-reduce: a peer rank did not arrive within the timeout "
+                               f"(error word {int(self.error_host[0])})")
+
+    def close(self) -> None:
+        self.buffers = []
+        self._error_dev = None
+        for ptr in self._opened:
+            self.lib.hl_ipc_close_handle(ctypes.c_void_p(ptr))
+        self._opened = []
+        for ptr in self._owned:
+            self.lib.hl_device_free(ctypes.c_void_p(ptr))
+        self._owned = []

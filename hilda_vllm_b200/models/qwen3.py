@@ -39,6 +39,7 @@ class Qwen3Attention(nn.Module):
         self.rms_norm_eps = rms_norm_eps
         self.qkv_proj = QKVParallelLinear(hidden_size, self.head_dim, num_heads, num_kv_heads, bias=False)
         self.o_proj = RowParallelLinear(num_heads * self.head_dim, hidden_size, bias=False)
+        self.o_proj.ar_slot = 0
         self.rotary_emb = get_rope(self.head_dim, rotary_dim=self.head_dim, max_position=max_position,
                                    base=rope_theta, rope_scaling=rope_scaling)
         self.attn = Attention(self.num_heads, self.head_dim, self.scaling, self.num_kv_heads)
@@ -63,6 +64,7 @@ class Qwen3MLP(nn.Module):
         super().__init__()
         self.gate_up_proj = MergedColumnParallelLinear(hidden_size, [intermediate_size] * 2, bias=False)
         self.down_proj = RowParallelLinear(intermediate_size, hidden_size, bias=False)
+        self.down_proj.ar_slot = 1
         assert hidden_act == "silu"
         self.act_fn = SiluAndMul()
 

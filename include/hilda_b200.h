@@ -291,6 +291,36 @@ int hl_argmax(const void* logits, int64_t row_stride, int rows, int vocab, int64
 int hl_argmax_shard(const void* logits, int64_t row_stride, int rows, int vocab, int64_t index_offset,
                     int64_t* out_tokens, float* out_values, void* stream);
 
+/* ------------------------------------------------------------------------------------
+ * Tensor-parallel all-reduce over NVLink peer memory fused with add + RMSNorm.
+ * Replaces dist.all_reduce after o_proj / down_proj (mini_vllm/layers/linear.py:176-178)
+ * together with the add + RMSNorm that follows it (layers/layernorm.py:30-42).
+ * Each rank allocates its partial-sum buffers and a signal area (hl_device_alloc, zeroed),
+ * shares them with hl_ipc_get_handle / hl_ipc_open_handle, and then, on every rank, with
+ * the same rows and the same order of calls:
+ *   x = bf16(sum over ranks p in order 0..world-1 of peer_data[p][row, :])   (fp32 sum)
+ *   x = x + residual (fp32); residual := bf16(x); out = bf16(bf16(x * rsqrt(mean(x^2)+eps)) * w)
+ * peer_data / peer_signal are host arrays of world device pointers (this rank's own at index
+ * rank); signal areas hold hl_allreduce_signal_bytes() bytes; epochs is this rank's int32
+ * [128] call counter array (zeroed), error_word this rank's int32.  hidden % 256 == 0, <= 8192.
+ * Partial-sum buffers must alternate between consecutive calls (two buffers), which makes one
+ * barrier per call sufficient.  A peer that does not arrive within timeout_ns sets
+ * HL_AR_TIMEOUT in *error_word and the call treats the partial sums as zero instead of hanging.
+ * ---------------------------------------------------------------------------------- */
+#define HL_AR_TIMEOUT 1
+
+int hl_device_alloc(int64_t bytes, void** ptr_out);
+int hl_device_free(void* ptr);
+/* cudaIpcMemHandle_t is 64 bytes. */
+int hl_ipc_get_handle(void* dev_ptr, void* handle_out);
+int hl_ipc_open_handle(const void* handle, void** dev_ptr_out);
+int hl_ipc_close_handle(void* dev_ptr);
+int64_t hl_allreduce_signal_bytes(void);
+int hl_allreduce_add_rmsnorm(void* const* peer_data, void* const* peer_signal, int world, int rank,
+                             int rows, int hidden, void* residual, const void* weight, void* out,
+                             int64_t out_stride, float eps, int* epochs, int* error_word,
+                             int64_t timeout_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

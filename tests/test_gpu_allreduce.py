@@ -1,0 +1,151 @@
+"""The fused NVLink all-reduce + add + RMSNorm (hl_allreduce_add_rmsnorm).
+
+* one rank: the kernel reduces to add + RMSNorm and must equal hl_rmsnorm bit for bit;
+* a peer that never arrives (its flag is never set): the bounded wait expires, the error word
+  says HL_AR_TIMEOUT, the context stays usable;
+* two GPUs (skipped with fewer): two processes, several alternating calls, outputs bit-identical
+  on both ranks and equal to bf16(sum of partials) + add + RMSNorm.
+"""
+import ctypes
+import os
+import socket
+
+import pytest
+import torch
+
+from hilda_vllm_b200 import _lib, kernels
+from hilda_vllm_b200.layers.nvlink_allreduce import NvlinkAllReduce
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _reference(partials, residual, weight, eps):
+    """bf16(fp32 sum in rank order) then the add + RMSNorm kernel."""
+    acc = torch.zeros_like(partials[0], dtype=torch.float32)
+    for p in partials:
+        acc = acc + p.float()
+    res = residual.clone()
+    y, res = kernels.rmsnorm(acc.bfloat16(), weight, eps, residual=res)
+    return y, res
+
+
+@pytest.mark.parametrize("rows,hidden", [(1, 1024), (256, 1024), (300, 4096)])
+def test_single_rank_equals_add_rmsnorm(rows, hidden):
+    g = torch.Generator().manual_seed(rows + hidden)
+    ar = NvlinkAllReduce(0, 1, 512, hidden, torch.device(DEV))
+    try:
+        w = (torch.rand(hidden, generator=g) + 0.5).bfloat16().to(DEV)
+        for slot in (0, 1, 0):
+            x = torch.randn(rows, hidden, generator=g).bfloat16().to(DEV)
+            res = torch.randn(rows, hidden, generator=g).bfloat16().to(DEV)
+            ar.output(slot, rows).copy_(x)
+            want_y, want_r = _reference([x], res, w, 1e-6)
+            got_y, got_r = ar.add_rmsnorm(slot, rows, res, w, 1e-6)
+            torch.cuda.synchronize()
+            assert torch.equal(got_y.view(torch.int16), want_y.view(torch.int16))
+            assert torch.equal(got_r.view(torch.int16), want_r.view(torch.int16))
+        ar.copy_error_word()
+        torch.cuda.synchronize()
+        ar.check_errors()
+    finally:
+        ar.close()
+
+
+def test_missing_peer_times_out_with_error_word():
+    """world=2 in one process: the 'peer' signal area is a local buffer nobody writes, so the
+    wait for rank 1 must give up after the (50 ms) limit and report it."""
+    lib = _lib.load()
+    rows, hidden = 4, 1024
+    data = torch.randn(rows, hidden, device=DEV).bfloat16()
+    sig_bytes = int(lib.hl_allreduce_signal_bytes())
+    sig = [torch.zeros(sig_bytes // 4, dtype=torch.int32, device=DEV) for _ in range(2)]
+    epochs = torch.zeros(128, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    res = torch.randn(rows, hidden, device=DEV).bfloat16()
+    out = torch.empty_like(res)
+    w = torch.ones(hidden, device=DEV).bfloat16()
+    arr = ctypes.c_void_p * 2
+    peer_data = arr(data.data_ptr(), data.data_ptr())
+    peer_sig = arr(sig[0].data_ptr(), sig[1].data_ptr())
+    stream = torch.cuda.current_stream().cuda_stream
+    kernels.check(lib.hl_allreduce_add_rmsnorm(ctypes.addressof(peer_data), ctypes.addressof(peer_sig), 2, 0, rows,
+                                               hidden, res.data_ptr(), w.data_ptr(), out.data_ptr(), out.stride(0),
+                                               1e-6, epochs.data_ptr(), err.data_ptr(), 50_000_000, stream),
+                  "hl_allreduce_add_rmsnorm")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1  # HL_AR_TIMEOUT
+    # Rank 0 announced itself in the peer's area; the context is still usable.
+    assert int(sig[1][0 * 8 + 0].item()) == 1
+    assert torch.isfinite(out.float()).all()
+    assert float((torch.ones(3, device=DEV) * 2).sum()) == 6.0
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                device_id=torch.device("cuda", rank))
+        hidden, rows = 1024, 256
+        ar = NvlinkAllReduce(rank, world, 512, hidden, torch.device("cuda", rank), timeout_s=10.0)
+        w = (torch.arange(hidden, device="cuda") % 7 + 1).bfloat16() / 4
+        results = []
+        for call in range(6):
+            slot = call % 2
+            g = torch.Generator().manual_seed(1000 * call + rank)
+            x = torch.randn(rows, hidden, generator=g).bfloat16().cuda()
+            g2 = torch.Generator().manual_seed(77 + call)
+            res = torch.randn(rows, hidden, generator=g2).bfloat16().cuda()
+            ar.output(slot, rows).copy_(x)
+            y, r = ar.add_rmsnorm(slot, rows, res, w, 1e-6)
+            parts = [torch.empty_like(x) for _ in range(world)]
+            dist.all_gather(parts, x)  # every rank's partials, to build the reference
+            res2 = torch.randn(rows, hidden, generator=torch.Generator().manual_seed(77 + call)).bfloat16().cuda()
+            want_y, want_r = _reference(parts, res2, w, 1e-6)
+            results.append((torch.equal(y.view(torch.int16), want_y.view(torch.int16)),
+                            torch.equal(r.view(torch.int16), want_r.view(torch.int16)),
+                            int(y.view(torch.int16).long().sum().item())))
+        ar.copy_error_word()
+        torch.cuda.synchronize()
+        dist.barrier()
+        q.put((rank, results, int(ar.error_host[0])))
+        ar.close()
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, repr(e), -1))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_ranks_bit_exact_and_identical():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    env_backup = os.environ.get("NCCL_NVLS_ENABLE")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+        for p in procs:
+            p.start()
+        out = [q.get(timeout=300) for _ in range(2)]
+        for p in procs:
+            p.join(timeout=60)
+    finally:
+        if env_backup is None:
+            os.environ.pop("NCCL_NVLS_ENABLE", None)
+        else:
+            os.environ["NCCL_NVLS_ENABLE"] = env_backup
+    out.sort()
+    for rank, results, err in out:
+        assert err == 0, (rank, results)
+        assert all(ok_y and ok_r for ok_y, ok_r, _ in results), (rank, results)
+    assert [c for *_, c in out[0][1]] == [c for *_, c in out[1][1]]  # identical on both ranks
