@@ -45,6 +45,13 @@ class Config:
     # Tensor parallelism: reduce decode-sized o_proj / down_proj outputs with the fused NVLink
     # all-reduce + add + RMSNorm kernel (False: NCCL all-reduce as the reference does).
     custom_allreduce: bool = True
+    # Overlap the host side of decode step k+1 with the GPU running step k while no running
+    # sequence can stop on EOS (see LLMEngine.step); False runs every step synchronously.
+    async_decode: bool = True
+    # The reference appends a padding row's token to a sequence preempted as a victim after it
+    # was put in the same decode batch (scheduler.py:326-340); True drops that token instead
+    # (correct outputs; block decisions then differ from the reference in that case).
+    drop_preempted_decode_token: bool = False
 
     def __post_init__(self):
         assert os.path.isdir(self.model)

@@ -11,7 +11,7 @@ from collections import deque
 import numpy as np
 import xxhash
 
-from hilda_vllm_b200.engine.sequence import Sequence
+from hilda_vllm_b200.engine.sequence import PLACEHOLDER, Sequence
 
 
 class Block:
@@ -38,6 +38,7 @@ class BlockManager:
         self.block_size = block_size
         self.blocks: list[Block] = [Block(i) for i in range(num_blocks)]
         self.hash_to_block_id: dict[int, int] = {}
+        self.deferred_hashes: list[tuple] = []  # (seq, page index, block id)
         self.free_block_ids: deque[int] = deque(range(num_blocks))
         self.used_block_ids: set[int] = set()
 
@@ -115,7 +116,30 @@ class BlockManager:
         elif phase == 0 and last.hash == -1:
             # The last page just filled up: register it in the prefix cache.
             token_ids = seq.block(seq.num_blocks - 1)
-            prefix = self.blocks[table[-2]].hash if len(table) > 1 else -1
-            h = self.compute_hash(token_ids, prefix)
-            last.update(h, token_ids)
-            self.hash_to_block_id[h] = last.block_id
+            if PLACEHOLDER in token_ids:
+                # Its last token is still on the GPU (overlapped decode): hash it once known.
+                self.deferred_hashes.append((seq, seq.num_blocks - 1, last.block_id))
+                return
+            self._register_full_block(table, len(table) - 1, token_ids)
+
+    def _register_full_block(self, table: list[int], i: int, token_ids: list[int]) -> None:
+        block = self.blocks[table[i]]
+        prefix = self.blocks[table[i - 1]].hash if i > 0 else -1
+        h = self.compute_hash(token_ids, prefix)
+        block.update(h, token_ids)
+        self.hash_to_block_id[h] = block.block_id
+
+    def resolve_deferred(self) -> None:
+        """Registers the pages whose hashing waited for a token read back from the GPU (the same
+        hash may_append computes, one step later); pages no longer owned are dropped."""
+        keep = []
+        for seq, i, block_id in self.deferred_hashes:
+            table = seq.block_table
+            if i >= len(table) or table[i] != block_id or self.blocks[block_id].hash != -1:
+                continue
+            token_ids = seq.block(i)
+            if PLACEHOLDER in token_ids:
+                keep.append((seq, i, block_id))
+                continue
+            self._register_full_block(table, i, token_ids)
+        self.deferred_hashes = keep

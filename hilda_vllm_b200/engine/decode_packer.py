@@ -12,6 +12,10 @@ what the device holds, so that each step it only emits events for slots whose st
   same owner, block table grew              -> ROW (tail only)   (_sync_decode_block_table_row)
   new owner / length not previous+1 / token the device does not hold -> SCALARS
 
+The device holds slot i's input token when the previous step sampled it there: either the host
+read it back (note_sampled) or the step was launched without reading it yet (note_launched,
+overlapped decode), in which case the host's copy of the sequence ends with PLACEHOLDER.
+
 Everything is serialised into one packet (header, events, block-id pool) that the runner
 copies to the device with a single host->device copy.  The block-table decisions are the
 reference's, so the device buffers end up bit-identical to the reference's graph buffers.
@@ -20,7 +24,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from hilda_vllm_b200.engine.sequence import SequenceStatus
+from hilda_vllm_b200.engine.sequence import PLACEHOLDER, SequenceStatus
 
 EV_SCALARS = 1
 EV_ROW = 2
@@ -71,6 +75,34 @@ class DecodePacker:
     def forget_tokens(self) -> None:
         self.token = [_UNKNOWN] * self.max_bs
 
+    def note_launched(self, batch: int, scheduled_seqs) -> None:
+        """Records that a decode step was launched whose sampled tokens stay on the device: slot
+        i's next_tokens then holds the token at position len(seq) of the sequence it ran (the host
+        learns its value later)."""
+        for i in range(batch):
+            seq = scheduled_seqs[i].seq
+            self.token[i] = _UNKNOWN if seq is None else ("dev", seq.seq_id, seq.num_tokens)
+        for i in range(batch, self.max_bs):
+            self.token[i] = _UNKNOWN
+
+    def _device_holds(self, i: int, seq) -> bool:
+        tok = self.token[i]
+        if isinstance(tok, tuple):
+            return tok == ("dev", seq.seq_id, seq.num_tokens - 1)
+        return tok is not _UNKNOWN and seq.last_token != PLACEHOLDER and tok == seq.last_token
+
+    def needs_host_tokens(self, scheduled_seqs) -> bool:
+        """True when building this step's packet would need a token the host has not read back
+        yet (a sequence whose last token is still on the GPU, in another slot or for an earlier
+        owner of its slot).  build() must not be called then."""
+        for i, sched in enumerate(scheduled_seqs):
+            seq = sched.seq
+            if seq is None or seq.status == SequenceStatus.WAITING or seq.last_token != PLACEHOLDER:
+                continue
+            if self.owner[i] != seq.seq_id or self.ctx[i] + 1 != seq.num_tokens or not self._device_holds(i, seq):
+                return True
+        return False
+
     def build(self, scheduled_seqs, graph_bs: int) -> int:
         """Serialises the packet for this step into self.buffer; returns its size in bytes."""
         bs = len(scheduled_seqs)
@@ -110,7 +142,9 @@ class DecodePacker:
                 row_count = n - row_start
                 pool_off = len(pool)
                 pool.extend(table[row_start:])
-            if not same_owner or ctx[i] + 1 != length or token[i] is _UNKNOWN or token[i] != seq.last_token:
+            if not same_owner or ctx[i] + 1 != length or not self._device_holds(i, seq):
+                if seq.last_token == PLACEHOLDER:
+                    raise RuntimeError("decode packet needs a token that is still on the GPU")
                 flags |= EV_SCALARS
             if flags:
                 events.append((flags, i, length, n, seq.seq_id, seq.last_token, row_start, row_count, pool_off, 0))

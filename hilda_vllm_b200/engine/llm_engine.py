@@ -18,7 +18,7 @@ import torch.multiprocessing as mp
 from hilda_vllm_b200.config import Config
 from hilda_vllm_b200.engine.model_runner import ModelRunner
 from hilda_vllm_b200.engine.scheduler import Scheduler
-from hilda_vllm_b200.engine.sequence import Sequence
+from hilda_vllm_b200.engine.sequence import PLACEHOLDER, Sequence
 from hilda_vllm_b200.sampling_params import SamplingParams
 from hilda_vllm_b200.utils.tokenizer import load_tokenizer
 
@@ -62,6 +62,7 @@ class LLMEngine:
         self.tokenizer = load_tokenizer(config.model, config.hf_config)
         config.eos = self.tokenizer.eos_token_id if self.tokenizer.eos_token_id is not None else -1
         self.scheduler = Scheduler(config)
+        self._inflight = None
         self.last_generate_stats = None
         self.last_step_diagnostics = None
         atexit.register(self.exit)
@@ -81,10 +82,54 @@ class LLMEngine:
         self.scheduler.add(seq)
         return seq
 
+    # ------------------------------------------------------------------ stepping
+    # Overlapped decode (config.async_decode, default on): while every running sequence stops
+    # by length (ignore_eos, or no EOS token), a greedy decode step is launched before the
+    # previous one's tokens are read back; its sequences get PLACEHOLDER tokens that the next
+    # step() fills.  The host then schedules and packs step k+1 while the GPU runs step k.  Any
+    # other step (prefill, sampling, EOS possible, a packet that needs a token still on the GPU)
+    # first drains the step in flight and runs synchronously, as the reference does.
+    def _drain(self) -> list:
+        """Reads back the step in flight, fills its placeholders, returns its finished outputs."""
+        if self._inflight is None:
+            return []
+        handle, pending, finished = self._inflight
+        self._inflight = None
+        self.scheduler.resolve_tokens(pending, self.model_runner.collect_decode(handle))
+        return [(seq.seq_id, seq.completion_token_ids) for seq in finished]
+
+    def _step_result(self, outputs, num_prefill_tokens, num_decode_tokens):
+        return outputs, num_prefill_tokens, num_decode_tokens, 0, 0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0
+
     def step(self):
+        if self.config.async_decode and self._inflight is not None and not self.scheduler.eos_cannot_stop():
+            early = self._drain()
+        else:
+            early = []
+        if self.scheduler.is_finished():
+            return self._step_result(early + self._drain(), 0, 0)
         seqs, is_prefill = self.scheduler.schedule()
         if not seqs:
-            return [], False, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0
+            return self._step_result(early + self._drain(), 0, 0)
+        if (self.config.async_decode and not is_prefill and self.scheduler.eos_cannot_stop()
+                and all(s.is_padding or s.seq.greedy for s in seqs)):
+            if not self.model_runner.can_launch_decode(seqs):
+                early += self._drain()
+            handle = self.model_runner.launch_decode(seqs)
+            self.last_step_diagnostics = {
+                "running": len(self.scheduler.running),
+                "waiting": len(self.scheduler.waiting),
+                "decode_batch": self.model_runner.last_decode_batch_info or {},
+            }
+            pending, finished = self.scheduler.postprocess_launched(seqs)
+            early += self._drain()
+            self._inflight = (handle, pending, finished)
+            return self._step_result(early, 0, len(pending))
+        early += self._drain()
+        outputs, n_pre, n_dec = self._step_sync(seqs, is_prefill)
+        return self._step_result(early + outputs, n_pre, n_dec)
+
+    def _step_sync(self, seqs, is_prefill):
         token_ids = self.model_runner.run(seqs, is_prefill)
         self.last_step_diagnostics = {
             "running": len(self.scheduler.running),
@@ -106,10 +151,10 @@ class LLMEngine:
         else:
             num_prefill_tokens = 0
             num_decode_tokens = sum(1 for s in seqs if not s.is_padding)
-        return outputs, num_prefill_tokens, num_decode_tokens, 0, 0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0
+        return outputs, num_prefill_tokens, num_decode_tokens
 
     def is_finished(self):
-        return self.scheduler.is_finished()
+        return self.scheduler.is_finished() and self._inflight is None
 
     def _add_sequences(self, prompts, sampling_params) -> list[Sequence]:
         if not isinstance(sampling_params, list):
@@ -129,6 +174,8 @@ class LLMEngine:
             self._update_generate_stats(stats, n_pre, n_dec, perf_counter() - t, self.last_step_diagnostics)
             for seq in seqs:
                 done = seq.completion_token_ids
+                if PLACEHOLDER in done:  # tokens still on the GPU are emitted next step
+                    done = done[:done.index(PLACEHOLDER)]
                 prev = emitted[seq.seq_id]
                 if len(done) <= prev:
                     continue

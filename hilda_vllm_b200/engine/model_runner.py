@@ -352,10 +352,16 @@ class ModelRunner:
         cap = packet_capacity_bytes(max_bs, mb)
         cap = (cap + 15) & ~15
         self.packet_dev = torch.zeros(cap, dtype=torch.uint8, device=dev)
-        self.packet_host = torch.zeros(cap, dtype=torch.uint8, device="cpu", pin_memory=True)
+        # Two pinned packet and token buffers: an overlapped decode step (launch_decode) uses one
+        # while the previous step's copies may still be pending on the other.
+        self.packet_bufs = [torch.zeros(cap, dtype=torch.uint8, device="cpu", pin_memory=True) for _ in range(2)]
+        self.tokens_bufs = [torch.zeros(max_bs, dtype=torch.int64, device="cpu", pin_memory=True) for _ in range(2)]
+        self.done_events = [torch.cuda.Event(), torch.cuda.Event()]
+        self.launch_parity = 0
+        self.packet_host = self.packet_bufs[0]
+        self.tokens_host = self.tokens_bufs[0]
         self.packer = DecodePacker(max_bs, mb, self.packet_host.numpy())
-        self.tokens_host = torch.zeros(max_bs, dtype=torch.int64, device="cpu", pin_memory=True)
-        self.copy_done = torch.cuda.Event()
+        self.copy_done = self.done_events[0]
         hq = hf.num_attention_heads // self.world_size
         d = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
         self.decode_workspace = kernels.make_decode_workspace(max_bs, hq, d, mb, self.block_size, dev)
@@ -450,6 +456,7 @@ class ModelRunner:
             return self.call("execute_prefill", meta, len(scheduled_seqs), rows, samp)
         bs = len(scheduled_seqs)
         graph_bs = self._decode_graph_batch_size(bs)
+        self.packer.buffer = self.packet_host.numpy()
         nbytes = self.packer.build(scheduled_seqs, graph_bs)
         real = [i for i, s in enumerate(scheduled_seqs) if not s.is_padding]
         samp = sampling_settings([scheduled_seqs[i].seq for i in real])
@@ -463,6 +470,59 @@ class ModelRunner:
         for i in real:
             out[i] = tokens[i]
         return out
+
+    # ------------------------------------------------------------------ overlapped decode
+    # A greedy decode step launched without waiting for its tokens: the argmax leaves them in
+    # next_tokens on the device (where the next step's pack kernel reads them) and one
+    # asynchronous device->host copy brings them to a pinned buffer that collect_decode() reads
+    # after the next step has been launched.
+    def can_launch_decode(self, scheduled_seqs) -> bool:
+        return all(s.is_padding or s.seq.greedy for s in scheduled_seqs) and \
+            not self.packer.needs_host_tokens(scheduled_seqs)
+
+    @torch.inference_mode()
+    def launch_decode(self, scheduled_seqs: list[ScheduledSequence]):
+        bs = len(scheduled_seqs)
+        graph_bs = self._decode_graph_batch_size(bs)
+        par = self.launch_parity
+        self.launch_parity ^= 1
+        self.packer.buffer = self.packet_bufs[par].numpy()
+        nbytes = self.packer.build(scheduled_seqs, graph_bs)
+        real = sum(1 for s in scheduled_seqs if not s.is_padding)
+        self.last_decode_batch_info = {"scheduled_bs": bs, "graph_bs": graph_bs, "active_seqs": real,
+                                       "padded_slots": bs - real, "pack_events": self.packer.last_num_events}
+        self.call("execute_decode_launch", self.packet_bufs[par][:nbytes].numpy(), bs, graph_bs, par)
+        self.packer.note_launched(bs, scheduled_seqs)
+        return par, bs
+
+    @torch.inference_mode()
+    def execute_decode_launch(self, packet: np.ndarray, bs: int, graph_bs: int, par: int):
+        nbytes = packet.nbytes
+        host = self.packet_bufs[par].numpy()
+        if packet.ctypes.data != host.ctypes.data:
+            host[:nbytes] = packet
+        self.packet_dev[:nbytes].copy_(self.packet_bufs[par][:nbytes], non_blocking=True)
+        self.io_bytes["h2d"] += nbytes
+        if self.recording is not None:
+            self.recording.append(self.packet_dev[:nbytes].clone())
+        if graph_bs in self.graphs:
+            self.graphs[graph_bs].replay()
+        else:
+            self._ensure_logits_buf(graph_bs)
+            self._decode_body(graph_bs, greedy=True)
+        self.tokens_bufs[par][:bs].copy_(self.graph_vars["next_tokens"][:bs], non_blocking=True)
+        self.io_bytes["d2h"] += 8 * bs
+        if self.allreduce is not None:
+            self.allreduce.copy_error_word()
+        self.done_events[par].record()
+        reset_context()
+
+    def collect_decode(self, handle) -> list[int]:
+        par, bs = handle
+        self.done_events[par].synchronize()
+        if self.allreduce is not None:
+            self.allreduce.check_errors()
+        return self.tokens_bufs[par][:bs].tolist()
 
     def _sample_rows(self, logits: torch.Tensor, samp) -> list[int]:
         if samp is None:

@@ -16,7 +16,7 @@ from collections import deque
 from dataclasses import dataclass
 
 from hilda_vllm_b200.engine.block_manager import BlockManager
-from hilda_vllm_b200.engine.sequence import Sequence, SequenceStatus
+from hilda_vllm_b200.engine.sequence import PLACEHOLDER, Sequence, SequenceStatus
 
 
 @dataclass
@@ -45,6 +45,7 @@ class Scheduler:
         self.max_num_seqs = config.max_num_seqs
         self.max_num_batched_tokens = config.max_num_batched_tokens
         self.eos = config.eos
+        self.drop_preempted_decode_token = bool(getattr(config, "drop_preempted_decode_token", False))
         self.enable_chunked_prefill = config.enable_chunked_prefill
         self.chunked_prefill_size = config.chunked_prefill_size
         self.chunked_prefill_min_size = config.chunked_prefill_min_size
@@ -257,10 +258,58 @@ class Scheduler:
     def _is_done(self, seq: Sequence, token_id: int) -> bool:
         return (not seq.ignore_eos and token_id == self.eos) or seq.num_completion_tokens == seq.max_tokens
 
+    def _skip_row(self, sched: ScheduledSequence) -> bool:
+        """Rows of a decode batch whose token is not appended.  A sequence preempted as a victim
+        after it was put in the batch is WAITING: the decode buffers treat it as padding, so its
+        row's token is not its own; the reference appends it anyway (scheduler.py:326-340), and so
+        does this scheduler unless config.drop_preempted_decode_token is set."""
+        if sched.is_padding:
+            return True
+        return self.drop_preempted_decode_token and sched.seq.status == SequenceStatus.WAITING
+
+    # ------------------------------------------------------------------ overlapped decode
+    # A decode step whose sampled tokens stay on the GPU until the next step has been launched.
+    # Used only while no running sequence can stop on EOS, so every stop is known from lengths
+    # alone and reading the tokens back later never changes a scheduling decision.
+    def eos_cannot_stop(self) -> bool:
+        return self.eos < 0 or all(seq.ignore_eos for seq in self.running)
+
+    def postprocess_launched(self, seqs: list[ScheduledSequence]) -> tuple[list[tuple[Sequence, int, int]],
+                                                                          list[Sequence]]:
+        """postprocess() for a launched decode step whose tokens are not read yet: each real
+        sequence gets a PLACEHOLDER token and sequences reaching max_tokens finish now.
+        Returns the (sequence, token position, batch row) triples to fill later and the
+        finished sequences."""
+        pending: list[tuple[Sequence, int, int]] = []
+        finished: list[Sequence] = []
+        for slot, sched in enumerate(seqs):
+            if self._skip_row(sched):
+                continue
+            seq = sched.seq
+            seq.num_computed_tokens += 1
+            pending.append((seq, seq.num_tokens, slot))
+            seq.append_token(PLACEHOLDER)
+            if seq.num_completion_tokens == seq.max_tokens:
+                self._finish(seq)
+                finished.append(seq)
+        self._maybe_shrink_batch()
+        return pending, finished
+
+    def resolve_tokens(self, pending: list[tuple[Sequence, int, int]], token_ids: list[int]) -> None:
+        """Fills the placeholders of a launched step with the tokens read back from the GPU
+        (token_ids: one per batch row)."""
+        for seq, pos, row in pending:
+            tok = token_ids[row]
+            assert seq.token_ids[pos] == PLACEHOLDER
+            seq.token_ids[pos] = tok
+            if pos == seq.num_tokens - 1:
+                seq.last_token = tok
+        self.block_manager.resolve_deferred()
+
     def postprocess(self, seqs: list[ScheduledSequence], token_ids: list[int | None], is_prefill: bool):
         if not is_prefill:
             for sched, token_id in zip(seqs, token_ids):
-                if sched.is_padding:
+                if self._skip_row(sched):
                     continue
                 seq = sched.seq
                 assert token_id is not None

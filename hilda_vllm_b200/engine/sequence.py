@@ -10,6 +10,11 @@ from itertools import count
 from hilda_vllm_b200.sampling_params import SamplingParams
 
 
+# Stands for a decode token that the GPU has sampled but the host has not read back yet
+# (overlapped decode steps); replaced by the real id one step later.
+PLACEHOLDER = -1
+
+
 class SequenceStatus(Enum):
     WAITING = auto()
     RUNNING = auto()
