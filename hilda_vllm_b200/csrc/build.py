@@ -25,6 +25,7 @@ SOURCES = [
     "abi.cu",
     "store_kv.cu",
     "paged_decode.cu",
+    "paged_decode_tc.cu",
     "varlen_prefill.cu",
     "prefill_tc.cu",
     "pack_decode.cu",

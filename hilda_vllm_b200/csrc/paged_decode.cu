@@ -29,7 +29,10 @@ namespace {
 
 constexpr int kDecodeThreads = 256;
 constexpr int kHeadDim = 128;
-constexpr int kSplit = 128;            // tokens per CTA (divides every supported block size)
+#ifndef HL_DECODE_SPLIT
+#define HL_DECODE_SPLIT 128
+#endif
+constexpr int kSplit = HL_DECODE_SPLIT;  // tokens per CTA (divides every supported block size)
 constexpr int kTileBytes = 16384;      // bytes per K (and per V) pipeline stage
 constexpr int kStages = 2;
 constexpr int kMaxBatch = 4096;        // capacity of the ticket array in the workspace
@@ -66,7 +69,7 @@ template <bool FP8, int HK>
 struct Traits {
   static constexpr int kElem = FP8 ? 1 : 2;
   static constexpr int kRowBytes = HK * kHeadDim * kElem;  // one token, all local KV heads
-  static constexpr int kT = kTileBytes / kRowBytes;         // tokens per tile
+  static constexpr int kT = kTileBytes / kRowBytes < kSplit ? kTileBytes / kRowBytes : kSplit;  // tokens per tile
   static constexpr int kPhases = 8 / HK;                    // warps sharing one KV head
   static constexpr int kTPW = kT / kPhases;                 // tokens per warp per tile
   static constexpr int kTPH = kTPW / 2;                     // tokens per half-warp per tile
@@ -535,6 +538,16 @@ int64_t max_splits_for(int max_blocks, int block_size) {
 }  // namespace
 }  // namespace hl
 
+namespace hl {
+int64_t decode_tc_workspace_bytes(int batch, int num_q_heads);
+int64_t tc_ticket_end(int batch, int num_q_heads);
+int decode_tc_launch(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+                     const int32_t* block_tables, int64_t bt_stride, int max_blocks, const int32_t* context_lens,
+                     int batch, int num_q_heads, int num_kv_heads, int block_size, int64_t num_blocks,
+                     float scale_log2, void* out, int64_t out_row_stride, void* ws, cudaStream_t stream);
+bool decode_tc_supported(int batch, int num_q_heads, int num_kv_heads, int block_size);
+}  // namespace hl
+
 using namespace hl;
 
 extern "C" int64_t hl_paged_decode_workspace_size(int batch, int num_q_heads, int head_dim, int max_blocks_per_seq,
@@ -542,7 +555,18 @@ extern "C" int64_t hl_paged_decode_workspace_size(int batch, int num_q_heads, in
   if (batch <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_blocks_per_seq <= 0 || block_size <= 0) return -1;
   const int64_t S = max_splits_for(max_blocks_per_seq, block_size);
   const int64_t rows = int64_t(batch) * S * num_q_heads;
-  return kWsMlOff + align256(rows * int64_t(sizeof(float2))) + rows * head_dim * int64_t(sizeof(float));
+  const int64_t simt = kWsMlOff + align256(rows * int64_t(sizeof(float2))) + rows * head_dim * int64_t(sizeof(float));
+  const int64_t tc = decode_tc_workspace_bytes(batch, num_q_heads);
+  return simt > tc ? simt : tc;
+}
+
+namespace {
+int paged_decode_impl(bool allow_tc, const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+                      int kv_dtype, const float* k_scale, const float* v_scale, const int32_t* block_tables,
+                      int64_t bt_stride, int max_blocks_per_seq, const int32_t* context_lens, int batch,
+                      int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                      float softmax_scale, void* out, int64_t out_row_stride, void* workspace, int64_t workspace_bytes,
+                      void* stream);
 }
 
 extern "C" int hl_paged_decode(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
@@ -551,6 +575,32 @@ extern "C" int hl_paged_decode(const void* q, int64_t q_row_stride, const void* 
                                int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
                                float softmax_scale, void* out, int64_t out_row_stride, void* workspace,
                                int64_t workspace_bytes, void* stream) {
+  return paged_decode_impl(false, q, q_row_stride, k_cache, v_cache, kv_dtype, k_scale, v_scale, block_tables,
+                           bt_stride, max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, head_dim,
+                           block_size, num_blocks, softmax_scale, out, out_row_stride, workspace, workspace_bytes,
+                           stream);
+}
+
+extern "C" int hl_paged_decode_tc(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+                                    int kv_dtype, const float* k_scale, const float* v_scale,
+                                    const int32_t* block_tables, int64_t bt_stride, int max_blocks_per_seq,
+                                    const int32_t* context_lens, int batch, int num_q_heads, int num_kv_heads,
+                                    int head_dim, int block_size, int64_t num_blocks, float softmax_scale, void* out,
+                                    int64_t out_row_stride, void* workspace, int64_t workspace_bytes, void* stream) {
+  return paged_decode_impl(true, q, q_row_stride, k_cache, v_cache, kv_dtype, k_scale, v_scale, block_tables,
+                           bt_stride, max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, head_dim,
+                           block_size, num_blocks, softmax_scale, out, out_row_stride, workspace, workspace_bytes,
+                           stream);
+}
+
+namespace {
+
+int paged_decode_impl(bool allow_tc, const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+                      int kv_dtype, const float* k_scale, const float* v_scale, const int32_t* block_tables,
+                      int64_t bt_stride, int max_blocks_per_seq, const int32_t* context_lens, int batch,
+                      int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                      float softmax_scale, void* out, int64_t out_row_stride, void* workspace, int64_t workspace_bytes,
+                      void* stream) {
   clear_error();
   HL_CHECK_ARG(batch >= 0, "hl_paged_decode: batch < 0");
   if (batch == 0) return HL_OK;
@@ -598,9 +648,27 @@ extern "C" int hl_paged_decode(const void* q, int64_t q_row_stride, const void* 
 
   const int g = num_q_heads / num_kv_heads;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (kv_dtype == HL_KV_FP8_E4M3) return dispatch_g<true>(g, num_kv_heads, p, s);
+  if (kv_dtype == HL_KV_FP8_E4M3) {
+    if (allow_tc) {
+      set_error("hl_paged_decode_tc: BF16 caches only");
+      return HL_ERR_UNSUPPORTED;
+    }
+    return dispatch_g<true>(g, num_kv_heads, p, s);
+  }
+  if (allow_tc) {
+    if (!decode_tc_supported(batch, num_q_heads, num_kv_heads, block_size)) {
+      set_error("hl_paged_decode_tc: needs batch <= 2048, Hq/Hk in {1,2,4,8,16}, block_size %% 128 == 0");
+      return HL_ERR_UNSUPPORTED;
+    }
+    HL_CHECK_ARG(num_blocks * block_size < (int64_t(1) << 31), "hl_paged_decode_tc: cache too large");
+    return decode_tc_launch(q, q_row_stride, k_cache, v_cache, block_tables, bt_stride, max_blocks_per_seq,
+                            context_lens, batch, num_q_heads, num_kv_heads, block_size, num_blocks, p.scale_log2, out,
+                            out_row_stride, workspace, s);
+  }
   return dispatch_g<false>(g, num_kv_heads, p, s);
 }
+
+}  // namespace
 
 extern "C" int hl_paged_decode_read_errors(const void* workspace, int32_t* errors_out, void* stream) {
   clear_error();
@@ -693,7 +761,9 @@ extern "C" int hl_paged_decode_noalloc(const void* q, int64_t q_row_stride, cons
   if (rc != HL_OK) return rc;
   // The array keeps whatever the previous call left: zero the error word and the tickets,
   // which the kernel expects to find at zero (the partials are always written before read).
-  cudaError_t e = cudaMemsetAsync(scratch, 0, size_t(kWsMlOff), static_cast<cudaStream_t>(stream));
+  // (both kernels keep the error word at 0 and their tickets right after it).
+  const int64_t zero_bytes = kWsMlOff > tc_ticket_end(batch, num_q_heads) ? kWsMlOff : tc_ticket_end(batch, num_q_heads);
+  cudaError_t e = cudaMemsetAsync(scratch, 0, size_t(zero_bytes), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     set_error("hl_paged_decode_noalloc: cudaMemsetAsync failed: %s", cudaGetErrorString(e));
     return HL_ERR_CUDA;

@@ -113,6 +113,24 @@ int hl_paged_decode(const void* q, int64_t q_row_stride,
                     void* out, int64_t out_row_stride,
                     void* workspace, int64_t workspace_bytes, void* stream);
 
+/* The same decode on the tensor cores, BF16 caches only (no counterpart in the reference):
+ * per 128-token tile of one KV head, S^T = K Q^T and O^T = V^T P^T with tcgen05 (M = 128, N = 16:
+ * the G <= 16 query heads padded), K/V tiles by TMA, P^T as bf16 hi + lo; one CTA per SM walks an
+ * even share of all (sequence, KV head, tile) units and the last CTA of a split (sequence, head)
+ * merges the partial results.  Same arguments and workspace as hl_paged_decode; needs batch <=
+ * 2048, Hq/Hk in {1,2,4,8,16}, block_size % 128 == 0 (HL_ERR_UNSUPPORTED otherwise).  Measured
+ * on B200 it streams the cache at the CUDA-core kernel's rate or slightly below (0.79 vs 0.82 of
+ * HBM peak in the config-2 decode step), so hl_paged_decode keeps the CUDA-core kernel. */
+int hl_paged_decode_tc(const void* q, int64_t q_row_stride,
+                    const void* k_cache, const void* v_cache, int kv_dtype,
+                    const float* k_scale, const float* v_scale,
+                    const int32_t* block_tables, int64_t bt_stride, int max_blocks_per_seq,
+                    const int32_t* context_lens, int batch,
+                    int num_q_heads, int num_kv_heads, int head_dim,
+                    int block_size, int64_t num_blocks, float softmax_scale,
+                    void* out, int64_t out_row_stride,
+                    void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Allocation-free variant of hl_paged_decode (no counterpart in the reference).  For callers
  * that cannot allocate device memory themselves — a host binding this library through an FFI
  * with no device allocator, or a serving loop whose memory is all reserved up front and must not

@@ -208,6 +208,42 @@ def test_decode_inside_cuda_graph():
         assert_close(out, want, **BF16_TOL, what=f"graph replay {trial}")
 
 
+@pytest.mark.parametrize("case", ["one_long", "mixed_long", "many_short", "g16"])
+def test_decode_tensor_core_against_oracle_and_simt(case):
+    """The tcgen05 decode kernel (hl_paged_decode_tc) against the fp32 oracle and the
+    CUDA-core kernel: one 20k-token sequence (each KV head's tiles spread over ~18 CTAs, merged
+    by the last one), long and short sequences mixed, many short ones, and G = 16."""
+    g = torch.Generator().manual_seed({"one_long": 1, "mixed_long": 2, "many_short": 3, "g16": 4}[case])
+    hq, hk = 16, 8
+    if case == "one_long":
+        lens = [20000]
+    elif case == "mixed_long":
+        lens = [9000, 1, 0, 300, 4097, 128, 129, 6000]
+    elif case == "many_short":
+        lens = torch.randint(0, 200, (300,), generator=g).tolist()
+    else:
+        hq, hk = 32, 2
+        lens = [777, 2048, 5, 0]
+    nblocks = sum(-(-n // 256) for n in lens) + 4
+    k, v, bt, ln = make_paged(g, len(lens), hk, 128, nblocks, 256, lens)
+    q = torch.randn(len(lens), hq, 128, generator=g).bfloat16()
+    ws = kernels.make_decode_workspace(len(lens), hq, 128, bt.shape[1], 256, DEV)
+    kd, vd, btd, lnd, qd = k.to(DEV), v.to(DEV), bt.to(DEV), ln.to(DEV), q.to(DEV)
+    for trial in range(2):  # tickets must be back at zero for the second launch
+        out = kernels.paged_decode(qd, kd, vd, btd, lnd, 128 ** -0.5, workspace=ws, tensor_cores=True)
+        torch.cuda.synchronize()
+        assert kernels.decode_errors(ws) == 0
+        idx = list(range(len(lens))) if len(lens) <= 16 else list(range(0, len(lens), 7))
+        want = oattn.paged_decode(q[idx], k, v, bt[idx], ln[idx], 128 ** -0.5)
+        assert_close(out[idx], want, **BF16_TOL, what=f"tensor-core decode {case} trial {trial}")
+    if hq // hk <= 8:  # the CUDA-core kernel covers GQA ratios 1, 2, 4, 8
+        simt = kernels.paged_decode(qd, kd, vd, btd, lnd, 128 ** -0.5, workspace=ws)
+        assert_close(out.float().cpu(), simt.float().cpu(), rtol=2e-2, atol=2e-3, what="tensor-core vs CUDA-core")
+    for i, n in enumerate(lens):
+        if n == 0:
+            assert torch.all(out[i] == 0)
+
+
 @pytest.mark.parametrize("hq,hk,scaled", [(16, 8, False), (16, 8, True), (32, 8, True), (8, 1, True)])
 def test_decode_fp8(hq, hk, scaled):
     g = torch.Generator().manual_seed(7 + hq)
