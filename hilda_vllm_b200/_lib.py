@@ -118,6 +118,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hl_allreduce_signal_bytes": (c_i64, []),
     "hl_allreduce_add_rmsnorm": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_i64, c_f32,
                                          c_vp, c_vp, c_i64, c_vp]),
+    "hl_gemm_workspace_size": (c_i64, [c_int, c_int, c_int, c_int]),
+    "hl_gemm_bf16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_i64, c_vp]),
     "hl_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_vp]),
     "hl_argmax": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp]),
     "hl_argmax_shard": (c_int, [c_vp, c_i64, c_int, c_int, c_i64, c_vp, c_vp, c_vp]),

@@ -31,6 +31,7 @@ SOURCES = [
     "pack_decode.cu",
     "layer_ops.cu",
     "allreduce.cu",
+    "gemm_tc.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -365,6 +365,46 @@ def qk_norm_rope_store(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, h
           "hl_qk_norm_rope_store")
 
 
+GEMM_PLAIN = 0
+GEMM_SILU_MUL = 1
+_gemm_ws: dict = {}
+
+
+def gemm_workspace(m: int, n: int, k: int, epilogue: int, device) -> torch.Tensor:
+    """A zeroed workspace for hl_gemm_bf16 of this shape, cached per (shape, device) so the
+    addresses stay fixed for CUDA-graph capture."""
+    key = (m, n, k, epilogue, str(device))
+    ws = _gemm_ws.get(key)
+    if ws is None:
+        nbytes = int(_lib.load().hl_gemm_workspace_size(m, n, k, epilogue))
+        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _gemm_ws[key] = ws
+    return ws
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
+           epilogue: int = GEMM_PLAIN) -> torch.Tensor:
+    """out = x @ weight.T on the tcgen05 GEMM (x [M, K], weight [N, K], bf16).  With
+    GEMM_SILU_MUL, weight is [2I, K] (gate rows, then up rows) and out = silu(x@gate.T) * (x@up.T)
+    [M, I]."""
+    _cuda(x, weight, out)
+    assert x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and x.dim() == 2
+    assert x.stride(1) == 1 and weight.stride(1) == 1
+    m, k = x.shape
+    n = weight.shape[0] if epilogue == GEMM_PLAIN else weight.shape[0] // 2
+    assert weight.shape[1] == k
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    assert out.shape == (m, n) and out.stride(1) == 1
+    if m == 0:
+        return out
+    ws = gemm_workspace(m, n, k, epilogue, x.device)
+    check(_lib.load().hl_gemm_bf16(x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(),
+                                   out.stride(0), m, n, k, epilogue, ws.data_ptr(), ws.numel(), _stream(x)),
+          "hl_gemm_bf16")
+    return out
+
+
 def silu_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     _cuda(x, out)
     rows, two_i = x.shape

@@ -310,6 +310,23 @@ int hl_argmax_shard(const void* logits, int64_t row_stride, int rows, int vocab,
                     int64_t* out_tokens, float* out_values, void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * Projection GEMM on tcgen05: D[M, N] = A[M, K] . B[N, K]^T, bf16 in / fp32 accumulate / bf16
+ * out, every matrix row-major with the given row strides (elements).  Replaces the nn.Linear
+ * products of the decode step (F.linear in mini_vllm/layers/linear.py and the LM head,
+ * embed_head.py:56-66): A = activations, B = the weight [out_features, in_features].
+ * HL_GEMM_SILU_MUL: B has 2N rows (gate rows [0, N), up rows [N, 2N) as in
+ * MergedColumnParallelLinear) and D = SiLU(A.gate^T) * (A.up^T) with the reference's
+ * SiluAndMul rounding (activation.py:12-16).  K % 64 == 0; 16-byte aligned operands and strides.
+ * The launch uses programmatic dependent launch: weight tiles are fetched before waiting for the
+ * previous kernel on the stream.  workspace: hl_gemm_workspace_size bytes, zeroed once (split-K
+ * tickets return to zero). */
+#define HL_GEMM_PLAIN 0
+#define HL_GEMM_SILU_MUL 1
+int64_t hl_gemm_workspace_size(int M, int N, int K, int epilogue);
+int hl_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int M, int N,
+                 int K, int epilogue, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Tensor-parallel all-reduce over NVLink peer memory fused with add + RMSNorm.
  * Replaces dist.all_reduce after o_proj / down_proj (mini_vllm/layers/linear.py:176-178)
  * together with the add + RMSNorm that follows it (layers/layernorm.py:30-42).

@@ -444,6 +444,38 @@ def test_argmax_lowest_index_on_ties():
     assert torch.equal(got, logits.float().argmax(-1))
 
 
+# ----------------------------------------------------------------------------- tcgen05 GEMM
+@pytest.mark.parametrize("m,n,k", [(256, 4096, 1024), (256, 1024, 2048), (256, 1024, 3072), (1, 1024, 1024),
+                                   (300, 1000, 128), (256, 151936, 1024), (512, 6144, 1024)])
+def test_gemm_matches_fp32_reference(m, n, k):
+    """hl_gemm_bf16 against an fp32 matmul of the same bf16 operands (split-K shapes, ragged M/N,
+    the LM head, a 512-row batch)."""
+    g = torch.Generator().manual_seed(m + n + k)
+    x = (torch.randn(m, k, generator=g) * 0.5).bfloat16()
+    w = (torch.randn(n, k, generator=g) * 0.05).bfloat16()
+    got = kernels.linear(x.to(DEV), w.to(DEV))
+    torch.cuda.synchronize()
+    want = (x.float().to(DEV) @ w.float().to(DEV).T).cpu()
+    assert_close(got, want, rtol=1e-2, atol=1e-2, what=f"gemm {m}x{n}x{k}")
+    again = kernels.linear(x.to(DEV), w.to(DEV))  # split-K tickets reset
+    assert torch.equal(again.cpu(), got.cpu())
+
+
+@pytest.mark.parametrize("m", [256, 64])
+def test_gemm_silu_mul_epilogue(m):
+    """GEMM with the SiLU*mul epilogue == gate_up GEMM followed by the SiluAndMul kernel (up to
+    the accumulation order of the GEMM)."""
+    g = torch.Generator().manual_seed(m)
+    inter, k = 3072, 1024
+    x = (torch.randn(m, k, generator=g) * 0.5).bfloat16().to(DEV)
+    w = (torch.randn(2 * inter, k, generator=g) * 0.05).bfloat16().to(DEV)
+    got = kernels.linear(x, w, epilogue=kernels.GEMM_SILU_MUL)
+    want = kernels.silu_mul(kernels.linear(x, w))
+    torch.cuda.synchronize()
+    assert got.shape == (m, inter)
+    assert_close(got, want, rtol=2e-2, atol=2e-3, what="gemm + silu_mul")
+
+
 # ----------------------------------------------------------------------------- flash-attn pin
 def _flash_attn():
     try:
