@@ -61,8 +61,8 @@ def parse():
                          "c4: mixed chunked prefill + decode with shared prefixes; c5: Qwen3-8B (TP over --gpus)")
     ap.add_argument("--kv", default="auto", choices=["auto", "fp8"], help="KV cache dtype for c5")
     ap.add_argument("--profile", default="",
-                    choices=["", "decode-kernel", "decode-steps", "prefill-kernel", "small-kernels", "allreduce",
-                             "gemm"],
+                    choices=["", "decode-kernel", "decode-kernel-tc", "decode-steps", "prefill-kernel", "small-kernels",
+                             "allreduce", "gemm"],
                     help="run a short profiling case instead of the benchmark: the CUDA profiler range "
                          "(cudaProfilerStart/Stop, for ncu --profile-from-start off) covers --steps "
                          "launches of the decode kernel alone (decode-kernel), of the prefill kernel "
@@ -599,7 +599,7 @@ def run_profile(args):
         return
     torch.cuda.set_device(0)
     g = torch.Generator().manual_seed(args.seed)
-    if args.profile == "decode-kernel":
+    if args.profile in ("decode-kernel", "decode-kernel-tc"):
         # Config-2 shapes at mid-job: 256 sequences, contexts U[65, 1087] (mean ~576), Hq 16 / Hk 8.
         b, hq, hk, d, bs = NUM_SEQS, 16, 8, 128, 256
         lens = torch.randint(PROMPT_LEN + 1, PROMPT_LEN + OUTPUT_LEN, (b,), generator=g)
@@ -618,21 +618,22 @@ def run_profile(args):
         ln = lens.to(torch.int32).to(dev)
         out = torch.empty_like(q)
         ws = kernels.make_decode_workspace(b, hq, d, mb, bs, dev)
+        tc = args.profile == "decode-kernel-tc"
         for _ in range(3):
-            kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws)
+            kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws, tensor_cores=tc)
         torch.cuda.synchronize()
         stream = torch.cuda.current_stream()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.profiler.start()
         e0.record(stream)
         for _ in range(args.steps):
-            kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws)
+            kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws, tensor_cores=tc)
         e1.record(stream)
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
         nbytes = int(lens.sum()) * hk * d * 2 * 2 + b * hq * d * 4
         us = e0.elapsed_time(e1) * 1e3 / args.steps
-        print(json.dumps({"profile": "decode-kernel", "launches": args.steps, "bytes_per_launch": nbytes,
+        print(json.dumps({"profile": args.profile, "launches": args.steps, "bytes_per_launch": nbytes,
                           "cache_gb": round(2 * kc.numel() * 2 / 1e9, 2), "us_per_launch": round(us, 2),
                           "gb_per_s": round(nbytes / us / 1e3, 1)}))
         return
