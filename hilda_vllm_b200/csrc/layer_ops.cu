@@ -305,10 +305,139 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
   }
 }
 
+// ---------------------------------------------------------------------------- sampling
+// Temperature sampling on the device by the Gumbel-max trick: token = argmax_i (logit_i / T + g_i)
+// with g_i = -log(-log u_i), u_i uniform in (0, 1).  This is the same distribution as the
+// reference's exponential race argmax_i softmax(logit / T)_i / E_i, E_i ~ Exp(1)
+// (mini_vllm/layers/sampler.py:12-25 with top_k = -1, top_p = 1): -log E is Gumbel distributed
+// and the softmax normaliser does not move the argmax.  u_i is a counter-based hash of (seed,
+// step, row, global vocabulary index): SplitMix64's finaliser (Steele, Lea & Flood, "Fast
+// splittable pseudorandom number generators", OOPSLA 2014), so the noise does not depend on how
+// the vocabulary is sharded over ranks.  Rows with T <= 0 take the plain argmax.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9e3779b97f4a7c15ull;
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ float gumbel(uint64_t key, int64_t index) {
+  const uint64_t h = splitmix64(key ^ (uint64_t(index) * 0xd1b54a32d192ed03ull));
+  const float u = (float(uint32_t(h >> 40)) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
+  return -__logf(-__logf(u));
+}
+
+__global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int vocab,
+                              int64_t index_offset, const float* __restrict__ temperatures, uint64_t seed,
+                              unsigned long long* __restrict__ step_state, int rows, int64_t* __restrict__ out_tokens,
+                              float* __restrict__ out_values) {
+  const int row = blockIdx.x;
+  const __nv_bfloat16* x = logits + int64_t(row) * row_stride;
+  const float t = temperatures ? temperatures[row] : 0.f;
+  const bool hot = t > 0.f;
+  const float inv_t = hot ? 1.0f / t : 1.0f;
+  __shared__ unsigned long long s_step;
+  if (threadIdx.x == 0) s_step = step_state ? step_state[0] : 0ull;
+  __syncthreads();
+  const uint64_t key = splitmix64(seed ^ splitmix64(s_step * 0x9e3779b97f4a7c15ull + uint64_t(row)));
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  int head = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    head = vocab & ~7;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    for (int i = threadIdx.x; i < (head >> 3); i += blockDim.x) {
+      const uint4 v = __ldg(xv + i);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t4 = 0; t4 < 4; ++t4) {
+        float a = bf16lo(w[t4]), b = bf16hi(w[t4]);
+        const int ia = 8 * i + 2 * t4;
+        if (hot) {
+          a = a * inv_t + gumbel(key, index_offset + ia);
+          b = b * inv_t + gumbel(key, index_offset + ia + 1);
+        }
+        if (a > best) {
+          best = a;
+          bi = ia;
+        }
+        if (b > best) {
+          best = b;
+          bi = ia + 1;
+        }
+      }
+    }
+  }
+  for (int i = head + threadIdx.x; i < vocab; i += blockDim.x) {
+    float v = __bfloat162float(x[i]);
+    if (hot) v = v * inv_t + gumbel(key, index_offset + i);
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sb[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sb[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      out_tokens[row] = index_offset + ((bi == 0x7fffffff) ? 0 : bi);
+      if (out_values) out_values[row] = best;
+      if (step_state) {
+        // The last row to finish advances the step for the next launch (every row has read it).
+        __threadfence();
+        if (atomicAdd(&step_state[1], 1ull) == (unsigned long long)(rows - 1)) {
+          step_state[1] = 0;
+          step_state[0] = s_step + 1;
+        }
+      }
+    }
+  }
+}
+
 }  // namespace
 }  // namespace hl
 
 using namespace hl;
+
+extern "C" int hl_sample(const void* logits, int64_t row_stride, int rows, int vocab, int64_t index_offset,
+                         const float* temperatures, uint64_t seed, void* step_state, int64_t* out_tokens,
+                         float* out_values, void* stream) {
+  clear_error();
+  if (rows == 0) return HL_OK;
+  HL_CHECK_ARG(logits && out_tokens && rows > 0 && vocab > 0, "hl_sample: bad arguments");
+  sample_kernel<<<rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+      (const __nv_bfloat16*)logits, row_stride, vocab, index_offset, temperatures, seed,
+      static_cast<unsigned long long*>(step_state), rows, out_tokens, out_values);
+  HL_CHECK_LAUNCH("hl_sample");
+  return HL_OK;
+}
 
 extern "C" int hl_rmsnorm(const void* in, int64_t in_stride, void* residual, const void* weight, void* out,
                           int64_t out_stride, int rows, int hidden, float eps, void* stream) {

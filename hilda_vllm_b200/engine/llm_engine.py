@@ -16,7 +16,7 @@ from time import perf_counter
 import torch.multiprocessing as mp
 
 from hilda_vllm_b200.config import Config
-from hilda_vllm_b200.engine.model_runner import ModelRunner
+from hilda_vllm_b200.engine.model_runner import ModelRunner, device_sampleable
 from hilda_vllm_b200.engine.scheduler import Scheduler
 from hilda_vllm_b200.engine.sequence import PLACEHOLDER, Sequence
 from hilda_vllm_b200.sampling_params import SamplingParams
@@ -84,7 +84,8 @@ class LLMEngine:
 
     # ------------------------------------------------------------------ stepping
     # Overlapped decode (config.async_decode, default on): while every running sequence stops
-    # by length (ignore_eos, or no EOS token), a greedy decode step is launched before the
+    # by length (ignore_eos, or no EOS token), a decode step sampled on the device (greedy or
+    # plain temperature) is launched before the
     # previous one's tokens are read back; its sequences get PLACEHOLDER tokens that the next
     # step() fills.  The host then schedules and packs step k+1 while the GPU runs step k.  Any
     # other step (prefill, sampling, EOS possible, a packet that needs a token still on the GPU)
@@ -112,7 +113,7 @@ class LLMEngine:
         if not seqs:
             return self._step_result(early + self._drain(), 0, 0)
         if (self.config.async_decode and not is_prefill and self.scheduler.eos_cannot_stop()
-                and all(s.is_padding or s.seq.greedy for s in seqs)):
+                and all(s.is_padding or device_sampleable(s.seq) for s in seqs)):
             if not self.model_runner.can_launch_decode(seqs):
                 early += self._drain()
             handle = self.model_runner.launch_decode(seqs)

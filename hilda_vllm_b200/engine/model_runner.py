@@ -7,8 +7,9 @@ Mirrors mini_vllm/engine/model_runner.py (ModelRunner) for the non-speculative p
   - prepare_decode (:652-720): replaced by DecodePacker + the hl_pack_decode_batch kernel, so
     the host sends one small packet per step instead of rewriting every slot;
   - capture_cudagraph / run_model (:735-832): one graph per batch bucket [1,2,4,8,16,...,512];
-    each graph holds the pack kernel, the whole model, the LM head and (for greedy sampling)
-    the argmax, so a decode step is: one packet copy, one graph replay, one token copy back;
+    each graph holds the pack kernel, the whole model, the LM head and the device sampler
+    (greedy argmax or Gumbel-max temperature sampling; top-k / top-p rows use the host
+    sampler), so a decode step is: one packet copy, one graph replay, one token copy back;
   - convert_prefill_to_decode_cache (:483-502): one launch for all layers;
   - the tensor-parallel RPC through shared memory (:82-130) with rank 0 driving.
 """
@@ -57,6 +58,27 @@ def sampling_settings(seqs: list[Sequence]):
         return None
     return ([s.temperature for s in seqs], [s.top_k for s in seqs], [s.top_p for s in seqs],
             [bool(getattr(s, "greedy", False)) for s in seqs])
+
+
+def device_sampleable(seq) -> bool:
+    """Greedy, or plain temperature sampling (no top-k / top-p): done on the device, inside the
+    decode graph (hl_sample)."""
+    return bool(getattr(seq, "greedy", False)) or (seq.top_k == -1 and seq.top_p >= 1.0)
+
+
+def decode_temperatures(scheduled_seqs) -> np.ndarray | None:
+    """Per-row temperature for the device sampler (0: greedy argmax, also for padding rows), or
+    None when some row needs top-k / top-p (the host sampler)."""
+    t = np.zeros(len(scheduled_seqs), np.float32)
+    for i, sched in enumerate(scheduled_seqs):
+        seq = sched.seq
+        if seq is None:
+            continue
+        if not device_sampleable(seq):
+            return None
+        if not getattr(seq, "greedy", False):
+            t[i] = seq.temperature
+    return t
 
 
 def merge_shard_argmax(all_val: torch.Tensor, all_idx: torch.Tensor) -> torch.Tensor:
@@ -365,6 +387,13 @@ class ModelRunner:
         hq = hf.num_attention_heads // self.world_size
         d = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
         self.decode_workspace = kernels.make_decode_workspace(max_bs, hq, d, mb, self.block_size, dev)
+        # Device sampler: per-slot temperature (0 = greedy), noise seed and launch counter.
+        self.graph_vars["temps"] = torch.zeros(max_bs, dtype=torch.float32, device=dev)
+        self.temps_bufs = [torch.zeros(max_bs, dtype=torch.float32, device="cpu", pin_memory=True) for _ in range(2)]
+        self.temps_host = np.zeros(max_bs, np.float32)  # what graph_vars["temps"] holds
+        self.sample_seed = (int(getattr(self.config, "seed", 0)) * 0x9E3779B1 + 0x5EED) & 0xFFFFFFFFFFFFFFFF
+        self.sample_state = torch.zeros(2, dtype=torch.int64, device=dev)
+        self.prefill_sample_state = torch.zeros(2, dtype=torch.int64, device=dev)  # rank 0's prefill rows
         # Per-rank greedy reduction buffers (tensor parallelism).
         tp = self.world_size
         self.tp_idx = torch.zeros(max_bs, dtype=torch.int64, device=dev)
@@ -405,7 +434,8 @@ class ModelRunner:
                     block_tables=gv["block_tables"][:n])
 
     def _decode_body(self, n: int, greedy: bool):
-        """Pack kernel + model + LM head (+ argmax) over the first n decode slots."""
+        """Pack kernel + model + LM head (+ the device sampler) over the first n decode slots;
+        greedy=False leaves the logits for the host sampler."""
         gv = self.graph_vars
         kernels.pack_decode_batch(self.packet_dev, n, self.block_size, gv["slot_seq_ids"], gv["slot_bt_lens"],
                                   gv["next_tokens"], gv["input_ids"], gv["positions"], gv["slot_mapping"],
@@ -415,22 +445,26 @@ class ModelRunner:
         logits = self.logits_buf[:n]
         torch.matmul(hidden, self.model.lm_head.weight.t(), out=logits)
         if greedy:
-            self._greedy_tokens(logits, gv["next_tokens"][:n])
+            self._device_tokens(logits, gv["next_tokens"][:n])
         return logits
 
-    def _greedy_tokens(self, logits: torch.Tensor, out: torch.Tensor):
-        """Argmax over the full vocabulary into `out` (device), on every rank.  Under tensor
-        parallelism each rank reduces its vocabulary shard to (max, index) and the ranks
-        all-gather those pairs (2 x 12 bytes per row instead of the logits); the lowest rank
-        wins ties, which is the lowest global index because shards are ordered."""
-        if self.world_size == 1:
-            kernels.argmax(logits, out)
-            return
+    def _device_tokens(self, logits: torch.Tensor, out: torch.Tensor):
+        """Token per row into `out` (device), on every rank: the greedy argmax, or for rows with a
+        temperature in graph_vars["temps"] a Gumbel-max sample (hl_sample).  Under tensor
+        parallelism each rank reduces its vocabulary shard to (max, index) — the noise is a
+        function of the global index, so the shards draw disjoint parts of one noise field —
+        and the ranks all-gather those pairs (2 x 12 bytes per row instead of the logits); the
+        lowest rank wins ties, which is the lowest global index because shards are ordered."""
         n = logits.shape[0]
+        temps = self.graph_vars["temps"][:n]
+        if self.world_size == 1:
+            kernels.sample(logits, temps, self.sample_seed, self.sample_state, out=out)
+            return
         head = self.model.lm_head
         idx = self.tp_idx[:n]
         val = self.tp_val[:n]
-        kernels.argmax_shard(logits, head.vocab_start_idx, idx, val)
+        kernels.sample(logits, temps, self.sample_seed, self.sample_state, out=idx, index_offset=head.vocab_start_idx,
+                       out_values=val)
         all_val = self.tp_all_val.view(-1)[: self.world_size * n].view(self.world_size, n)
         all_idx = self.tp_all_idx.view(-1)[: self.world_size * n].view(self.world_size, n)
         dist.all_gather_into_tensor(all_val, val)
@@ -459,17 +493,37 @@ class ModelRunner:
         self.packer.buffer = self.packet_host.numpy()
         nbytes = self.packer.build(scheduled_seqs, graph_bs)
         real = [i for i, s in enumerate(scheduled_seqs) if not s.is_padding]
-        samp = sampling_settings([scheduled_seqs[i].seq for i in real])
+        temps = decode_temperatures(scheduled_seqs)
+        samp = None if temps is not None else sampling_settings([scheduled_seqs[i].seq for i in real])
+        temps = self._temps_change(temps, graph_bs)
         self.last_decode_batch_info = {"scheduled_bs": bs, "graph_bs": graph_bs, "active_seqs": len(real),
                                        "padded_slots": bs - len(real), "pack_events": self.packer.last_num_events}
         packet = self.packet_host[:nbytes].numpy()
-        tokens = self.call("execute_decode", packet, bs, graph_bs,
-                           real, samp)
+        tokens = self.call("execute_decode", packet, bs, graph_bs, real, samp, temps)
         self.packer.note_sampled(bs, tokens)
         out: list[int | None] = [None] * bs
         for i in real:
             out[i] = tokens[i]
         return out
+
+    def _temps_change(self, temps: np.ndarray | None, graph_bs: int) -> np.ndarray | None:
+        """The [0, graph_bs) temperatures to upload this step, or None if the device holds them."""
+        if temps is None:
+            return None
+        full = np.zeros(graph_bs, np.float32)
+        full[: len(temps)] = temps
+        if np.array_equal(self.temps_host[:graph_bs], full):
+            return None
+        self.temps_host[:graph_bs] = full
+        return full
+
+    def _upload_temps(self, temps: np.ndarray | None, par: int) -> None:
+        if temps is None:
+            return
+        n = len(temps)
+        self.temps_bufs[par][:n].numpy()[:] = temps
+        self.graph_vars["temps"][:n].copy_(self.temps_bufs[par][:n], non_blocking=True)
+        self.temps_host[:n] = temps
 
     # ------------------------------------------------------------------ overlapped decode
     # A greedy decode step launched without waiting for its tokens: the argmax leaves them in
@@ -477,8 +531,7 @@ class ModelRunner:
     # asynchronous device->host copy brings them to a pinned buffer that collect_decode() reads
     # after the next step has been launched.
     def can_launch_decode(self, scheduled_seqs) -> bool:
-        return all(s.is_padding or s.seq.greedy for s in scheduled_seqs) and \
-            not self.packer.needs_host_tokens(scheduled_seqs)
+        return decode_temperatures(scheduled_seqs) is not None and not self.packer.needs_host_tokens(scheduled_seqs)
 
     @torch.inference_mode()
     def launch_decode(self, scheduled_seqs: list[ScheduledSequence]):
@@ -488,15 +541,17 @@ class ModelRunner:
         self.launch_parity ^= 1
         self.packer.buffer = self.packet_bufs[par].numpy()
         nbytes = self.packer.build(scheduled_seqs, graph_bs)
+        temps = self._temps_change(decode_temperatures(scheduled_seqs), graph_bs)
         real = sum(1 for s in scheduled_seqs if not s.is_padding)
         self.last_decode_batch_info = {"scheduled_bs": bs, "graph_bs": graph_bs, "active_seqs": real,
                                        "padded_slots": bs - real, "pack_events": self.packer.last_num_events}
-        self.call("execute_decode_launch", self.packet_bufs[par][:nbytes].numpy(), bs, graph_bs, par)
+        self.call("execute_decode_launch", self.packet_bufs[par][:nbytes].numpy(), bs, graph_bs, par, temps)
         self.packer.note_launched(bs, scheduled_seqs)
         return par, bs
 
     @torch.inference_mode()
-    def execute_decode_launch(self, packet: np.ndarray, bs: int, graph_bs: int, par: int):
+    def execute_decode_launch(self, packet: np.ndarray, bs: int, graph_bs: int, par: int, temps=None):
+        self._upload_temps(temps, par)
         nbytes = packet.nbytes
         host = self.packet_bufs[par].numpy()
         if packet.ctypes.data != host.ctypes.data:
@@ -529,6 +584,9 @@ class ModelRunner:
             return kernels.argmax(logits).tolist()
         temps, ks, ps, greedy = samp
         dev = self.device
+        if all(g or (k == -1 and p >= 1.0) for g, k, p in zip(greedy, ks, ps)):
+            t = torch.tensor([0.0 if g else x for g, x in zip(greedy, temps)], dtype=torch.float32, device=dev)
+            return kernels.sample(logits, t, self.sample_seed ^ 0xA5A5, self.prefill_sample_state).tolist()
         sampled = self.sampler(logits, torch.tensor(temps, dtype=torch.float32, device=dev),
                                torch.tensor(ks, dtype=torch.int32, device=dev),
                                torch.tensor(ps, dtype=torch.float32, device=dev))
@@ -561,7 +619,8 @@ class ModelRunner:
         return token_ids
 
     @torch.inference_mode()
-    def execute_decode(self, packet: np.ndarray, bs: int, graph_bs: int, real: list[int], samp):
+    def execute_decode(self, packet: np.ndarray, bs: int, graph_bs: int, real: list[int], samp, temps=None):
+        self._upload_temps(temps, 0)
         nbytes = packet.nbytes
         host = self.packet_host.numpy()
         if packet.ctypes.data != host.ctypes.data:
@@ -654,6 +713,8 @@ class ModelRunner:
         gv["context_lens"].zero_()
         gv["slot_mapping"].fill_(-1)
         gv["positions"].zero_()
+        gv["temps"].zero_()
+        self.temps_host[:] = 0.0
         self.packer = DecodePacker(self.max_bs, self.max_num_decode_blocks, self.packet_host.numpy())
 
     @torch.inference_mode()

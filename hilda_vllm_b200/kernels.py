@@ -370,6 +370,27 @@ GEMM_SILU_MUL = 1
 _gemm_ws: dict = {}
 
 
+def sample(logits: torch.Tensor, temperatures: torch.Tensor | None, seed: int, step_state: torch.Tensor | None,
+           out: torch.Tensor | None = None, index_offset: int = 0,
+           out_values: torch.Tensor | None = None) -> torch.Tensor:
+    """Per row: Gumbel-max temperature sample (temperatures[row] > 0) or greedy argmax of bf16
+    logits [rows, V] (hl_sample).  step_state: int64 [2] device counter advanced per launch."""
+    _cuda(logits, temperatures, step_state, out, out_values)
+    rows, vocab = logits.shape
+    assert logits.dtype == torch.bfloat16 and logits.stride(1) == 1
+    if temperatures is not None:
+        assert temperatures.dtype == torch.float32 and temperatures.is_contiguous() and temperatures.numel() >= rows
+    if step_state is not None:
+        assert step_state.dtype == torch.int64 and step_state.numel() >= 2
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int64, device=logits.device)
+    lib = _lib.load()
+    check(lib.hl_sample(logits.data_ptr(), logits.stride(0), rows, vocab, int(index_offset), _p(temperatures),
+                        int(seed) & 0xFFFFFFFFFFFFFFFF, _p(step_state), out.data_ptr(), _p(out_values),
+                        _stream(logits)), "hl_sample")
+    return out
+
+
 def gemm_workspace(m: int, n: int, k: int, epilogue: int, device) -> torch.Tensor:
     """A zeroed workspace for hl_gemm_bf16 of this shape, cached per (shape, device) so the
     addresses stay fixed for CUDA-graph capture."""

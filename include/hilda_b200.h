@@ -356,6 +356,18 @@ int hl_allreduce_add_rmsnorm(void* const* peer_data, void* const* peer_signal, i
                              int64_t out_stride, float eps, int* epochs, int* error_word,
                              int64_t timeout_ns, void* stream);
 
+/* Token per row of bf16 logits: rows with temperatures[row] > 0 are sampled by the Gumbel-max
+ * trick, argmax_i (logit_i / T + Gumbel noise) — the distribution of the reference's
+ * exponential-race Sampler with top_k = -1, top_p = 1 (mini_vllm/layers/sampler.py:12-25) — the
+ * others (or all, temperatures = NULL) take the greedy argmax.  The noise is a counter-based hash
+ * of (seed, step, row, index_offset + i), so vocabulary shards of a tensor-parallel LM head draw
+ * disjoint parts of the same noise; out_values (optional) receives the winning perturbed value for
+ * merging shards.  step_state: device uint64[2] (zeroed once); the launch reads the step and its
+ * last row advances it, so CUDA-graph replays draw fresh noise.  NULL: step 0 every call. */
+int hl_sample(const void* logits, int64_t row_stride, int rows, int vocab, int64_t index_offset,
+              const float* temperatures, uint64_t seed, void* step_state, int64_t* out_tokens,
+              float* out_values, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

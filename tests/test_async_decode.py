@@ -16,6 +16,7 @@ import pytest
 
 from hilda_vllm_b200.engine.decode_packer import DecodePacker
 from hilda_vllm_b200.engine.llm_engine import LLMEngine
+from hilda_vllm_b200.engine.model_runner import decode_temperatures
 from hilda_vllm_b200.engine.scheduler import Scheduler
 from hilda_vllm_b200.engine.sequence import PLACEHOLDER, Sequence, SequenceStatus
 from hilda_vllm_b200.sampling_params import SamplingParams
@@ -91,7 +92,7 @@ class FakeRunner:
         return [None if s.is_padding else t for s, t in zip(scheduled, tokens)]
 
     def can_launch_decode(self, scheduled):
-        return all(s.is_padding or s.seq.greedy for s in scheduled) and not self.packer.needs_host_tokens(scheduled)
+        return decode_temperatures(scheduled) is not None and not self.packer.needs_host_tokens(scheduled)
 
     def launch_decode(self, scheduled):
         tokens = self._device_step(scheduled)
@@ -119,10 +120,10 @@ def make_engine(async_decode: bool, num_blocks: int, max_num_seqs: int = 8, bloc
     return eng
 
 
-def drive(eng, prompts, max_tokens, greedy=True):
+def drive(eng, prompts, max_tokens, greedy=True, top_k=-1):
     seqs = []
     for p, m in zip(prompts, max_tokens):
-        seq = Sequence(p, SamplingParams(max_tokens=m, ignore_eos=True, greedy=greedy))
+        seq = Sequence(p, SamplingParams(max_tokens=m, ignore_eos=True, greedy=greedy, top_k=top_k))
         eng.model_runner.prompts[seq.seq_id] = list(p)
         eng.scheduler.add(seq)
         seqs.append(seq)
@@ -165,13 +166,16 @@ def test_overlapped_decode_matches_synchronous(num_blocks, drop_victim_token):
     assert results[False][2] == 0
 
 
-def test_sampled_sequences_run_synchronously():
+@pytest.mark.parametrize("top_k,overlapped", [(-1, True), (5, False)])
+def test_which_sampled_sequences_overlap(top_k, overlapped):
+    """Plain temperature sampling runs on the device and overlaps; top-k needs the host sampler,
+    so those steps run synchronously."""
     Sequence.counter = iter(range(10_000))
     eng = make_engine(True, 200)
     rng = np.random.default_rng(3)
     prompts = [rng.integers(0, 4000, 10).tolist() for _ in range(4)]
-    seqs, outputs = drive(eng, prompts, [12] * 4, greedy=False)
-    assert eng.model_runner.launched == 0 and len(outputs) == 4
+    seqs, outputs = drive(eng, prompts, [12] * 4, greedy=False, top_k=top_k)
+    assert (eng.model_runner.launched > 0) == overlapped and len(outputs) == 4
 
 
 def test_deferred_page_hash_equals_synchronous_hash():

@@ -139,6 +139,30 @@ def test_overlapped_decode_equals_synchronous(tmp_path, golden_dir):
     assert [len(t) for t in res[True]] == [sp.max_tokens for sp in sps]
 
 
+def test_temperature_sampling_on_device_overlapped_equals_synchronous(tmp_path, golden_dir):
+    """Temperature-sampled requests (top_k -1, top_p 1) are sampled inside the decode graph
+    (Gumbel-max, seeded noise), so overlapped and synchronous stepping draw the same tokens;
+    a top-k request falls back to the host sampler and still completes."""
+    d = tiny_dir(tmp_path, golden_dir)
+    g = torch.Generator().manual_seed(31)
+    prompts = [torch.randint(0, 512, (int(n),), generator=g).tolist() for n in (7, 120, 33, 260)]
+    sps = [SamplingParams(temperature=0.6, max_tokens=40, ignore_eos=True) for _ in prompts]
+    res = {}
+    for mode in (False, True):
+        llm = LLM(str(d), load_format="random", seed=7, max_num_seqs=8, max_model_len=1024,
+                  max_num_batched_tokens=2048, kvcache_block_cap=32, async_decode=mode, gpu_memory_utilization=0.5)
+        res[mode] = [o["token_ids"] for o in llm.generate(prompts, sps, use_tqdm=False)]
+        if mode:
+            topk = llm.generate(prompts[:2], SamplingParams(temperature=0.6, top_k=5, max_tokens=12, ignore_eos=True),
+                                use_tqdm=False)
+            assert all(len(o["token_ids"]) == 12 for o in topk)
+        llm.exit()
+    assert res[True] == res[False]
+    assert all(len(t) == 40 for t in res[True])
+    # sampling, not greedy: the runs differ from the argmax path somewhere
+    assert any(len(set(t)) > 1 for t in res[True])
+
+
 def test_qwen3_0_6b_greedy_32_steps_matches_oracle():
     from transformers import AutoConfig
 

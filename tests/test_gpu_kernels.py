@@ -444,6 +444,50 @@ def test_argmax_lowest_index_on_ties():
     assert torch.equal(got, logits.float().argmax(-1))
 
 
+# ----------------------------------------------------------------------------- device sampling
+def test_sample_greedy_rows_equal_argmax_and_shards_merge():
+    """hl_sample: temperature-0 rows are the argmax; with temperatures, sampling two vocabulary
+    shards (index_offset) and keeping the larger perturbed value gives the same token as sampling
+    the whole row (the noise is a function of the global index)."""
+    g = torch.Generator().manual_seed(17)
+    rows, vocab = 64, 151936
+    logits = torch.randn(rows, vocab, generator=g).bfloat16().to(DEV)
+    zero = torch.zeros(rows, dtype=torch.float32, device=DEV)
+    assert torch.equal(kernels.sample(logits, zero, 5, None).cpu(), kernels.argmax(logits).cpu())
+    temps = (torch.rand(rows, generator=g) + 0.3).to(DEV)
+    full = kernels.sample(logits, temps, 5, None)
+    half = vocab // 2
+    vals, idxs = [], []
+    for off in (0, half):
+        v = torch.empty(rows, dtype=torch.float32, device=DEV)
+        i = kernels.sample(logits[:, off:off + half].contiguous(), temps, 5, None, index_offset=off, out_values=v)
+        vals.append(v)
+        idxs.append(i)
+    merged = torch.where(vals[1] > vals[0], idxs[1], idxs[0])
+    assert torch.equal(merged.cpu(), full.cpu())
+
+
+def test_sample_matches_softmax_distribution():
+    """Empirical token frequencies of Gumbel-max sampling (the step counter advancing per launch)
+    match softmax(logits / T) — the reference Sampler's distribution — within sampling error."""
+    g = torch.Generator().manual_seed(23)
+    rows, vocab, T = 512, 16, 0.7
+    base = torch.randn(vocab, generator=g) * 1.5
+    logits = base.bfloat16().repeat(rows, 1).to(DEV)
+    temps = torch.full((rows,), T, dtype=torch.float32, device=DEV)
+    state = torch.zeros(2, dtype=torch.int64, device=DEV)
+    counts = torch.zeros(vocab, dtype=torch.float64)
+    launches = 40
+    for _ in range(launches):
+        tok = kernels.sample(logits, temps, 1234, state)
+        counts += torch.bincount(tok.cpu(), minlength=vocab).double()
+    assert int(state[0].item()) == launches and int(state[1].item()) == 0
+    freq = counts / counts.sum()
+    want = torch.softmax(base.bfloat16().float() / T, -1).double()
+    n = rows * launches
+    assert float((freq - want).abs().max()) < 5 * float((want * (1 - want) / n).sqrt().max()) + 1e-4
+
+
 # ----------------------------------------------------------------------------- tcgen05 GEMM
 @pytest.mark.parametrize("m,n,k", [(256, 4096, 1024), (256, 1024, 2048), (256, 1024, 3072), (1, 1024, 1024),
                                    (300, 1000, 128), (256, 151936, 1024), (512, 6144, 1024)])
