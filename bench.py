@@ -305,6 +305,14 @@ def run_ours(args):
                "wall_s": round(wall, 3), "output_tokens": n_out,
                "prefill_s": round(stats["prefill_time_s"], 4), "decode_s": round(stats["decode_time_s"], 3),
                "decode_tok_s": round(stats["decode_throughput_toks"], 1)}
+        # The same job sampled at temperature 0.6 (the reference's own benchmark setting,
+        # benchmarks/bench.py:186-192): sampled on the device by the Gumbel-max kernel.
+        fresh()
+        t0 = time.perf_counter()
+        outs_t = llm.generate(prompts, SamplingParams(temperature=0.6, max_tokens=OUTPUT_LEN, ignore_eos=True),
+                              use_tqdm=False)
+        wall_t = time.perf_counter() - t0
+        e2e["temperature_0_6_tok_s"] = round(sum(len(o["token_ids"]) for o in outs_t) / wall_t, 1)
 
     cpu = None
     if not args.no_cpu and world == 1:
