@@ -6,7 +6,8 @@
 // (post_attention_layernorm / the next layer's input_layernorm / the final norm,
 // mini_vllm/layers/layernorm.py:30-42, models/qwen3.py:150-157).  Here one kernel does both:
 // every rank keeps its partial sums in a buffer that the other ranks mapped through CUDA IPC,
-// a CTA meets the same CTA of every peer at a flag barrier (peer stores, local polling), then
+// a CTA meets the same CTA of every peer at a flag barrier (relaxed peer stores, acquire polls of
+// its own flags), then
 // reads its rows from all ranks' buffers over NVLink with plain loads, sums them in fp32 in
 // rank order (so every rank computes bit-identical results), rounds to bf16 (the all-reduce
 // result, as NCCL returns it) and applies the reference's add + RMSNorm arithmetic.
@@ -53,8 +54,12 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-__device__ __forceinline__ void store_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// The flag store needs no release: the partial sums it announces were written by an earlier
+// kernel of this stream and are complete in this GPU's memory before this kernel starts.  The
+// poll keeps acquire semantics so that the peer-buffer loads after it cannot be served from
+// copies older than the flag.
+__device__ __forceinline__ void store_flag_sys(int* p, int v) {
+  asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ int load_acquire_sys(const int* p) {
@@ -84,9 +89,7 @@ __global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(const __grid
   __syncthreads();
   const int epoch = s_epoch;
   if (tid < p.world && tid != p.rank) {
-    // The partials peers will read were written by an earlier kernel of this stream, so they are
-    // complete in this GPU's memory; the release store orders nothing else.
-    store_release_sys(p.signal[tid] + blk * kArMaxRanks + p.rank, epoch);
+    store_flag_sys(p.signal[tid] + blk * kArMaxRanks + p.rank, epoch);
     const int* mine = p.signal[p.rank] + blk * kArMaxRanks + tid;
     const unsigned long long t0 = global_ns();
     bool arrived = false;

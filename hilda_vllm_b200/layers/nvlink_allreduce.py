@@ -101,9 +101,9 @@ class NvlinkAllReduce:
     def fits(self, rows: int) -> bool:
         """Whether this batch takes the fused one-shot path.  Every rank reads the rows of all
         the others, so the traffic grows with (world - 1) x hidden: measured on B200 (56 calls in
-        a graph), it beats NCCL + RMSNorm at 2 ranks up to hidden 4096 (18 vs 28 us at 256 rows)
-        and at 8 ranks for hidden 1024 (19 vs 34 us), but not at 8 ranks for hidden 4096
-        (73 vs 41 us), where NCCL's ring / tree moves less data."""
+        a graph, 256 rows), it beats NCCL + RMSNorm at 2 ranks up to hidden 4096 (7.8 vs 18.3 us
+        at hidden 1024, 14.9 vs 27.8 at 4096) and at 8 ranks for hidden 1024 (18.7 vs 34.2 us),
+        but not at 8 ranks for hidden 4096 (72.7 vs 40.8 us), where NCCL moves less data."""
         if not 0 < rows <= self.max_rows:
             return False
         return self.world == 2 or self.hidden <= 2048
