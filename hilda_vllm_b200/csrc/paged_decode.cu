@@ -655,12 +655,19 @@ int paged_decode_impl(bool allow_tc, const void* q, int64_t q_row_stride, const 
     }
     return dispatch_g<true>(g, num_kv_heads, p, s);
   }
-  if (allow_tc) {
+  // With four or more query heads per KV head the CUDA-core kernel spends two FMAs per cache
+  // byte plus the half-warp score reductions and runs out of issue slots well below the HBM
+  // rate (G = 4: 0.59 of the copy peak at 256 x 900 tokens, G = 8: 0.24), while the tcgen05
+  // kernel puts the G heads on the MMA's N = 16 columns at no extra cost (0.73 / 0.72 there).
+  // For G <= 2 the CUDA-core kernel is the faster one at every measured length.
+  const bool tc_fits = decode_tc_supported(batch, num_q_heads, num_kv_heads, block_size) &&
+                       num_blocks * block_size < (int64_t(1) << 31);
+  if (allow_tc || (g >= 4 && tc_fits)) {
     if (!decode_tc_supported(batch, num_q_heads, num_kv_heads, block_size)) {
       set_error("hl_paged_decode_tc: needs batch <= 2048, Hq/Hk in {1,2,4,8,16}, block_size %% 128 == 0");
       return HL_ERR_UNSUPPORTED;
     }
-    HL_CHECK_ARG(num_blocks * block_size < (int64_t(1) << 31), "hl_paged_decode_tc: cache too large");
+    HL_CHECK_ARG(tc_fits, "hl_paged_decode_tc: cache too large");
     return decode_tc_launch(q, q_row_stride, k_cache, v_cache, block_tables, bt_stride, max_blocks_per_seq,
                             context_lens, batch, num_q_heads, num_kv_heads, block_size, num_blocks, p.scale_log2, out,
                             out_row_stride, workspace, s);

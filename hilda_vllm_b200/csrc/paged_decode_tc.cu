@@ -27,6 +27,8 @@
 // Every wait is bounded; no cluster launch, no multicast.
 #include "hl_common.cuh"
 
+#include <atomic>
+
 #include <cuda.h>
 
 namespace hl {
@@ -59,6 +61,7 @@ constexpr int kOffBarTc = kOffEp + 1024;
 constexpr int kSmemTc = kOffBarTc + 256 + 1024;
 constexpr int kMaxBatchTc = 2048;
 constexpr int kMaxGridTc = 256;
+constexpr int kMaxDevicesTc = 64;
 constexpr uint32_t kTmemColsTc = 64;        // S0 [0,16) S1 [16,32) O0 [32,48) O1 [48,64)
 constexpr float kRescale = 8.f;
 
@@ -702,20 +705,26 @@ bool encode3(CUtensorMap* map, const void* base, uint64_t heads, uint64_t outer,
 
 template <int G>
 int launch_g(const TcDecodeParams& prm, cudaStream_t stream) {
-  static bool configured = false;  // first call happens before any graph capture
-  static int grid = 0;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_tc_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemTc);
-    int dev = 0, sms = 0;
-    if (e == cudaSuccess) e = cudaGetDevice(&dev);
+  // Per device: the shared-memory opt-in is a per-device attribute.  The first call on a device
+  // happens before any graph capture (the engine's eager warm-up).
+  static std::atomic<int> grid_of[kMaxDevicesTc];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevicesTc) {
+    set_error("hl_paged_decode: no usable current device");
+    return HL_ERR_CUDA;
+  }
+  int grid = grid_of[dev].load(std::memory_order_acquire);
+  if (grid == 0) {
+    int sms = 0;
+    e = cudaFuncSetAttribute(paged_decode_tc_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) {
       set_error("hl_paged_decode: tensor-core kernel setup: %s", cudaGetErrorString(e));
       return HL_ERR_CUDA;
     }
     grid = sms < kMaxGridTc ? sms : kMaxGridTc;
-    configured = true;
+    grid_of[dev].store(grid, std::memory_order_release);
   }
   paged_decode_tc_kernel<G><<<grid, kThreadsTc, kSmemTc, stream>>>(prm);
   HL_CHECK_LAUNCH("hl_paged_decode");

@@ -208,6 +208,30 @@ def test_decode_inside_cuda_graph():
         assert_close(out, want, **BF16_TOL, what=f"graph replay {trial}")
 
 
+@pytest.mark.parametrize("hq,hk", [(32, 8), (64, 8)])
+def test_decode_cuda_core_kernel_at_high_gqa_ratio(hq, hk):
+    """hl_paged_decode runs the tensor-core kernel for BF16 caches with Hq/Hk >= 4 up to 2048
+    sequences and the CUDA-core kernel beyond; a 2100-sequence batch (sequences share pages of a
+    small pool) keeps the CUDA-core kernel's G = 4 / 8 instantiations covered."""
+    g = torch.Generator().manual_seed(hq)
+    b, nb, bs = 2100, 12, 256
+    lens = torch.randint(0, 700, (b,), generator=g)
+    lens[:4] = torch.tensor([0, 1, 256, 699])
+    k = torch.randn(nb, bs, hk, 128, generator=g).bfloat16()
+    v = torch.randn(nb, bs, hk, 128, generator=g).bfloat16()
+    bt = torch.randint(0, nb, (b, 3), generator=g, dtype=torch.int32)
+    q = torch.randn(b, hq, 128, generator=g).bfloat16()
+    ws = kernels.make_decode_workspace(b, hq, 128, 3, bs, DEV)
+    out = kernels.paged_decode(q.to(DEV), k.to(DEV), v.to(DEV), bt.to(DEV), lens.to(torch.int32).to(DEV),
+                               128 ** -0.5, workspace=ws)
+    torch.cuda.synchronize()
+    assert kernels.decode_errors(ws) == 0
+    idx = list(range(4)) + list(range(5, b, 97))
+    want = oattn.paged_decode(q[idx], k, v, bt[idx], lens[idx].to(torch.int32), 128 ** -0.5)
+    assert_close(out[idx], want, **BF16_TOL, what=f"CUDA-core decode hq={hq} hk={hk} B={b}")
+    assert torch.all(out[0] == 0)
+
+
 @pytest.mark.parametrize("case", ["one_long", "mixed_long", "many_short", "g16"])
 def test_decode_tensor_core_against_oracle_and_simt(case):
     """The tcgen05 decode kernel (hl_paged_decode_tc) against the fp32 oracle and the
