@@ -41,6 +41,9 @@ constexpr int64_t kWsTicketOff = 256;  // int32 tickets[kMaxBatch]
 constexpr int64_t kWsMlOff = kWsTicketOff + 4 * kMaxBatch + 256;  // float2 (m, l) [B][S][Hq]
 
 constexpr float kLog2e = 1.4426950408889634f;
+// Smallest GQA ratio that hl_paged_decode hands to the tensor-core kernel.
+constexpr int kTcMinGroupBf16 = 4;
+constexpr int kTcMinGroupFp8 = 4;
 
 __host__ __device__ constexpr int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
@@ -541,11 +544,12 @@ int64_t max_splits_for(int max_blocks, int block_size) {
 namespace hl {
 int64_t decode_tc_workspace_bytes(int batch, int num_q_heads);
 int64_t tc_ticket_end(int batch, int num_q_heads);
-int decode_tc_launch(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
-                     const int32_t* block_tables, int64_t bt_stride, int max_blocks, const int32_t* context_lens,
-                     int batch, int num_q_heads, int num_kv_heads, int block_size, int64_t num_blocks,
-                     float scale_log2, void* out, int64_t out_row_stride, void* ws, cudaStream_t stream);
-bool decode_tc_supported(int batch, int num_q_heads, int num_kv_heads, int block_size);
+int decode_tc_launch(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache, bool fp8,
+                     const float* k_scale, const float* v_scale, const int32_t* block_tables, int64_t bt_stride,
+                     int max_blocks, const int32_t* context_lens, int batch, int num_q_heads, int num_kv_heads,
+                     int block_size, int64_t num_blocks, float scale_log2, void* out, int64_t out_row_stride, void* ws,
+                     cudaStream_t stream);
+bool decode_tc_supported(int batch, int num_q_heads, int num_kv_heads, int block_size, bool fp8);
 }  // namespace hl
 
 using namespace hl;
@@ -648,30 +652,27 @@ int paged_decode_impl(bool allow_tc, const void* q, int64_t q_row_stride, const 
 
   const int g = num_q_heads / num_kv_heads;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (kv_dtype == HL_KV_FP8_E4M3) {
-    if (allow_tc) {
-      set_error("hl_paged_decode_tc: BF16 caches only");
-      return HL_ERR_UNSUPPORTED;
-    }
-    return dispatch_g<true>(g, num_kv_heads, p, s);
-  }
-  // With four or more query heads per KV head the CUDA-core kernel spends two FMAs per cache
-  // byte plus the half-warp score reductions and runs out of issue slots well below the HBM
-  // rate (G = 4: 0.59 of the copy peak at 256 x 900 tokens, G = 8: 0.24), while the tcgen05
-  // kernel puts the G heads on the MMA's N = 16 columns at no extra cost (0.73 / 0.72 there).
-  // For G <= 2 the CUDA-core kernel is the faster one at every measured length.
-  const bool tc_fits = decode_tc_supported(batch, num_q_heads, num_kv_heads, block_size) &&
+  const bool fp8 = kv_dtype == HL_KV_FP8_E4M3;
+  // With four or more query heads per KV head (two or more for e4m3 bytes) the CUDA-core
+  // kernel spends two or more FMAs per cache byte plus the half-warp score reductions and runs
+  // out of issue slots well below the HBM rate (BF16 at 256 x 900 tokens: G = 4 0.59 of the copy
+  // peak, G = 8 0.24; e4m3 G = 4 0.28), while the tcgen05 kernel puts the G heads on the MMA's
+  // N = 16 columns at no extra cost.  For BF16 G <= 2 the CUDA-core kernel is the faster one at
+  // every measured length.
+  const bool tc_fits = decode_tc_supported(batch, num_q_heads, num_kv_heads, block_size, fp8) &&
                        num_blocks * block_size < (int64_t(1) << 31);
-  if (allow_tc || (g >= 4 && tc_fits)) {
-    if (!decode_tc_supported(batch, num_q_heads, num_kv_heads, block_size)) {
-      set_error("hl_paged_decode_tc: needs batch <= 2048, Hq/Hk in {1,2,4,8,16}, block_size %% 128 == 0");
+  if (allow_tc || (g >= (fp8 ? kTcMinGroupFp8 : kTcMinGroupBf16) && tc_fits)) {
+    if (!decode_tc_supported(batch, num_q_heads, num_kv_heads, block_size, fp8)) {
+      set_error("hl_paged_decode_tc: needs batch <= 2048, Hq/Hk in {1,2,4,8,16} (BF16) or {1,2,4,8} (FP8), "
+                "block_size %% 128 == 0");
       return HL_ERR_UNSUPPORTED;
     }
     HL_CHECK_ARG(tc_fits, "hl_paged_decode_tc: cache too large");
-    return decode_tc_launch(q, q_row_stride, k_cache, v_cache, block_tables, bt_stride, max_blocks_per_seq,
-                            context_lens, batch, num_q_heads, num_kv_heads, block_size, num_blocks, p.scale_log2, out,
-                            out_row_stride, workspace, s);
+    return decode_tc_launch(q, q_row_stride, k_cache, v_cache, fp8, k_scale, v_scale, block_tables, bt_stride,
+                            max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, block_size,
+                            num_blocks, p.scale_log2, out, out_row_stride, workspace, s);
   }
+  if (fp8) return dispatch_g<true>(g, num_kv_heads, p, s);
   return dispatch_g<false>(g, num_kv_heads, p, s);
 }
 

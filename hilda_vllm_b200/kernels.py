@@ -151,8 +151,9 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
     q [B, Hq, D] (or [B, 1, Hq, D]) bf16; k_cache/v_cache [NB, BS, Hk, D] bf16 or e4m3;
     block_tables [B, >= max_blocks] int32; context_lens [B] int32.  Returns out [B, Hq, D].
     The semantics are flash_attn_with_kvcache's for a single causal query token
-    (mini_vllm/layers/attention.py:162-170).  tensor_cores=True runs the tcgen05 variant
-    (hl_paged_decode_tc, BF16 caches only) instead of the CUDA-core kernel."""
+    (mini_vllm/layers/attention.py:162-170).  The library picks the kernel (the tcgen05 one for
+    GQA ratios >= 4); tensor_cores=True forces the tcgen05 variant (hl_paged_decode_tc) for any
+    ratio it supports."""
     if q.dim() == 4:
         assert q.shape[1] == 1
         q = q.squeeze(1)

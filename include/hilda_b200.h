@@ -96,9 +96,9 @@ int hl_copy_kv_bf16_to_fp8(const void* src_k, const void* src_v, void* dst_k, vo
  *   block_tables: [B, bt_stride] int32; only the first max_blocks_per_seq entries are read
  *   context_lens: [B] int32; rows with 0 produce zeros.
  * Requires head_dim == 128, block_size % 256 == 0, Hq % Hk == 0, Hk in {1,2,4,8},
- * Hq/Hk in {1,2,4,8} (FP8) or {1,2,4,8,16} (BF16).  Kernel choice: BF16 caches with Hq/Hk >= 4
- * and batch <= 2048 run the tensor-core kernel of hl_paged_decode_tc (the CUDA-core kernel is
- * issue-bound there); everything else runs the CUDA-core split-K kernel.  The workspace (>= hl_paged_decode_workspace_size bytes) must be
+ * Hq/Hk in {1,2,4,8} (FP8) or {1,2,4,8,16} (BF16).  Kernel choice: Hq/Hk >= 4 with batch <= 2048
+ * runs the tensor-core kernel of hl_paged_decode_tc (the CUDA-core kernel is issue-bound there);
+ * everything else runs the CUDA-core split-K kernel.  The workspace (>= hl_paged_decode_workspace_size bytes) must be
  * zero-filled once before first use; the kernel leaves it ready for the next launch.
  * Launches that share one workspace must not overlap on the GPU.
  * ---------------------------------------------------------------------------------- */
@@ -115,12 +115,14 @@ int hl_paged_decode(const void* q, int64_t q_row_stride,
                     void* out, int64_t out_row_stride,
                     void* workspace, int64_t workspace_bytes, void* stream);
 
-/* The same decode on the tensor cores, BF16 caches only (no counterpart in the reference):
- * per 128-token tile of one KV head, S^T = K Q^T and O^T = V^T P^T with tcgen05 (M = 128, N = 16:
- * the G <= 16 query heads padded), K/V tiles by TMA, P^T as bf16 hi + lo; one CTA per SM walks an
- * even share of all (sequence, KV head, tile) units and the last CTA of a split (sequence, head)
- * merges the partial results.  Same arguments and workspace as hl_paged_decode; needs batch <=
- * 2048, Hq/Hk in {1,2,4,8,16}, block_size % 128 == 0 (HL_ERR_UNSUPPORTED otherwise).  Measured
+/* The same decode on the tensor cores (no counterpart in the reference): per 128-token tile of
+ * one KV head, S^T = K Q^T and O^T = V^T P^T with tcgen05 (M = 128, N = 16: the G <= 16 query
+ * heads padded), K/V tiles by TMA, P^T as bf16 hi + lo; one CTA per SM walks an even share of all
+ * (sequence, KV head, tile) units and the last CTA of a split (sequence, head) merges the partial
+ * results.  FP8 caches: converter warps turn the staged e4m3 tiles into f16 operands (exact) and
+ * Q into f16 with an exact power-of-two shift; the products run with f16 operands, P^T as one f16.
+ * Same arguments and workspace as hl_paged_decode; needs batch <= 2048, Hq/Hk in {1,2,4,8,16}
+ * (BF16) or {1,2,4,8} (FP8), block_size % 128 == 0 (HL_ERR_UNSUPPORTED otherwise).  Measured
  * on B200 at Hq/Hk = 2 it streams the cache slightly below the CUDA-core kernel (0.79 vs 0.82 of
  * HBM peak in the config-2 decode step); at Hq/Hk >= 4 it is the faster one and hl_paged_decode
  * calls it itself.  This entry point forces it for any supported ratio. */

@@ -120,7 +120,7 @@ def test_copy_bf16_to_fp8_all_layers_bit_exact():
 
 
 # ----------------------------------------------------------------------------- decode
-def run_decode(q, k, v, bt, lens, scale, fp8=False, ks=None, vs=None, ws=None):
+def run_decode(q, k, v, bt, lens, scale, fp8=False, ks=None, vs=None, ws=None, tensor_cores=False):
     if fp8:
         kd = k.to(DEV).view(torch.float8_e4m3fn)
         vd = v.to(DEV).view(torch.float8_e4m3fn)
@@ -128,7 +128,7 @@ def run_decode(q, k, v, bt, lens, scale, fp8=False, ks=None, vs=None, ws=None):
         kd, vd = k.to(DEV), v.to(DEV)
     return kernels.paged_decode(q.to(DEV), kd, vd, bt.to(DEV), lens.to(DEV), scale, workspace=ws,
                                 k_scale=None if ks is None else ks.to(DEV),
-                                v_scale=None if vs is None else vs.to(DEV))
+                                v_scale=None if vs is None else vs.to(DEV), tensor_cores=tensor_cores)
 
 
 def test_decode_config1_shapes():
@@ -268,8 +268,12 @@ def test_decode_tensor_core_against_oracle_and_simt(case):
             assert torch.all(out[i] == 0)
 
 
-@pytest.mark.parametrize("hq,hk,scaled", [(16, 8, False), (16, 8, True), (32, 8, True), (8, 1, True)])
-def test_decode_fp8(hq, hk, scaled):
+@pytest.mark.parametrize("hq,hk,scaled,tc", [(16, 8, False, False), (16, 8, True, False), (32, 8, True, False),
+                                             (8, 1, True, False), (16, 8, True, True), (8, 8, True, True),
+                                             (16, 2, False, True)])
+def test_decode_fp8(hq, hk, scaled, tc):
+    """e4m3 caches with per-head scales.  Hq/Hk >= 4 runs the tensor-core kernel by default;
+    tc=True forces it for the smaller ratios."""
     g = torch.Generator().manual_seed(7 + hq)
     lens = [0, 1, 129, 256, 700, 1500]
     kb, vb, bt, ln = make_paged(g, len(lens), hk, 128, 24, 256, lens)
@@ -278,7 +282,7 @@ def test_decode_fp8(hq, hk, scaled):
     kq = kv_store.quantize_e4m3(kb, ks)
     vq = kv_store.quantize_e4m3(vb, vs)
     q = torch.randn(len(lens), hq, 128, generator=g).bfloat16()
-    out = run_decode(q, kq, vq, bt, ln, 128 ** -0.5, fp8=True, ks=ks, vs=vs)
+    out = run_decode(q, kq, vq, bt, ln, 128 ** -0.5, fp8=True, ks=ks, vs=vs, tensor_cores=tc)
     want = oattn.paged_decode(q, kq, vq, bt, ln, 128 ** -0.5, ks, vs, fp8=True)
     assert_close(out, want, rtol=2e-2, atol=6e-2, what="fp8")
     assert_close(out, want, **BF16_TOL, what="fp8 (tight)")
@@ -660,3 +664,66 @@ def test_prefill_tensor_core_paged_with_prefix_chunks(one_head):
     assert kernels.prefill_errors() == 0
     want = oattn.varlen_prefill(q, k, v, cuq, cuk, 128 ** -0.5, block_table=bt)
     assert_close(out, want, **BF16_TOL, what="tcgen05 prefill paged")
+
+
+@pytest.mark.parametrize("case", ["one_long", "many_short", "q_range"])
+def test_decode_fp8_tensor_core_splits_and_q_range(case):
+    """The tcgen05 kernel on e4m3 caches: a 20k-token sequence split over many CTAs (partial
+    merges), many short sequences, and query rows whose magnitudes span 2^-20 .. 2^20 (Q goes to
+    f16 with a per-head power-of-two shift)."""
+    g = torch.Generator().manual_seed({"one_long": 11, "many_short": 12, "q_range": 13}[case])
+    hq, hk = 32, 8
+    if case == "one_long":
+        lens = [20000]
+    elif case == "many_short":
+        lens = torch.randint(0, 200, (300,), generator=g).tolist()
+    else:
+        lens = [300, 1000, 77, 2]
+    nblocks = sum(-(-n // 256) for n in lens) + 4
+    kb, vb, bt, ln = make_paged(g, len(lens), hk, 128, nblocks, 256, lens)
+    ks = torch.rand(hk, generator=g) + 0.5
+    vs = torch.rand(hk, generator=g) + 0.5
+    kq = kv_store.quantize_e4m3(kb, ks)
+    vq = kv_store.quantize_e4m3(vb, vs)
+    q = torch.randn(len(lens), hq, 128, generator=g)
+    if case == "q_range":
+        exps = torch.tensor([-20.0, -6.0, 0.0, 20.0])
+        q = q * (2.0 ** exps).view(-1, 1, 1)
+    q = q.bfloat16()
+    ws = kernels.make_decode_workspace(len(lens), hq, 128, bt.shape[1], 256, DEV)
+    for trial in range(2):
+        out = run_decode(q, kq, vq, bt, ln, 128 ** -0.5, fp8=True, ks=ks, vs=vs, ws=ws)
+        torch.cuda.synchronize()
+        assert kernels.decode_errors(ws) == 0
+        idx = list(range(len(lens))) if len(lens) <= 16 else list(range(0, len(lens), 7))
+        want = oattn.paged_decode(q[idx], kq, vq, bt[idx], ln[idx], 128 ** -0.5, ks, vs, fp8=True)
+        assert_close(out[idx], want, **BF16_TOL, what=f"fp8 tensor-core {case} trial {trial}")
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_decode_tensor_core_ignores_nan_past_context(fp8):
+    """Cache slots past a sequence's context may hold any bits (an uninitialised cache); the
+    tcgen05 kernel loads whole 128-token tiles, so it must keep NaN there out of P.V."""
+    g = torch.Generator().manual_seed(21 + fp8)
+    hq, hk = 32, 8
+    lens = [1, 100, 129, 255, 300]
+    kb, vb, bt, ln = make_paged(g, len(lens), hk, 128, 8, 256, lens)
+    q = torch.randn(len(lens), hq, 128, generator=g).bfloat16()
+    if fp8:
+        kc, vc = kv_store.quantize_e4m3(kb, None), kv_store.quantize_e4m3(vb, None)
+        nan_byte = 0x7F
+    else:
+        kc, vc = kb.clone(), vb.clone()
+    for i, n in enumerate(lens):
+        for j in range(n, -(-n // 256) * 256):
+            blk = int(bt[i, j // 256])
+            if fp8:
+                kc[blk, j % 256] = nan_byte
+                vc[blk, j % 256] = nan_byte
+            else:
+                kc[blk, j % 256] = float("nan")
+                vc[blk, j % 256] = float("nan")
+    out = run_decode(q, kc, vc, bt, ln, 128 ** -0.5, fp8=fp8)
+    assert torch.isfinite(out.float()).all()
+    want = oattn.paged_decode(q, kc, vc, bt, ln, 128 ** -0.5, fp8=fp8)
+    assert_close(out, want, **BF16_TOL, what=f"NaN past context fp8={fp8}")

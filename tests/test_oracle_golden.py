@@ -154,3 +154,17 @@ def test_oracle_model_matches_reference_modules_greedy(golden_dir):
             toks = model.logits(model.forward(ids, pos, ctx), ctx).argmax(-1).tolist()
         assert toks == step["tokens"]
         seqs = [s + [t] for s, t in zip(seqs, toks)]
+
+
+def test_e4m3_to_f16_bit_placement_is_exact():
+    """The tensor-core FP8 decode converts e4m3 to f16 by bit placement (byte to the high byte of
+    a 16-bit half, shift right by one, carry the sign from bit 14 to 15), giving value x 2^-8;
+    restated here over all 256 bytes against torch's e4m3 decoding."""
+    b = np.arange(256, dtype=np.uint32)
+    x = (b << 8) >> 1
+    h = ((x + (x & 0x4000)) & 0xFFFF).astype(np.uint16)
+    got = torch.from_numpy(h.view(np.int16)).view(torch.float16).float()
+    want = torch.from_numpy(b.astype(np.uint8)).view(torch.float8_e4m3fn).float() / 256
+    finite = ~torch.isnan(want)
+    assert torch.equal(got[finite], want[finite])
+    assert int(finite.sum()) == 254
