@@ -609,8 +609,14 @@ def run_profile(args):
     g = torch.Generator().manual_seed(args.seed)
     if args.profile in ("decode-kernel", "decode-kernel-tc"):
         # Config-2 shapes at mid-job: 256 sequences, contexts U[65, 1087] (mean ~576), Hq 16 / Hk 8.
+        # --workload c5: the Qwen3-8B layout (Hq 32 / Hk 8, GQA 4) at its mid-job contexts (prompt
+        # U[256, 1024] + 256 generated); --kv fp8 stores the cache as e4m3.
         b, hq, hk, d, bs = NUM_SEQS, 16, 8, 128, 256
         lens = torch.randint(PROMPT_LEN + 1, PROMPT_LEN + OUTPUT_LEN, (b,), generator=g)
+        if args.workload == "c5":
+            hq = 32
+            lens = torch.randint(256 + 256, 1024 + 256 + 1, (b,), generator=g)
+        fp8 = args.kv == "fp8"
         nblk = [-(-int(n) // bs) for n in lens]
         perm = torch.randperm(sum(nblk), generator=g).tolist()
         mb = max(nblk)
@@ -621,6 +627,8 @@ def run_profile(args):
         dev = torch.device("cuda", 0)
         kc = torch.randn(sum(nblk), bs, hk, d, device=dev, dtype=torch.bfloat16)
         vc = torch.randn_like(kc)
+        if fp8:
+            kc, vc = kc.to(torch.float8_e4m3fn), vc.to(torch.float8_e4m3fn)
         q = torch.randn(b, hq, d, device=dev, dtype=torch.bfloat16)
         bt = torch.tensor(tables, dtype=torch.int32, device=dev)
         ln = lens.to(torch.int32).to(dev)
@@ -639,10 +647,12 @@ def run_profile(args):
         e1.record(stream)
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
-        nbytes = int(lens.sum()) * hk * d * 2 * 2 + b * hq * d * 4
+        elem = 1 if fp8 else 2
+        nbytes = int(lens.sum()) * hk * d * elem * 2 + b * hq * d * 4
         us = e0.elapsed_time(e1) * 1e3 / args.steps
-        print(json.dumps({"profile": args.profile, "launches": args.steps, "bytes_per_launch": nbytes,
-                          "cache_gb": round(2 * kc.numel() * 2 / 1e9, 2), "us_per_launch": round(us, 2),
+        print(json.dumps({"profile": args.profile, "workload": args.workload, "kv": "fp8" if fp8 else "bf16",
+                          "hq": hq, "hk": hk, "launches": args.steps, "bytes_per_launch": nbytes,
+                          "cache_gb": round(2 * kc.numel() * elem / 1e9, 2), "us_per_launch": round(us, 2),
                           "gb_per_s": round(nbytes / us / 1e3, 1)}))
         return
     if args.profile == "prefill-kernel":
