@@ -122,6 +122,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hl_gemm_bf16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_i64, c_vp]),
     "hl_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_vp]),
     "hl_sample": (c_int, [c_vp, c_i64, c_int, c_int, c_i64, c_vp, ctypes.c_uint64, c_vp, c_vp, c_vp, c_vp]),
+    "hl_sample_filtered": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_vp, ctypes.c_uint64, c_vp, c_vp,
+                                   c_vp]),
     "hl_argmax": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp]),
     "hl_argmax_shard": (c_int, [c_vp, c_i64, c_int, c_int, c_i64, c_vp, c_vp, c_vp]),
 }

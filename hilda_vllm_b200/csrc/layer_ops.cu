@@ -354,8 +354,8 @@ __global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
         float a = bf16lo(w[t4]), b = bf16hi(w[t4]);
         const int ia = 8 * i + 2 * t4;
         if (hot) {
-          a = a * inv_t + gumbel(key, index_offset + ia);
-          b = b * inv_t + gumbel(key, index_offset + ia + 1);
+          a = __fmaf_rn(a, inv_t, gumbel(key, index_offset + ia));
+          b = __fmaf_rn(b, inv_t, gumbel(key, index_offset + ia + 1));
         }
         if (a > best) {
           best = a;
@@ -370,7 +370,7 @@ __global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
   }
   for (int i = head + threadIdx.x; i < vocab; i += blockDim.x) {
     float v = __bfloat162float(x[i]);
-    if (hot) v = v * inv_t + gumbel(key, index_offset + i);
+    if (hot) v = __fmaf_rn(v, inv_t, gumbel(key, index_offset + i));
     if (v > best || (v == best && i < bi)) {
       best = v;
       bi = i;
@@ -421,6 +421,370 @@ __global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
   }
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// Sampling with top-k / top-p on the device (mini_vllm/layers/sampler.py:13-49): per row
+// x = logits / temperature; top-k keeps the k largest x; top-p then keeps, in descending order
+// of x, the tokens whose inclusive cumulative softmax probability (over the top-k set) is below
+// top_p, and always the first; the token is a draw from the softmax over what is kept, taken
+// as the Gumbel-max argmax(x + g) with the noise of hl_sample (so a row without top-k / top-p
+// gets exactly hl_sample's token).  Tokens of equal value are ordered by index (lowest first)
+// wherever the boundary of a filter cuts through them; torch.sort leaves that order unspecified.
+//
+// One CTA per row.  x's order is the order of the bf16 logits, so the selections work on a
+// 16-bit order-preserving key of the logit bits with two 256-bin histograms (high byte, then
+// the low byte inside the chosen bin): counts for top-k, softmax mass for top-p.  Each thread
+// owns a contiguous range of the row, so "first m by index" is a block-wide scan of counts.
+// ---------------------------------------------------------------------------------------------
+constexpr int kFilterThreads = 1024;
+constexpr float kLog2eF = 1.4426950408889634f;
+
+__device__ __forceinline__ uint32_t order_key(uint32_t b16) {
+  return (b16 & 0x8000u) ? (~b16 & 0xffffu) : (b16 | 0x8000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  const uint32_t b = (k & 0x8000u) ? (k & 0x7fffu) : (~k & 0xffffu);
+  return __uint_as_float(b << 16);
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_incl_scan(T v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  return v;
+}
+
+// Warp 0: scanning the 256 bins from the top, the bin b where the running total reaches
+// `target` (above < target <= above + h[b]); -1 when the total stays below it.
+template <typename T>
+__device__ int find_from_top(const T* h, T target, T* above_out) {
+  const int lane = threadIdx.x & 31;
+  T part[8];
+  T sum = T(0);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    part[j] = h[255 - (lane * 8 + j)];
+    sum += part[j];
+  }
+  const T incl = warp_incl_scan(sum, lane);
+  const T excl = incl - sum;
+  const unsigned m = __ballot_sync(0xffffffffu, excl < target && target <= incl);
+  int res = -1;
+  T above = T(0);
+  if (m) {
+    const int src = __ffs(m) - 1;
+    if (lane == src) {
+      T c = excl;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (res < 0 && target <= c + part[j]) {
+          res = 255 - (lane * 8 + j);
+          above = c;
+        }
+        c += part[j];
+      }
+    }
+    res = __shfl_sync(0xffffffffu, res, src);
+    above = __shfl_sync(0xffffffffu, above, src);
+  }
+  *above_out = above;
+  return res;
+}
+
+struct FilterShared {
+  unsigned hc[256];
+  float hm[256];
+  unsigned wsum[32];
+  float wsumf[32];
+  int ires[2];
+  float fres[4];
+  unsigned ures[4];
+};
+
+// Block-wide exclusive scan of one count per thread; also returns the total.
+__device__ __forceinline__ unsigned block_excl_scan(unsigned v, unsigned* total, FilterShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned incl = warp_incl_scan(v, lane);
+  if (lane == 31) sh.wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned w = sh.wsum[lane];
+    const unsigned wi = warp_incl_scan(w, lane);
+    sh.wsum[lane] = wi - w;
+    if (lane == 31) sh.ures[3] = wi;
+  }
+  __syncthreads();
+  const unsigned r = sh.wsum[warp] + incl - v;
+  *total = sh.ures[3];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ float block_sum(float v, FilterShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) sh.wsumf[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float w = sh.wsumf[lane];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+    if (lane == 0) sh.fres[3] = w;
+  }
+  __syncthreads();
+  const float r = sh.fres[3];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kFilterThreads) sample_filtered_kernel(
+    const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int vocab, const float* __restrict__ temperatures,
+    const int32_t* __restrict__ top_ks, const float* __restrict__ top_ps, uint64_t seed,
+    unsigned long long* __restrict__ step_state, int rows, int64_t* __restrict__ out_tokens) {
+  __shared__ FilterShared sh;
+  __shared__ unsigned long long s_step;
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint16_t* xr = reinterpret_cast<const uint16_t*>(logits + int64_t(row) * row_stride);
+  const float t = temperatures ? temperatures[row] : 0.f;
+  const bool hot = t > 0.f;
+  const float inv_t = hot ? 1.0f / t : 1.0f;
+  const int k = top_ks ? top_ks[row] : 0;
+  const float top_p = top_ps ? top_ps[row] : 1.f;
+  const bool filt_k = hot && k > 0 && k < vocab;
+  const bool filt_p = hot && top_p < 1.f;
+  if (tid == 0) s_step = step_state ? step_state[0] : 0ull;
+  __syncthreads();
+  const uint64_t key = splitmix64(seed ^ splitmix64(s_step * 0x9e3779b97f4a7c15ull + uint64_t(row)));
+  const int seg = (vocab + kFilterThreads - 1) / kFilterThreads;
+  const int begin = min(vocab, tid * seg), end = min(vocab, begin + seg);
+
+  // Kept set: K = {key > kap} + the first m_k (by index) with key == kap; F = K filtered the same
+  // way by (vp, idx_p).  Defaults keep everything.
+  uint32_t kap = 0, vp = 0;
+  int idx_k = INT_MAX, idx_p = INT_MAX;
+  auto in_k = [&](int i, uint32_t kk) { return kk > kap || (kk == kap && i <= idx_k); };
+  auto in_f = [&](int i, uint32_t kk) { return in_k(i, kk) && (kk > vp || (kk == vp && i <= idx_p)); };
+  // Index of the m-th (1-based, index order) element of the row satisfying pred; INT_MAX if none.
+  auto nth_index = [&](auto pred, unsigned m) {
+    unsigned c = 0;
+    for (int i = begin; i < end; ++i) c += pred(i, order_key(__ldg(xr + i))) ? 1u : 0u;
+    unsigned total;
+    const unsigned ex = block_excl_scan(c, &total, sh);
+    if (tid == 0) sh.ires[0] = INT_MAX;
+    __syncthreads();
+    if (ex < m && m <= ex + c) {
+      unsigned seen = ex;
+      for (int i = begin; i < end; ++i) {
+        if (pred(i, order_key(__ldg(xr + i))) && ++seen == m) {
+          sh.ires[0] = i;
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    const int r = sh.ires[0];
+    __syncthreads();
+    return r;
+  };
+
+  if (filt_k || filt_p) {
+    // High-byte counts and the maximum key.
+    for (int i = tid; i < 256; i += kFilterThreads) sh.hc[i] = 0u;
+    __syncthreads();
+    uint32_t kmax = 0;
+    for (int i = begin; i < end; ++i) {
+      const uint32_t kk = order_key(__ldg(xr + i));
+      kmax = max(kmax, kk);
+      if (filt_k) atomicAdd(&sh.hc[kk >> 8], 1u);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    if (lane == 0) sh.wsum[warp] = kmax;
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t w = sh.wsum[lane];
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) w = max(w, __shfl_xor_sync(0xffffffffu, w, o));
+      if (lane == 0) sh.ures[0] = w;
+    }
+    __syncthreads();
+    kmax = sh.ures[0];
+
+    if (filt_k) {
+      // k-th largest key: high byte, then low byte inside that bin.
+      if (warp == 0) {
+        unsigned above;
+        const int b1 = find_from_top(sh.hc, unsigned(k), &above);
+        if (lane == 0) {
+          sh.ires[1] = b1;
+          sh.ures[1] = above;
+        }
+      }
+      __syncthreads();
+      const int b1 = sh.ires[1];
+      const unsigned above1 = sh.ures[1];
+      __syncthreads();
+      for (int i = tid; i < 256; i += kFilterThreads) sh.hc[i] = 0u;
+      __syncthreads();
+      for (int i = begin; i < end; ++i) {
+        const uint32_t kk = order_key(__ldg(xr + i));
+        if (int(kk >> 8) == b1) atomicAdd(&sh.hc[kk & 0xffu], 1u);
+      }
+      __syncthreads();
+      if (warp == 0) {
+        unsigned above;
+        const int b2 = find_from_top(sh.hc, unsigned(k) - above1, &above);
+        if (lane == 0) {
+          sh.ires[1] = b2;
+          sh.ures[1] = above1 + above;
+          sh.ures[2] = b2 >= 0 ? sh.hc[b2] : 0u;
+        }
+      }
+      __syncthreads();
+      kap = (uint32_t(b1) << 8) | uint32_t(sh.ires[1]);
+      const unsigned m_k = unsigned(k) - sh.ures[1];  // ties at kap to keep, >= 1
+      const unsigned n_tie = sh.ures[2];
+      __syncthreads();
+      if (m_k < n_tie) idx_k = nth_index([&](int, uint32_t kk) { return kk == kap; }, m_k);
+    }
+
+    if (filt_p) {
+      // Softmax mass over K by high byte; the top token (key kmax, lowest index) is always in K.
+      const float vmax = key_float(kmax) * inv_t;
+      for (int i = tid; i < 256; i += kFilterThreads) sh.hm[i] = 0.f;
+      __syncthreads();
+      float z = 0.f;
+      for (int i = begin; i < end; ++i) {
+        const uint32_t kk = order_key(__ldg(xr + i));
+        if (!in_k(i, kk)) continue;
+        const float e = exp2f((key_float(kk) * inv_t - vmax) * kLog2eF);
+        z += e;
+        atomicAdd(&sh.hm[kk >> 8], e);
+      }
+      z = block_sum(z, sh);
+      const float thr = top_p * z;
+      if (warp == 0) {
+        float above;
+        const int c1 = find_from_top(sh.hm, thr, &above);
+        if (lane == 0) {
+          sh.ires[1] = c1;
+          sh.fres[0] = above;
+        }
+      }
+      __syncthreads();
+      const int c1 = sh.ires[1];
+      const float above1 = sh.fres[0];
+      __syncthreads();
+      if (c1 >= 0) {
+        for (int i = tid; i < 256; i += kFilterThreads) {
+          sh.hm[i] = 0.f;
+          sh.hc[i] = 0u;
+        }
+        __syncthreads();
+        for (int i = begin; i < end; ++i) {
+          const uint32_t kk = order_key(__ldg(xr + i));
+          if (int(kk >> 8) != c1 || !in_k(i, kk)) continue;
+          atomicAdd(&sh.hm[kk & 0xffu], exp2f((key_float(kk) * inv_t - vmax) * kLog2eF));
+          atomicAdd(&sh.hc[kk & 0xffu], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+          float above;
+          int c2 = find_from_top(sh.hm, thr - above1, &above);
+          if (c2 < 0) {  // rounding: the crossing is the lowest non-empty bin
+            above = 0.f;
+            c2 = -1;
+            float acc = 0.f;
+            for (int b = 255; b >= 0; --b) {
+              if (sh.hc[b] != 0u) {
+                c2 = b;
+                above = acc;
+              }
+              acc += sh.hm[b];
+            }
+          }
+          if (lane == 0) {
+            sh.ires[1] = c2;
+            sh.fres[1] = above1 + above;
+            sh.ures[2] = c2 >= 0 ? sh.hc[c2] : 0u;
+          }
+        }
+        __syncthreads();
+        const int c2 = sh.ires[1];
+        const float cum_gt = sh.fres[1];
+        const unsigned n_tie = sh.ures[2];
+        __syncthreads();
+        if (c2 >= 0) {
+          vp = (uint32_t(c1) << 8) | uint32_t(c2);
+          const float e_v = exp2f((key_float(vp) * inv_t - vmax) * kLog2eF);
+          // tie r (0-based) is kept iff cum_gt + (r + 1) e_v < thr
+          float mf = ceilf((thr - cum_gt) / e_v) - 1.f;
+          unsigned m_p = mf <= 0.f ? 0u : (mf >= float(n_tie) ? n_tie : unsigned(mf));
+          if (vp == kmax && m_p == 0u) m_p = 1u;  // the first token is always kept
+          if (m_p < n_tie)
+            idx_p = m_p == 0u ? -1 : nth_index([&](int i, uint32_t kk) { return kk == vp && in_k(i, kk); }, m_p);
+        }
+      }
+    }
+  }
+
+  // Gumbel-max (or argmax for a greedy row) over the kept tokens; lowest index among equals.
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = begin; i < end; ++i) {
+    const uint32_t raw = __ldg(xr + i);
+    if ((filt_k || filt_p) && !in_f(i, order_key(raw))) continue;
+    float v = __uint_as_float(raw << 16);
+    if (hot) v = __fmaf_rn(v, inv_t, gumbel(key, i));
+    if (v > best) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    sh.wsumf[warp] = best;
+    sh.wsum[warp] = unsigned(bi);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = sh.wsumf[lane];
+    bi = int(sh.wsum[lane]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      out_tokens[row] = (bi == 0x7fffffff) ? 0 : bi;
+      if (step_state) {
+        __threadfence();
+        if (atomicAdd(&step_state[1], 1ull) == (unsigned long long)(rows - 1)) {
+          step_state[1] = 0;
+          step_state[0] = s_step + 1;
+        }
+      }
+    }
+  }
+}
+
 }  // namespace
 }  // namespace hl
 
@@ -436,6 +800,20 @@ extern "C" int hl_sample(const void* logits, int64_t row_stride, int rows, int v
       (const __nv_bfloat16*)logits, row_stride, vocab, index_offset, temperatures, seed,
       static_cast<unsigned long long*>(step_state), rows, out_tokens, out_values);
   HL_CHECK_LAUNCH("hl_sample");
+  return HL_OK;
+}
+
+extern "C" int hl_sample_filtered(const void* logits, int64_t row_stride, int rows, int vocab,
+                                  const float* temperatures, const int32_t* top_ks, const float* top_ps,
+                                  uint64_t seed, void* step_state, int64_t* out_tokens, void* stream) {
+  clear_error();
+  if (rows == 0) return HL_OK;
+  HL_CHECK_ARG(logits && out_tokens && rows > 0 && vocab > 0 && row_stride >= vocab,
+               "hl_sample_filtered: bad arguments");
+  sample_filtered_kernel<<<rows, kFilterThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      (const __nv_bfloat16*)logits, row_stride, vocab, temperatures, top_ks, top_ps, seed,
+      static_cast<unsigned long long*>(step_state), rows, out_tokens);
+  HL_CHECK_LAUNCH("hl_sample_filtered");
   return HL_OK;
 }
 

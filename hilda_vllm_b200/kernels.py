@@ -392,6 +392,30 @@ def sample(logits: torch.Tensor, temperatures: torch.Tensor | None, seed: int, s
     return out
 
 
+def sample_filtered(logits: torch.Tensor, temperatures: torch.Tensor | None, top_ks: torch.Tensor | None,
+                    top_ps: torch.Tensor | None, seed: int, step_state: torch.Tensor | None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """hl_sample with the reference's top-k / top-p filters (mini_vllm/layers/sampler.py:13-49):
+    per row a Gumbel-max draw from softmax(logits / T) restricted to the top-k, then top-p, set
+    (top_ks int32, <= 0 or >= V: no filter; top_ps float32, >= 1: no filter); greedy argmax where
+    T <= 0.  Rows without filters get exactly sample()'s token for the same seed and step."""
+    _cuda(logits, temperatures, top_ks, top_ps, step_state, out)
+    rows, vocab = logits.shape
+    assert logits.dtype == torch.bfloat16 and logits.stride(1) == 1
+    for t, dt in ((temperatures, torch.float32), (top_ks, torch.int32), (top_ps, torch.float32)):
+        if t is not None:
+            assert t.dtype == dt and t.is_contiguous() and t.numel() >= rows
+    if step_state is not None:
+        assert step_state.dtype == torch.int64 and step_state.numel() >= 2
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int64, device=logits.device)
+    lib = _lib.load()
+    check(lib.hl_sample_filtered(logits.data_ptr(), logits.stride(0), rows, vocab, _p(temperatures), _p(top_ks),
+                                 _p(top_ps), int(seed) & 0xFFFFFFFFFFFFFFFF, _p(step_state), out.data_ptr(),
+                                 _stream(logits)), "hl_sample_filtered")
+    return out
+
+
 def gemm_workspace(m: int, n: int, k: int, epilogue: int, device) -> torch.Tensor:
     """A zeroed workspace for hl_gemm_bf16 of this shape, cached per (shape, device) so the
     addresses stay fixed for CUDA-graph capture."""

@@ -373,6 +373,19 @@ int hl_sample(const void* logits, int64_t row_stride, int rows, int vocab, int64
               const float* temperatures, uint64_t seed, void* step_state, int64_t* out_tokens,
               float* out_values, void* stream);
 
+/* hl_sample with the reference's top-k and top-p filters (mini_vllm/layers/sampler.py:13-49):
+ * per row x = logit / T; top_ks[row] in (0, vocab) keeps the k largest x; top_ps[row] < 1 then
+ * keeps, in descending order of x, the tokens whose inclusive cumulative softmax probability over
+ * the top-k set is below top_p (always at least the first); the token is the Gumbel-max draw over
+ * what is kept, with hl_sample's noise, so a row without filters gets exactly hl_sample's token.
+ * Where a filter boundary cuts through equal logits, lower vocabulary ids come first (torch.sort
+ * leaves that order unspecified).  top_ks / top_ps may be NULL (no filter); rows with T <= 0 take
+ * the greedy argmax.  Full-vocabulary rows only (no index_offset: vocabulary shards of a
+ * tensor-parallel head cannot decide a global top-k).  step_state as for hl_sample. */
+int hl_sample_filtered(const void* logits, int64_t row_stride, int rows, int vocab,
+                       const float* temperatures, const int32_t* top_ks, const float* top_ps,
+                       uint64_t seed, void* step_state, int64_t* out_tokens, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

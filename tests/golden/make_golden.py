@@ -325,6 +325,27 @@ def tiny_config():
     return Qwen3Config(**tiny_config_dict())
 
 
+def golden_sampler(ref):
+    """Kept-token masks of the reference Sampler's _apply_top_k / _apply_top_p
+    (mini_vllm/layers/sampler.py:27-49) on seeded rows without equal logits, where the kept set
+    does not depend on torch.sort's tie order."""
+    from mini_vllm.layers.sampler import Sampler
+
+    g = torch.Generator().manual_seed(31)
+    rows, vocab = 48, 97
+    logits = torch.randn(rows, vocab, generator=g) * 3
+    temps = torch.rand(rows, generator=g) + 0.3
+    top_ks = torch.randint(-1, vocab + 3, (rows,), generator=g)
+    top_ks[top_ks == 0] = -1
+    top_ps = (torch.rand(rows, generator=g) * 1.1).clamp(0.01, 1.0)
+    top_ps[::5] = 1.0
+    x = logits / temps.unsqueeze(1)
+    masked = Sampler._apply_top_p(Sampler._apply_top_k(x.clone(), top_ks), top_ps)
+    np.savez_compressed(HERE / "sampler_filters.npz", logits=logits.numpy(), temps=temps.numpy(),
+                        top_ks=top_ks.numpy().astype(np.int32), top_ps=top_ps.numpy(),
+                        keep=torch.isfinite(masked).numpy())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("HILDA_REFERENCE", "/root/reference"))
@@ -349,6 +370,8 @@ def main():
         golden_layers(args.reference)
     if not only or "tiny" in only:
         golden_tiny_model(args.reference)
+    if not only or "sampler" in only:
+        golden_sampler(args.reference)
 
 
 if __name__ == "__main__":

@@ -727,3 +727,100 @@ def test_decode_tensor_core_ignores_nan_past_context(fp8):
     assert torch.isfinite(out.float()).all()
     want = oattn.paged_decode(q, kc, vc, bt, ln, 128 ** -0.5, fp8=fp8)
     assert_close(out, want, **BF16_TOL, what=f"NaN past context fp8={fp8}")
+
+
+# ----------------------------------------------------------------------------- top-k / top-p sampling
+def _filtered_rows(g, rows, vocab, scale=3.0, levels=0):
+    x = torch.randn(rows, vocab, generator=g) * scale
+    if levels:  # few distinct values: filter boundaries cut through groups of equal logits
+        x = torch.randint(0, levels, (rows, vocab), generator=g).float()
+    return x.bfloat16()
+
+
+@pytest.mark.parametrize("vocab", [1000, 151936])
+def test_sample_filtered_without_filters_equals_sample(vocab):
+    """Rows without top-k / top-p (k in {-1, 0, >= V}, p = 1) get exactly hl_sample's token for
+    the same seed and step, greedy rows included."""
+    g = torch.Generator().manual_seed(vocab)
+    rows = 64
+    logits = _filtered_rows(g, rows, vocab).to(DEV)
+    temps = torch.rand(rows, generator=g) + 0.2
+    temps[::4] = 0.0
+    temps = temps.to(DEV)
+    ks = torch.tensor([[-1, 0, vocab, vocab + 5][i % 4] for i in range(rows)], dtype=torch.int32, device=DEV)
+    ps = torch.ones(rows, dtype=torch.float32, device=DEV)
+    for step in range(3):
+        s1 = torch.tensor([step, 0], dtype=torch.int64, device=DEV)
+        s2 = s1.clone()
+        want = kernels.sample(logits, temps, 77, s1)
+        got = kernels.sample_filtered(logits, temps, ks, ps, 77, s2)
+        assert torch.equal(got, want)
+        assert torch.equal(s1, s2)
+    got = kernels.sample_filtered(logits, temps, None, None, 5, None)
+    assert torch.equal(got, kernels.sample(logits, temps, 5, None))
+
+
+@pytest.mark.parametrize("vocab,levels", [(151936, 0), (5000, 8), (3000, 0)])
+def test_sample_filtered_draws_stay_in_the_kept_set(vocab, levels):
+    """Every draw lies in the reference's kept set (oracle/sampler.kept_set, equal logits ordered
+    by index): top-k alone, top-p alone, both, greedy rows with filters; levels > 0 makes the
+    top-k boundary cut through groups of equal logits."""
+    from oracle.sampler import kept_set
+
+    g = torch.Generator().manual_seed(vocab + levels)
+    rows = 48
+    logits = _filtered_rows(g, rows, vocab, levels=levels)
+    temps = torch.rand(rows, generator=g) + 0.3
+    temps[::7] = 0.0
+    ks = torch.randint(1, 300, (rows,), generator=g).to(torch.int32)
+    ks[1::3] = -1
+    ps = (torch.rand(rows, generator=g) * 0.95 + 0.04).to(torch.float32)
+    ps[2::3] = 1.0
+    state = torch.zeros(2, dtype=torch.int64, device=DEV)
+    ld, td, kd, pd = logits.to(DEV), temps.to(DEV), ks.to(DEV), ps.to(DEV)
+    keep = []
+    for r in range(rows):
+        t = float(temps[r])
+        if t <= 0:
+            keep.append(None)
+            continue
+        # top_p + 1e-4: a draw may sit exactly on the boundary that float sums in another order decide
+        keep.append(kept_set(logits[r], t, int(ks[r]), min(1.0, float(ps[r]) + 1e-4)
+                             if float(ps[r]) < 1.0 else 1.0))
+    for _ in range(8):
+        tok = kernels.sample_filtered(ld, td, kd, pd, 99, state).cpu()
+        for r in range(rows):
+            if keep[r] is None:
+                assert int(tok[r]) == int(torch.argmax(logits[r].float())), r
+            else:
+                assert bool(keep[r][int(tok[r])]), (r, int(tok[r]), int(ks[r]), float(ps[r]))
+    assert int(state[0]) == 8
+
+
+@pytest.mark.parametrize("k,p,levels", [(10, 1.0, 0), (-1, 0.8, 0), (12, 0.7, 0), (9, 1.0, 5)])
+def test_sample_filtered_matches_reference_distribution(k, p, levels):
+    """Empirical frequencies over many rows and launches match the reference's distribution
+    (softmax over the kept set, oracle/sampler.filtered_distribution) within sampling error;
+    with levels = 5 the top-k boundary splits a group of equal logits (lowest ids kept)."""
+    from oracle.sampler import filtered_distribution
+
+    g = torch.Generator().manual_seed(41 + k + levels)
+    rows, vocab, T = 512, 40, 0.9
+    base = (torch.randn(vocab, generator=g) * 1.5) if not levels else \
+        torch.randint(0, levels, (vocab,), generator=g).float()
+    base = base.bfloat16()
+    logits = base.repeat(rows, 1).to(DEV)
+    temps = torch.full((rows,), T, dtype=torch.float32, device=DEV)
+    ks = torch.full((rows,), k, dtype=torch.int32, device=DEV)
+    ps = torch.full((rows,), p, dtype=torch.float32, device=DEV)
+    state = torch.zeros(2, dtype=torch.int64, device=DEV)
+    counts = torch.zeros(vocab, dtype=torch.float64)
+    launches = 40
+    for _ in range(launches):
+        tok = kernels.sample_filtered(logits, temps, ks, ps, 4321, state)
+        counts += torch.bincount(tok.cpu(), minlength=vocab).double()
+    freq = counts / counts.sum()
+    want = filtered_distribution(base, T, k, p)
+    assert float(freq[want == 0].sum()) == 0.0
+    n = rows * launches
+    assert float((freq - want).abs().max()) < 5 * float((want * (1 - want) / n).sqrt().max()) + 1e-4

@@ -168,3 +168,31 @@ def test_e4m3_to_f16_bit_placement_is_exact():
     finite = ~torch.isnan(want)
     assert torch.equal(got[finite], want[finite])
     assert int(finite.sum()) == 254
+
+
+def test_sampler_filter_oracle_matches_reference_golden(golden_dir):
+    """oracle/sampler.kept_set against the reference Sampler's own _apply_top_k / _apply_top_p
+    masks (tests/golden/sampler_filters.npz, rows without equal logits)."""
+    from oracle.sampler import kept_set
+
+    g = np.load(golden_dir / "sampler_filters.npz")
+    logits = torch.from_numpy(g["logits"])
+    for r in range(logits.shape[0]):
+        mine = kept_set(logits[r], float(g["temps"][r]), int(g["top_ks"][r]), float(g["top_ps"][r]))
+        ref = torch.from_numpy(g["keep"][r])
+        if float(g["top_ps"][r]) < 1.0:
+            assert torch.equal(mine, ref), r
+        else:
+            # The reference skips _apply_top_p only when no row of the batch filters; here a
+            # top_p = 1 row is filtered anyway and loses exactly the top-k tokens whose float32
+            # inclusive cumsum reaches 1.0 (often the last kept one, whatever its probability).
+            # The restatement (and hl_sample_filtered) keep per-row semantics: no top-p filter.
+            x = logits[r] / torch.tensor(g["temps"][r])
+            order = torch.sort(x, descending=True, stable=True).indices
+            order = order[mine[order]]
+            cum = torch.cumsum(torch.softmax(x[order], 0), 0)
+            dropped = torch.zeros_like(mine)
+            dropped[order[cum >= 1.0]] = True
+            dropped[order[0]] = False
+            assert torch.equal(ref, mine & ~dropped), r
+    assert (g["keep"].sum(1) < logits.shape[1]).sum() > 20  # most rows actually filter something
