@@ -327,21 +327,12 @@ __device__ __forceinline__ float gumbel(uint64_t key, int64_t index) {
   return -__logf(-__logf(u));
 }
 
-__global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int vocab,
-                              int64_t index_offset, const float* __restrict__ temperatures, uint64_t seed,
-                              unsigned long long* __restrict__ step_state, int rows, int64_t* __restrict__ out_tokens,
-                              float* __restrict__ out_values) {
-  const int row = blockIdx.x;
-  const __nv_bfloat16* x = logits + int64_t(row) * row_stride;
-  const float t = temperatures ? temperatures[row] : 0.f;
-  const bool hot = t > 0.f;
-  const float inv_t = hot ? 1.0f / t : 1.0f;
-  __shared__ unsigned long long s_step;
-  if (threadIdx.x == 0) s_step = step_state ? step_state[0] : 0ull;
-  __syncthreads();
-  const uint64_t key = splitmix64(seed ^ splitmix64(s_step * 0x9e3779b97f4a7c15ull + uint64_t(row)));
-  float best = -INFINITY;
-  int bi = 0x7fffffff;
+// Per-thread best (value, index) over a row, threads strided over it with 16-byte loads when the
+// row is aligned: x_i / T + Gumbel noise when hot, else x_i; the lowest index among equals.
+__device__ __forceinline__ void row_best_strided(const __nv_bfloat16* __restrict__ x, int vocab, int64_t index_offset,
+                                                 bool hot, float inv_t, uint64_t key, float& best, int& bi) {
+  best = -INFINITY;
+  bi = 0x7fffffff;
   int head = 0;
   if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
     head = vocab & ~7;
@@ -376,6 +367,24 @@ __global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
       bi = i;
     }
   }
+}
+
+__global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int vocab,
+                              int64_t index_offset, const float* __restrict__ temperatures, uint64_t seed,
+                              unsigned long long* __restrict__ step_state, int rows, int64_t* __restrict__ out_tokens,
+                              float* __restrict__ out_values) {
+  const int row = blockIdx.x;
+  const __nv_bfloat16* x = logits + int64_t(row) * row_stride;
+  const float t = temperatures ? temperatures[row] : 0.f;
+  const bool hot = t > 0.f;
+  const float inv_t = hot ? 1.0f / t : 1.0f;
+  __shared__ unsigned long long s_step;
+  if (threadIdx.x == 0) s_step = step_state ? step_state[0] : 0ull;
+  __syncthreads();
+  const uint64_t key = splitmix64(seed ^ splitmix64(s_step * 0x9e3779b97f4a7c15ull + uint64_t(row)));
+  float best;
+  int bi;
+  row_best_strided(x, vocab, index_offset, hot, inv_t, key, best, bi);
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) {
     const float ob = __shfl_xor_sync(0xffffffffu, best, o);
@@ -734,16 +743,21 @@ __global__ void __launch_bounds__(kFilterThreads) sample_filtered_kernel(
   }
 
   // Gumbel-max (or argmax for a greedy row) over the kept tokens; lowest index among equals.
+  // Rows without a filter take hl_sample's scan, so their token (and cost) is hl_sample's.
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = begin; i < end; ++i) {
-    const uint32_t raw = __ldg(xr + i);
-    if ((filt_k || filt_p) && !in_f(i, order_key(raw))) continue;
-    float v = __uint_as_float(raw << 16);
-    if (hot) v = __fmaf_rn(v, inv_t, gumbel(key, i));
-    if (v > best) {
-      best = v;
-      bi = i;
+  if (!(filt_k || filt_p)) {
+    row_best_strided(logits + int64_t(row) * row_stride, vocab, 0, hot, inv_t, key, best, bi);
+  } else {
+    for (int i = begin; i < end; ++i) {
+      const uint32_t raw = __ldg(xr + i);
+      if (!in_f(i, order_key(raw))) continue;
+      float v = __uint_as_float(raw << 16);
+      if (hot) v = __fmaf_rn(v, inv_t, gumbel(key, i));
+      if (v > best) {
+        best = v;
+        bi = i;
+      }
     }
   }
 #pragma unroll

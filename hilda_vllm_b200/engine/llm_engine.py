@@ -16,7 +16,7 @@ from time import perf_counter
 import torch.multiprocessing as mp
 
 from hilda_vllm_b200.config import Config
-from hilda_vllm_b200.engine.model_runner import ModelRunner, device_sampleable
+from hilda_vllm_b200.engine.model_runner import ModelRunner
 from hilda_vllm_b200.engine.scheduler import Scheduler
 from hilda_vllm_b200.engine.sequence import PLACEHOLDER, Sequence
 from hilda_vllm_b200.sampling_params import SamplingParams
@@ -113,7 +113,7 @@ class LLMEngine:
         if not seqs:
             return self._step_result(early + self._drain(), 0, 0)
         if (self.config.async_decode and not is_prefill and self.scheduler.eos_cannot_stop()
-                and all(s.is_padding or device_sampleable(s.seq) for s in seqs)):
+                and all(s.is_padding or self.model_runner.samples_on_device(s.seq) for s in seqs)):
             if not self.model_runner.can_launch_decode(seqs):
                 early += self._drain()
             handle = self.model_runner.launch_decode(seqs)

@@ -30,7 +30,6 @@ from hilda_vllm_b200.engine.sequence import Sequence
 from hilda_vllm_b200.layers import nvlink_allreduce
 from hilda_vllm_b200.layers.attention import Attention
 from hilda_vllm_b200.layers.nvlink_allreduce import NvlinkAllReduce
-from hilda_vllm_b200.layers.sampler import Sampler
 from hilda_vllm_b200.models.qwen3 import Qwen3ForCausalLM
 from hilda_vllm_b200.utils.context import get_context, reset_context, set_context
 from hilda_vllm_b200.utils.loader import has_checkpoint, load_model, random_init
@@ -60,25 +59,39 @@ def sampling_settings(seqs: list[Sequence]):
             [bool(getattr(s, "greedy", False)) for s in seqs])
 
 
-def device_sampleable(seq) -> bool:
-    """Greedy, or plain temperature sampling (no top-k / top-p): done on the device, inside the
-    decode graph (hl_sample)."""
-    return bool(getattr(seq, "greedy", False)) or (seq.top_k == -1 and seq.top_p >= 1.0)
+def device_sampleable(seq, filters: bool = False) -> bool:
+    """Whether the decode graph samples this sequence on the device: greedy and plain temperature
+    sampling always (hl_sample), top-k / top-p too when `filters` (one GPU holds the whole
+    vocabulary: hl_sample_filtered)."""
+    return bool(getattr(seq, "greedy", False)) or filters or (seq.top_k == -1 and seq.top_p >= 1.0)
 
 
-def decode_temperatures(scheduled_seqs) -> np.ndarray | None:
-    """Per-row temperature for the device sampler (0: greedy argmax, also for padding rows), or
-    None when some row needs top-k / top-p (the host sampler)."""
-    t = np.zeros(len(scheduled_seqs), np.float32)
+def decode_sampling(scheduled_seqs, filters: bool = False) -> np.ndarray | None:
+    """Per-row device sampler settings as one float32 [3, n] array — temperature (0: greedy argmax,
+    also for padding rows), top_k (int32 bits; 0 = no filter), top_p (1 = no filter) — or None when
+    some row needs the host sampler."""
+    n = len(scheduled_seqs)
+    out = np.zeros((3, n), np.float32)
+    out[2] = 1.0
+    ks = out[1].view(np.int32)
     for i, sched in enumerate(scheduled_seqs):
         seq = sched.seq
         if seq is None:
             continue
-        if not device_sampleable(seq):
+        if not device_sampleable(seq, filters):
             return None
         if not getattr(seq, "greedy", False):
-            t[i] = seq.temperature
-    return t
+            out[0, i] = seq.temperature
+            ks[i] = max(int(seq.top_k), 0)
+            out[2, i] = seq.top_p
+    return out
+
+
+def decode_temperatures(scheduled_seqs) -> np.ndarray | None:
+    """Per-row temperature for hl_sample (0: greedy argmax, also for padding rows), or None when
+    some row needs top-k / top-p."""
+    samp = decode_sampling(scheduled_seqs)
+    return None if samp is None else samp[0].copy()
 
 
 def merge_shard_argmax(all_val: torch.Tensor, all_idx: torch.Tensor) -> torch.Tensor:
@@ -184,7 +197,6 @@ class ModelRunner:
                 load_model(self.model, config.model)
             else:
                 random_init(self.model, hf, seed=config.seed, std=config.init_std, device=self.device)
-            self.sampler = Sampler()
             self.vocab_size = hf.vocab_size
             self.warmup_model()
             self.allocate_kv_cache()
@@ -387,10 +399,15 @@ class ModelRunner:
         hq = hf.num_attention_heads // self.world_size
         d = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
         self.decode_workspace = kernels.make_decode_workspace(max_bs, hq, d, mb, self.block_size, dev)
-        # Device sampler: per-slot temperature (0 = greedy), noise seed and launch counter.
-        self.graph_vars["temps"] = torch.zeros(max_bs, dtype=torch.float32, device=dev)
-        self.temps_bufs = [torch.zeros(max_bs, dtype=torch.float32, device="cpu", pin_memory=True) for _ in range(2)]
-        self.temps_host = np.zeros(max_bs, np.float32)  # what graph_vars["temps"] holds
+        # Device sampler: per-slot [temperature (0 = greedy); top_k (int32 bits, 0 = none); top_p],
+        # noise seed and launch counter.  samp_host mirrors what the device holds.
+        self.graph_vars["samp"] = torch.zeros(3, max_bs, dtype=torch.float32, device=dev)
+        self.graph_vars["samp"][2].fill_(1.0)
+        self.graph_vars["temps"] = self.graph_vars["samp"][0]
+        self.samp_bufs = [torch.zeros(3, max_bs, dtype=torch.float32, device="cpu", pin_memory=True) for _ in range(2)]
+        self.samp_host = np.zeros((3, max_bs), np.float32)
+        self.samp_host[2] = 1.0
+        self.device_filters = self.world_size == 1  # top-k / top-p need the whole vocabulary
         self.sample_seed = (int(getattr(self.config, "seed", 0)) * 0x9E3779B1 + 0x5EED) & 0xFFFFFFFFFFFFFFFF
         self.sample_state = torch.zeros(2, dtype=torch.int64, device=dev)
         self.prefill_sample_state = torch.zeros(2, dtype=torch.int64, device=dev)  # rank 0's prefill rows
@@ -458,7 +475,9 @@ class ModelRunner:
         n = logits.shape[0]
         temps = self.graph_vars["temps"][:n]
         if self.world_size == 1:
-            kernels.sample(logits, temps, self.sample_seed, self.sample_state, out=out)
+            samp = self.graph_vars["samp"]
+            kernels.sample_filtered(logits, temps, samp[1].view(torch.int32)[:n], samp[2][:n], self.sample_seed,
+                                    self.sample_state, out=out)
             return
         head = self.model.lm_head
         idx = self.tp_idx[:n]
@@ -493,7 +512,7 @@ class ModelRunner:
         self.packer.buffer = self.packet_host.numpy()
         nbytes = self.packer.build(scheduled_seqs, graph_bs)
         real = [i for i, s in enumerate(scheduled_seqs) if not s.is_padding]
-        temps = decode_temperatures(scheduled_seqs)
+        temps = decode_sampling(scheduled_seqs, self.device_filters)
         samp = None if temps is not None else sampling_settings([scheduled_seqs[i].seq for i in real])
         temps = self._temps_change(temps, graph_bs)
         self.last_decode_batch_info = {"scheduled_bs": bs, "graph_bs": graph_bs, "active_seqs": len(real),
@@ -506,32 +525,40 @@ class ModelRunner:
             out[i] = tokens[i]
         return out
 
-    def _temps_change(self, temps: np.ndarray | None, graph_bs: int) -> np.ndarray | None:
-        """The [0, graph_bs) temperatures to upload this step, or None if the device holds them."""
-        if temps is None:
+    def _temps_change(self, samp: np.ndarray | None, graph_bs: int) -> np.ndarray | None:
+        """The [3, max_bs] sampler settings to upload this step (slots [0, graph_bs) from `samp`,
+        padding slots greedy and unfiltered), or None if the device already holds them."""
+        if samp is None:
             return None
-        full = np.zeros(graph_bs, np.float32)
-        full[: len(temps)] = temps
-        if np.array_equal(self.temps_host[:graph_bs], full):
+        full = self.samp_host.copy()
+        full[:, :graph_bs] = 0.0
+        full[2, :graph_bs] = 1.0
+        full[:, : samp.shape[1]] = samp
+        if np.array_equal(full.view(np.uint32), self.samp_host.view(np.uint32)):
             return None
-        self.temps_host[:graph_bs] = full
+        self.samp_host[:] = full
         return full
 
-    def _upload_temps(self, temps: np.ndarray | None, par: int) -> None:
-        if temps is None:
+    def _upload_temps(self, samp: np.ndarray | None, par: int) -> None:
+        """Copies a whole settings block (what _temps_change returned) to the device; the other
+        ranks receive it with the step and keep their own mirror."""
+        if samp is None:
             return
-        n = len(temps)
-        self.temps_bufs[par][:n].numpy()[:] = temps
-        self.graph_vars["temps"][:n].copy_(self.temps_bufs[par][:n], non_blocking=True)
-        self.temps_host[:n] = temps
+        self.samp_bufs[par].numpy()[:] = samp
+        self.graph_vars["samp"].copy_(self.samp_bufs[par], non_blocking=True)
+        self.samp_host[:] = samp
 
     # ------------------------------------------------------------------ overlapped decode
     # A greedy decode step launched without waiting for its tokens: the argmax leaves them in
     # next_tokens on the device (where the next step's pack kernel reads them) and one
     # asynchronous device->host copy brings them to a pinned buffer that collect_decode() reads
     # after the next step has been launched.
+    def samples_on_device(self, seq) -> bool:
+        return device_sampleable(seq, self.device_filters)
+
     def can_launch_decode(self, scheduled_seqs) -> bool:
-        return decode_temperatures(scheduled_seqs) is not None and not self.packer.needs_host_tokens(scheduled_seqs)
+        return (decode_sampling(scheduled_seqs, self.device_filters) is not None
+                and not self.packer.needs_host_tokens(scheduled_seqs))
 
     @torch.inference_mode()
     def launch_decode(self, scheduled_seqs: list[ScheduledSequence]):
@@ -541,7 +568,7 @@ class ModelRunner:
         self.launch_parity ^= 1
         self.packer.buffer = self.packet_bufs[par].numpy()
         nbytes = self.packer.build(scheduled_seqs, graph_bs)
-        temps = self._temps_change(decode_temperatures(scheduled_seqs), graph_bs)
+        temps = self._temps_change(decode_sampling(scheduled_seqs, self.device_filters), graph_bs)
         real = sum(1 for s in scheduled_seqs if not s.is_padding)
         self.last_decode_batch_info = {"scheduled_bs": bs, "graph_bs": graph_bs, "active_seqs": real,
                                        "padded_slots": bs - real, "pack_events": self.packer.last_num_events}
@@ -580,21 +607,16 @@ class ModelRunner:
         return self.tokens_bufs[par][:bs].tolist()
 
     def _sample_rows(self, logits: torch.Tensor, samp) -> list[int]:
+        """Tokens for rows of full-vocabulary logits (rank 0): greedy argmax, or a device draw with
+        the request's temperature, top-k and top-p (hl_sample_filtered)."""
         if samp is None:
             return kernels.argmax(logits).tolist()
         temps, ks, ps, greedy = samp
         dev = self.device
-        if all(g or (k == -1 and p >= 1.0) for g, k, p in zip(greedy, ks, ps)):
-            t = torch.tensor([0.0 if g else x for g, x in zip(greedy, temps)], dtype=torch.float32, device=dev)
-            return kernels.sample(logits, t, self.sample_seed ^ 0xA5A5, self.prefill_sample_state).tolist()
-        sampled = self.sampler(logits, torch.tensor(temps, dtype=torch.float32, device=dev),
-                               torch.tensor(ks, dtype=torch.int32, device=dev),
-                               torch.tensor(ps, dtype=torch.float32, device=dev))
-        greedy_rows = [i for i, g in enumerate(greedy) if g]
-        if greedy_rows:
-            idx = torch.tensor(greedy_rows, device=dev)
-            sampled[idx] = kernels.argmax(logits[idx].contiguous())
-        return sampled.tolist()
+        t = torch.tensor([0.0 if g else x for g, x in zip(greedy, temps)], dtype=torch.float32, device=dev)
+        k = torch.tensor([0 if g else max(int(x), 0) for g, x in zip(greedy, ks)], dtype=torch.int32, device=dev)
+        p = torch.tensor([1.0 if g else x for g, x in zip(greedy, ps)], dtype=torch.float32, device=dev)
+        return kernels.sample_filtered(logits, t, k, p, self.sample_seed ^ 0xA5A5, self.prefill_sample_state).tolist()
 
     def _gather_logits(self, logits: torch.Tensor) -> torch.Tensor | None:
         if self.world_size == 1:
@@ -713,8 +735,10 @@ class ModelRunner:
         gv["context_lens"].zero_()
         gv["slot_mapping"].fill_(-1)
         gv["positions"].zero_()
-        gv["temps"].zero_()
-        self.temps_host[:] = 0.0
+        gv["samp"].zero_()
+        gv["samp"][2].fill_(1.0)
+        self.samp_host[:] = 0.0
+        self.samp_host[2] = 1.0
         self.packer = DecodePacker(self.max_bs, self.max_num_decode_blocks, self.packet_host.numpy())
 
     @torch.inference_mode()

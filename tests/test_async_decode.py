@@ -16,7 +16,7 @@ import pytest
 
 from hilda_vllm_b200.engine.decode_packer import DecodePacker
 from hilda_vllm_b200.engine.llm_engine import LLMEngine
-from hilda_vllm_b200.engine.model_runner import decode_temperatures
+from hilda_vllm_b200.engine.model_runner import decode_sampling, device_sampleable
 from hilda_vllm_b200.engine.scheduler import Scheduler
 from hilda_vllm_b200.engine.sequence import PLACEHOLDER, Sequence, SequenceStatus
 from hilda_vllm_b200.sampling_params import SamplingParams
@@ -35,7 +35,8 @@ def tok(seq_id: int, pos: int) -> int:
 
 
 class FakeRunner:
-    def __init__(self, max_bs: int, block_size: int, max_model_len: int):
+    def __init__(self, max_bs: int, block_size: int, max_model_len: int, device_filters: bool = False):
+        self.device_filters = device_filters  # ModelRunner: True on one GPU (hl_sample_filtered)
         self.max_blocks = -(-max_model_len // block_size)
         self.block_size = block_size
         self.packer = DecodePacker(max_bs, self.max_blocks)
@@ -91,8 +92,12 @@ class FakeRunner:
         self.packer.note_sampled(len(scheduled), tokens)
         return [None if s.is_padding else t for s, t in zip(scheduled, tokens)]
 
+    def samples_on_device(self, seq):
+        return device_sampleable(seq, self.device_filters)
+
     def can_launch_decode(self, scheduled):
-        return decode_temperatures(scheduled) is not None and not self.packer.needs_host_tokens(scheduled)
+        return (decode_sampling(scheduled, self.device_filters) is not None
+                and not self.packer.needs_host_tokens(scheduled))
 
     def launch_decode(self, scheduled):
         tokens = self._device_step(scheduled)
@@ -105,7 +110,7 @@ class FakeRunner:
 
 
 def make_engine(async_decode: bool, num_blocks: int, max_num_seqs: int = 8, block_size: int = 16,
-                max_model_len: int = 256, drop_victim_token: bool = True):
+                max_model_len: int = 256, drop_victim_token: bool = True, device_filters: bool = False):
     cfg = SimpleNamespace(kvcache_block_size=block_size, max_num_seqs=max_num_seqs, max_num_batched_tokens=128,
                           eos=-1, enable_chunked_prefill=True, chunked_prefill_size=64, chunked_prefill_min_size=16,
                           chunked_prefill_tile_size=16, num_kvcache_blocks=num_blocks, async_decode=async_decode,
@@ -114,7 +119,7 @@ def make_engine(async_decode: bool, num_blocks: int, max_num_seqs: int = 8, bloc
     eng = LLMEngine.__new__(LLMEngine)
     eng.config = cfg
     eng.scheduler = Scheduler(cfg)
-    eng.model_runner = FakeRunner(max_num_seqs, block_size, max_model_len)
+    eng.model_runner = FakeRunner(max_num_seqs, block_size, max_model_len, device_filters)
     eng._inflight = None
     eng.last_step_diagnostics = None
     return eng
@@ -166,12 +171,13 @@ def test_overlapped_decode_matches_synchronous(num_blocks, drop_victim_token):
     assert results[False][2] == 0
 
 
-@pytest.mark.parametrize("top_k,overlapped", [(-1, True), (5, False)])
-def test_which_sampled_sequences_overlap(top_k, overlapped):
-    """Plain temperature sampling runs on the device and overlaps; top-k needs the host sampler,
-    so those steps run synchronously."""
+@pytest.mark.parametrize("top_k,device_filters,overlapped", [(-1, False, True), (5, False, False), (5, True, True)])
+def test_which_sampled_sequences_overlap(top_k, device_filters, overlapped):
+    """Plain temperature sampling runs on the device and overlaps; top-k overlaps too where the
+    device sampler has the whole vocabulary (one GPU), else it needs the host sampler and those
+    steps run synchronously."""
     Sequence.counter = iter(range(10_000))
-    eng = make_engine(True, 200)
+    eng = make_engine(True, 200, device_filters=device_filters)
     rng = np.random.default_rng(3)
     prompts = [rng.integers(0, 4000, 10).tolist() for _ in range(4)]
     seqs, outputs = drive(eng, prompts, [12] * 4, greedy=False, top_k=top_k)

@@ -140,9 +140,9 @@ def test_overlapped_decode_equals_synchronous(tmp_path, golden_dir):
 
 
 def test_temperature_sampling_on_device_overlapped_equals_synchronous(tmp_path, golden_dir):
-    """Temperature-sampled requests (top_k -1, top_p 1) are sampled inside the decode graph
-    (Gumbel-max, seeded noise), so overlapped and synchronous stepping draw the same tokens;
-    a top-k request falls back to the host sampler and still completes."""
+    """Sampled requests — plain temperature, and with top-k / top-p — are sampled on the device
+    inside the decode graph (Gumbel-max, seeded noise; hl_sample_filtered on one GPU), so
+    overlapped and synchronous stepping draw the same tokens."""
     d = tiny_dir(tmp_path, golden_dir)
     g = torch.Generator().manual_seed(31)
     prompts = [torch.randint(0, 512, (int(n),), generator=g).tolist() for n in (7, 120, 33, 260)]
@@ -152,12 +152,14 @@ def test_temperature_sampling_on_device_overlapped_equals_synchronous(tmp_path, 
         llm = LLM(str(d), load_format="random", seed=7, max_num_seqs=8, max_model_len=1024,
                   max_num_batched_tokens=2048, kvcache_block_cap=32, async_decode=mode, gpu_memory_utilization=0.5)
         res[mode] = [o["token_ids"] for o in llm.generate(prompts, sps, use_tqdm=False)]
-        if mode:
-            topk = llm.generate(prompts[:2], SamplingParams(temperature=0.6, top_k=5, max_tokens=12, ignore_eos=True),
-                                use_tqdm=False)
-            assert all(len(o["token_ids"]) == 12 for o in topk)
+        # top-k / top-p requests: sampled on the device too (one GPU), so they overlap as well
+        filt = [SamplingParams(temperature=0.8, top_k=[5, -1, 40, 3][i], top_p=[1.0, 0.9, 0.7, 0.5][i],
+                               max_tokens=24, ignore_eos=True) for i in range(len(prompts))]
+        res[("filt", mode)] = [o["token_ids"] for o in llm.generate(prompts, filt, use_tqdm=False)]
         llm.exit()
     assert res[True] == res[False]
+    assert res[("filt", True)] == res[("filt", False)]
+    assert all(len(t) == 24 for t in res[("filt", True)])
     assert all(len(t) == 40 for t in res[True])
     # sampling, not greedy: the runs differ from the argmax path somewhere
     assert any(len(set(t)) > 1 for t in res[True])
@@ -221,3 +223,19 @@ def test_tensor_parallel_2_matches_oracle(tmp_path, golden_dir):
     checked, exact, ties = check_against_oracle(hf, 0, prompts, [o["token_ids"] for o in outs])
     print(f"TP=2 greedy: {exact}/{checked} exact argmax matches, {len(ties)} bf16 ties")
     assert checked == len(prompts) * (steps + 1) and exact >= 0.9 * checked
+
+
+def test_top_k_1_equals_greedy_oracle(tmp_path, golden_dir):
+    """top_k = 1 leaves one token whatever the temperature: the device filter must reproduce the
+    greedy tokens (prefill rows and the overlapped decode graph alike)."""
+    d = tiny_dir(tmp_path, golden_dir)
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 512, (int(n),), generator=g).tolist() for n in (9, 64, 200)]
+    llm = LLM(str(d), load_format="random", seed=7, max_num_seqs=8, max_model_len=1024,
+              max_num_batched_tokens=2048, kvcache_block_cap=32, gpu_memory_utilization=0.5)
+    greedy = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(greedy=True, max_tokens=20,
+                                                                           ignore_eos=True), use_tqdm=False)]
+    top1 = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(temperature=1.3, top_k=1, max_tokens=20,
+                                                                         ignore_eos=True), use_tqdm=False)]
+    llm.exit()
+    assert top1 == greedy
