@@ -105,6 +105,9 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row
                                     void* __restrict__ v_cache, const int32_t* __restrict__ slot_mapping,
                                     int64_t num_slots, const float* __restrict__ k_scale,
                                     const float* __restrict__ v_scale) {
+  // Let the next kernel (the decode attention, launched as a programmatic dependent) start its
+  // prologue now; it waits for this grid's writes before it reads q or the newest K/V slot.
+  asm volatile("griddepcontrol.launch_dependents;");
   const int heads = num_q_heads + (KV == kNoStore ? 1 : 2) * num_kv_heads;
   const int64_t gid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;  // (token, head) index
   const int ln = threadIdx.x & 15;

@@ -44,6 +44,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 // Smallest GQA ratio that hl_paged_decode hands to the tensor-core kernel.
 constexpr int kTcMinGroupBf16 = 4;
 constexpr int kTcMinGroupFp8 = 4;
+constexpr int kMaxDecodeDevices = 64;
 
 __host__ __device__ constexpr int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
@@ -225,9 +226,17 @@ paged_decode_kernel(const DecodeParams p) {
   }
   __syncthreads();
 
+  // Programmatic dependent launch: this grid may start while the kernel before it (the fused
+  // QK-norm/RoPE/KV-store of this layer) still runs.  That kernel writes q and, for each
+  // sequence, only the newest token's K/V slot, which lies in the sequence's last split; every
+  // earlier kernel has finished.  So context lengths, block tables and the pages of earlier
+  // splits may be read at once, and the last split and q only after griddepcontrol.wait (a no-op
+  // when the launch carries no programmatic dependency).
+  const bool newest_here = tok1 == L;
   if (bad_block) {
     if (tid == 0) atomicOr(ws_err, 2);
   } else if (tid == 0) {
+    if (newest_here) asm volatile("griddepcontrol.wait;" ::: "memory");
     const int npre = ntiles < kStages ? ntiles : kStages;
     for (int i = 0; i < npre; ++i) {
       mbar_arrive_expect_tx(&full[i], 2 * kT * kRow);
@@ -236,6 +245,7 @@ paged_decode_kernel(const DecodeParams p) {
     }
   }
 
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // Query slice of the G query heads that share KV head h, pre-scaled so that the
   // softmax runs in base 2 (and, for FP8, with k_scale folded in).
   float2 qs[G][4];
@@ -494,19 +504,40 @@ paged_decode_kernel(const DecodeParams p) {
 template <bool FP8, int G, int HK>
 int launch_decode(const DecodeParams& p, cudaStream_t stream) {
   constexpr size_t smem = size_t(kStages) * 2 * kTileBytes + kStages * sizeof(uint64_t) + 16;
-  static bool configured = false;  // first call happens before any graph capture
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<FP8, G, HK>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  // The shared-memory opt-in is per device; the first call on a device happens before any graph
+  // capture (the engine's eager warm-up).
+  static std::atomic<bool> configured[kMaxDecodeDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDecodeDevices) {
+    set_error("hl_paged_decode: no usable current device");
+    return HL_ERR_CUDA;
+  }
+  if (!configured[dev].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(paged_decode_kernel<FP8, G, HK>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) {
       set_error("hl_paged_decode: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
       return HL_ERR_CUDA;
     }
-    configured = true;
+    configured[dev].store(true, std::memory_order_release);
   }
-  dim3 grid(p.max_splits, p.batch);
-  paged_decode_kernel<FP8, G, HK><<<grid, kDecodeThreads, smem, stream>>>(p);
-  HL_CHECK_LAUNCH("hl_paged_decode");
+  // Launched as a programmatic dependent of the previous kernel in the stream (see the kernel's
+  // griddepcontrol.wait placement).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.max_splits, p.batch);
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, paged_decode_kernel<FP8, G, HK>, p);
+  if (e != cudaSuccess) {
+    set_error("hl_paged_decode: launch failed: %s", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
   return HL_OK;
 }
 

@@ -793,6 +793,9 @@ class ModelRunner:
         stream = torch.cuda.current_stream()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 20
+        # Nothing in flight before the start event: the decode kernel is a programmatic dependent
+        # launch and would otherwise begin under the last warm-up launch's tail.
+        torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(reps):
             launch()
