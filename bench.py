@@ -353,7 +353,7 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(sweep_s * 1e3, 2), "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights std 0.02, random token ids)",
         "config": {"workload": "qwen3-0.6b decode-heavy: 256 seqs, prompt 64, 1024 greedy tokens, ignore_eos, "
                                "block 256, CUDA graphs (BASELINE configs[1])",
@@ -848,7 +848,7 @@ def run_workload(args):
     e2e = fields["e2e"]
     line = {"metric": f"{desc}: output tok/s", "value": e2e["value"], "unit": "tok/s", "n_gpus": args.gpus,
             "steps": 1, "warmup": 1, "ms_per_step": round(e2e["wall_s"] * 1e3, 1), "higher_is_better": True,
-            "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
+            "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic", "config": {"workload": args.workload, "desc": desc,
                                                              "parallelism": f"tp{args.gpus}"},
             **fields}
