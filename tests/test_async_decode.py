@@ -202,3 +202,35 @@ def test_deferred_page_hash_equals_synchronous_hash():
             registered.append(sorted(bm.hash_to_block_id.items()))
         hashes[mode] = registered[-1]
     assert hashes[True] == hashes[False] and len(hashes[True]) >= 2
+
+
+def test_decode_sampling_settings_encoding():
+    """Per-row device sampler settings: greedy and padding rows are (T 0, k 0, p 1); top_k travels
+    as int32 bits in the float32 block (-1 -> 0, no filter); rows with filters make the whole
+    batch host-sampled unless the device has the full vocabulary."""
+    from hilda_vllm_b200.engine.model_runner import ModelRunner
+
+    Sequence.counter = iter(range(10_000))
+    mk = lambda **kw: Sequence([1, 2, 3], SamplingParams(max_tokens=4, **kw))
+    seqs = [mk(greedy=True), mk(temperature=0.7), mk(temperature=1.2, top_k=7, top_p=0.9), None]
+    sched = [SimpleNamespace(seq=s, is_padding=s is None) for s in seqs]
+    assert decode_sampling(sched, filters=False) is None
+    out = decode_sampling(sched, filters=True)
+    assert out.dtype == np.float32 and out.shape == (3, 4)
+    np.testing.assert_array_equal(out[0], np.array([0.0, 0.7, 1.2, 0.0], np.float32))
+    np.testing.assert_array_equal(out[1].view(np.int32), [0, 0, 7, 0])
+    np.testing.assert_array_equal(out[2], np.array([1.0, 1.0, 0.9, 1.0], np.float32))
+    plain = decode_sampling(sched[:2], filters=False)
+    np.testing.assert_array_equal(plain[1].view(np.int32), [0, 0])
+
+    # upload only on change: the mirror starts as "greedy, unfiltered" everywhere
+    runner = SimpleNamespace(samp_host=np.zeros((3, 8), np.float32))
+    runner.samp_host[2] = 1.0
+    change = ModelRunner._temps_change
+    assert change(runner, decode_sampling(sched[:1], True), 1) is None  # greedy: nothing to send
+    block = change(runner, out, 4)
+    assert block is not None and block.shape == (3, 8)
+    np.testing.assert_array_equal(block[:, :4].view(np.uint32), out.view(np.uint32))
+    assert change(runner, out, 4) is None  # the device already holds it
+    assert change(runner, out[:, :2].copy(), 4) is not None  # rows 2, 3 go back to greedy
+    np.testing.assert_array_equal(runner.samp_host[1, :4].view(np.int32), [0, 0, 0, 0])
