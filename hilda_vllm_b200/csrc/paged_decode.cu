@@ -19,6 +19,10 @@
 // heads of the KV head are kept in registers, so every K/V byte is read from HBM once and
 // used G times.  Splits of one sequence are combined by the CTA that finishes last (atomic
 // ticket in the workspace); sequences that fit in one split write the output directly.
+//
+// Kernel choice (hl_paged_decode): this CUDA-core kernel serves GQA ratios 1 and 2; ratios >= 4
+// (with at most 2048 sequences) go to the tcgen05 kernel of paged_decode_tc.cu, whose cost does
+// not grow with the number of query heads per KV head.
 #include "hl_common.cuh"
 
 #include <atomic>
