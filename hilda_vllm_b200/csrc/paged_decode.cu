@@ -169,14 +169,97 @@ __device__ __forceinline__ void merge_state(float (&m)[G], float (&l)[G], float2
   }
 }
 
+template <bool B>
+struct BoolTag {
+  static constexpr bool value = B;
+};
+
+// Softmax reference maximum moves only when a tile's maximum exceeds it by more than this (log2
+// units): probabilities stay <= 2^8 (exact range in fp32) and the accumulators are rescaled in
+// few tiles instead of every one.
+constexpr float kLazyLog2 = 8.f;
+
+// One staged tile of kT tokens for this warp's KV head: the half-warp's kTPH tokens, all G query
+// heads.  kFull: every token of the tile is inside the context (no per-token checks).
+template <bool FP8, int G, int HK, class FullTag>
+__device__ __forceinline__ void decode_tile(FullTag, const uint8_t* Ks, int tile_tok0, int tok1, int phase, int hw,
+                                            int ln, int h, const float2 (&qs)[G][4], float (&m)[G], float (&l)[G],
+                                            float2 (&acc)[G][4]) {
+  constexpr bool kFull = FullTag::value;
+  using Tr = Traits<FP8, HK>;
+  constexpr int kTPW = Tr::kTPW;
+  constexpr int kTPH = Tr::kTPH;
+  constexpr int kRow = Tr::kRowBytes;
+  const uint8_t* Vs = Ks + kTileBytes;
+  // Partial q.k over this lane's 8 dimensions, packed fp32x2 FMAs; sc[j * kTPH + i].
+  float sc[G * kTPH];
+  bool valid[kTPH];
+#pragma unroll
+  for (int i = 0; i < kTPH; ++i) {
+    const int tt = phase * kTPW + 2 * i + hw;
+    valid[i] = kFull || tile_tok0 + tt < tok1;
+    float2 kx[4];
+    load8x2<FP8>(Ks + tt * kRow + (h * kHeadDim + 8 * ln) * Tr::kElem, kx);
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      float2 a = __fmul2_rn(qs[j][0], kx[0]);
+      a = __ffma2_rn(qs[j][1], kx[1], a);
+      a = __ffma2_rn(qs[j][2], kx[2], a);
+      a = __ffma2_rn(qs[j][3], kx[3], a);
+      sc[j * kTPH + i] = a.x + a.y;
+    }
+  }
+  halfwarp_allreduce<G * kTPH>(sc, ln, hw);
+
+  float pr[G][kTPH];
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    float mt = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kTPH; ++i)
+      if (valid[i]) mt = fmaxf(mt, sc[j * kTPH + i]);
+    if (mt > m[j] + kLazyLog2) {  // also the first tile with a token (m = -inf)
+      const float corr = exp2f(m[j] - mt);
+      l[j] *= corr;
+      const float2 c2 = make_float2(corr, corr);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[j][c] = __fmul2_rn(acc[j][c], c2);
+      m[j] = mt;
+    }
+    if (m[j] == -INFINITY) {
+#pragma unroll
+      for (int i = 0; i < kTPH; ++i) pr[j][i] = 0.f;
+      continue;
+    }
+    float ps = 0.f;
+#pragma unroll
+    for (int i = 0; i < kTPH; ++i) {
+      pr[j][i] = valid[i] ? exp2f(sc[j * kTPH + i] - m[j]) : 0.f;
+      ps += pr[j][i];
+    }
+    l[j] += ps;
+  }
+#pragma unroll
+  for (int i = 0; i < kTPH; ++i) {
+    if (!valid[i]) continue;  // never touch V rows past the context (may hold NaN bits)
+    const int tt = phase * kTPW + 2 * i + hw;
+    float2 vx[4];
+    load8x2<FP8>(Vs + tt * kRow + (h * kHeadDim + 8 * ln) * Tr::kElem, vx);
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const float2 p2 = make_float2(pr[j][i], pr[j][i]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[j][c] = __ffma2_rn(p2, vx[c], acc[j][c]);
+    }
+  }
+}
+
 template <bool FP8, int G, int HK>
 __global__ void __launch_bounds__(kDecodeThreads, (G <= 2 ? 3 : (G <= 4 ? 2 : 1)))
 paged_decode_kernel(const DecodeParams p) {
   using Tr = Traits<FP8, HK>;
   constexpr int kT = Tr::kT;
   constexpr int kRow = Tr::kRowBytes;
-  constexpr int kTPW = Tr::kTPW;
-  constexpr int kTPH = Tr::kTPH;
   constexpr int kHq = HK * G;
 
   extern __shared__ __align__(128) uint8_t smem[];
@@ -285,70 +368,12 @@ paged_decode_kernel(const DecodeParams p) {
       // below, so no thread is left alone in a shuffle or a __syncthreads.
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], (t / kStages) & 1));
       if (ok) {
-      const uint8_t* Ks = smem + stage * 2 * kTileBytes;
-      const uint8_t* Vs = Ks + kTileBytes;
-      const int tile_tok0 = tok0 + t * kT;
-
-      // Partial q.k over this lane's 8 dimensions, packed fp32x2 FMAs; sc[j * kTPH + i].
-      float sc[G * kTPH];
-      bool valid[kTPH];
-#pragma unroll
-      for (int i = 0; i < kTPH; ++i) {
-        const int tt = phase * kTPW + 2 * i + hw;
-        valid[i] = tile_tok0 + tt < tok1;
-        float2 kx[4];
-        load8x2<FP8>(Ks + tt * kRow + (h * kHeadDim + 8 * ln) * Tr::kElem, kx);
-#pragma unroll
-        for (int j = 0; j < G; ++j) {
-          float2 a = __fmul2_rn(qs[j][0], kx[0]);
-          a = __ffma2_rn(qs[j][1], kx[1], a);
-          a = __ffma2_rn(qs[j][2], kx[2], a);
-          a = __ffma2_rn(qs[j][3], kx[3], a);
-          sc[j * kTPH + i] = a.x + a.y;
-        }
-      }
-      halfwarp_allreduce<G * kTPH>(sc, ln, hw);
-
-      float pr[G][kTPH];
-#pragma unroll
-      for (int j = 0; j < G; ++j) {
-        float mt = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < kTPH; ++i)
-          if (valid[i]) mt = fmaxf(mt, sc[j * kTPH + i]);
-        const float mn = fmaxf(m[j], mt);
-        if (mn == -INFINITY) {
-#pragma unroll
-          for (int i = 0; i < kTPH; ++i) pr[j][i] = 0.f;
-          continue;
-        }
-        const float corr = exp2f(m[j] - mn);
-        float ps = 0.f;
-#pragma unroll
-        for (int i = 0; i < kTPH; ++i) {
-          pr[j][i] = valid[i] ? exp2f(sc[j * kTPH + i] - mn) : 0.f;
-          ps += pr[j][i];
-        }
-        l[j] = l[j] * corr + ps;
-        const float2 c2 = make_float2(corr, corr);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[j][c] = __fmul2_rn(acc[j][c], c2);
-        m[j] = mn;
-      }
-#pragma unroll
-      for (int i = 0; i < kTPH; ++i) {
-        if (!valid[i]) continue;  // never touch V rows past the context (may hold NaN bits)
-        const int tt = phase * kTPW + 2 * i + hw;
-        float2 vx[4];
-        load8x2<FP8>(Vs + tt * kRow + (h * kHeadDim + 8 * ln) * Tr::kElem, vx);
-#pragma unroll
-        for (int j = 0; j < G; ++j) {
-          const float2 p2 = make_float2(pr[j][i], pr[j][i]);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) acc[j][c] = __ffma2_rn(p2, vx[c], acc[j][c]);
-        }
-      }
-
+        const uint8_t* Ks = smem + stage * 2 * kTileBytes;
+        const int tile_tok0 = tok0 + t * kT;
+        if (tile_tok0 + kT <= tok1)
+          decode_tile<FP8, G, HK>(BoolTag<true>{}, Ks, tile_tok0, tok1, phase, hw, ln, h, qs, m, l, acc);
+        else
+          decode_tile<FP8, G, HK>(BoolTag<false>{}, Ks, tile_tok0, tok1, phase, hw, ln, h, qs, m, l, acc);
       }  // ok
       // Every warp is done with this stage: refill it (or leave together on a timeout).
       if (__syncthreads_or(!ok)) {
