@@ -281,16 +281,16 @@ def run_ours(args):
     hk = hf.num_key_value_heads // world
     g_ratio = hf.num_attention_heads // hf.num_key_value_heads
     # DRAM traffic per launch: one ncu capture of this kernel on the config-2 mid-job launch
-    # (`bench.py --profile decode-kernel`: 614.02 MB read + 12.30 MB written for 609.6 MB of
+    # (`bench.py --profile decode-kernel`: 614.70 MB read + 12.28 MB written for 609.6 MB of
     # algorithmic bytes), scaled to this run's average launch — the traffic is the cache bytes
     # read once plus the split-K partials, so it grows with the bytes processed.
-    ncu_ratio = (614.02 + 12.30) / 609.6 if (g_ratio == 2 and hk == 8) else None
+    ncu_ratio = (614.70 + 12.28) / 609.6 if (g_ratio == 2 and hk == 8) else None
     bpl = kbytes / max(1, len(samples))
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4),
                 "traffic": int(ncu_ratio * bpl) if ncu_ratio else None,
                 "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one config-2 mid-job launch "
-                                   "(bench.py --profile decode-kernel), 1.027x algorithmic, scaled to this run's "
+                                   "(bench.py --profile decode-kernel), 1.028x algorithmic, scaled to this run's "
                                    "average launch") if ncu_ratio else None,
                 "kernel": f"paged_decode_kernel<bf16,G={g_ratio},Hk={hk}>",
                 "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "of fallback (6650 GB/s)",
