@@ -282,6 +282,10 @@ paged_decode_kernel(const DecodeParams p) {
   float* ws_o = reinterpret_cast<float*>(
       p.ws + kWsMlOff + align256(int64_t(p.batch) * p.max_splits * kHq * sizeof(float2)));
 
+  // Launched as a programmatic dependent of the previous kernel in the stream: the CTAs may be
+  // scheduled while it finishes, but nothing earlier kernels wrote (context lengths, block
+  // tables, q, the cache) is read before griddepcontrol.wait, so any predecessor is safe.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   int L = p.context_lens[b];
   const int Lmax = p.max_blocks * p.block_size;
   L = L < 0 ? 0 : (L > Lmax ? Lmax : L);
@@ -313,17 +317,9 @@ paged_decode_kernel(const DecodeParams p) {
   }
   __syncthreads();
 
-  // Programmatic dependent launch: this grid may start while the kernel before it (the fused
-  // QK-norm/RoPE/KV-store of this layer) still runs.  That kernel writes q and, for each
-  // sequence, only the newest token's K/V slot, which lies in the sequence's last split; every
-  // earlier kernel has finished.  So context lengths, block tables and the pages of earlier
-  // splits may be read at once, and the last split and q only after griddepcontrol.wait (a no-op
-  // when the launch carries no programmatic dependency).
-  const bool newest_here = tok1 == L;
   if (bad_block) {
     if (tid == 0) atomicOr(ws_err, 2);
   } else if (tid == 0) {
-    if (newest_here) asm volatile("griddepcontrol.wait;" ::: "memory");
     const int npre = ntiles < kStages ? ntiles : kStages;
     for (int i = 0; i < npre; ++i) {
       mbar_arrive_expect_tx(&full[i], 2 * kT * kRow);
@@ -332,7 +328,6 @@ paged_decode_kernel(const DecodeParams p) {
     }
   }
 
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   // Query slice of the G query heads that share KV head h, pre-scaled so that the
   // softmax runs in base 2 (and, for FP8, with k_scale folded in).
   float2 qs[G][4];
