@@ -67,8 +67,8 @@ constexpr int kSmemTc = kOffBarTc + kBarBytes + 1024;
 //   S^T = K Q^T runs as kind::f8f6f4 straight from the staged K bytes.  Q, after an exact
 //   power-of-two shift that puts its largest |q| in [2^7, 2^8), is split into two e4m3 terms,
 //   q1 = q truncated to 4 significant bits and q2 = q - q1 (the other <= 4 bits of a bf16), so
-//   the two accumulating passes give K Q^T exactly (only components ~2^17 below the head's
-//   largest lose their last bits to the e4m3 subnormal grid).
+//   the two terms reproduce every component within 2^8 of the head's largest exactly; smaller
+//   ones lose low bits to the e4m3 subnormal grid, at most 2^-16 of the largest.
 //   O^T += V^T P^T needs P with f16 range and precision, so four converter warps turn each V
 //   row into f16 (e4m3 -> f16 x 2^-8, exact, by bit placement) in a double-buffered tile, and
 //   the product runs as kind::f16.

@@ -196,3 +196,44 @@ def test_sampler_filter_oracle_matches_reference_golden(golden_dir):
             dropped[order[0]] = False
             assert torch.equal(ref, mine & ~dropped), r
     assert (g["keep"].sum(1) < logits.shape[1]).sum() > 20  # most rows actually filter something
+
+
+def _e4m3_head(x: np.ndarray) -> np.ndarray:
+    """x truncated to 4 significant bits (>= 2^-6) or to the 2^-9 grid (below): the larger e4m3
+    term of the tensor-core FP8 decode's Q split (restated bit for bit)."""
+    a = np.abs(x).astype(np.float32)
+    big = (a.view(np.uint32) & np.uint32(0xFFF00000)).view(np.float32)
+    small = (np.floor(a * np.float32(512)) * np.float32(1 / 512)).astype(np.float32)
+    return np.copysign(np.where(a >= np.float32(0.015625), big, small), x).astype(np.float32)
+
+
+def _e4m3_byte(x: np.ndarray) -> np.ndarray:
+    """e4m3 byte of a value on the e4m3 grid (truncating below it), |x| < 2^8 (restated)."""
+    u = x.astype(np.float32).view(np.uint32).astype(np.int64)
+    sign = (u >> 24) & 0x80
+    e = ((u >> 23) & 0xFF) - 120
+    m = (u >> 20) & 7
+    sh = 1 - e
+    sub = np.where(sh <= 4, (8 | m) >> np.clip(sh, 0, 31), 0)
+    return (sign | np.where(e >= 1, (e << 3) | m, sub)).astype(np.uint8)
+
+
+def test_fp8_decode_q_split_is_exact():
+    """The tensor-core FP8 decode feeds Q to a kind::f8f6f4 MMA as two e4m3 terms: after a
+    power-of-two shift putting the head's largest |q| in [2^7, 2^8), q1 = q truncated to 4
+    significant bits and q2 = q - q1.  Over every finite bf16 value (as the largest component,
+    and as a component 2^k below it): q1 + q2 reproduces q exactly whenever q >= 2^-1 after the
+    shift (8 of a bf16's bits fit in two 4-bit terms), and within 2^-9 below that."""
+    bits = np.arange(65536, dtype=np.uint32)
+    vals = (bits << 16).view(np.float32)
+    vals = vals[np.isfinite(vals) & (vals != 0)]
+    e4 = lambda b: torch.from_numpy(b).view(torch.float8_e4m3fn).float().numpy()
+    for k in (0, 3, 7, 12, 20):  # the component sits 2^k below the head's largest |q|
+        e = np.floor(np.log2(np.abs(vals))).astype(np.int64)
+        x = np.ldexp(np.abs(vals) / np.exp2(e), 7 - k).astype(np.float32) * np.sign(vals)  # same mantissa
+        h = _e4m3_head(x)
+        rec = e4(_e4m3_byte(h)) + e4(_e4m3_byte((x - h).astype(np.float32)))
+        err = np.abs(rec - x.astype(np.float64))
+        exact = np.abs(x) >= 0.5
+        assert np.all(err[exact] == 0), k
+        assert np.all(err <= 2.0 ** -9), (k, float(err.max()))
