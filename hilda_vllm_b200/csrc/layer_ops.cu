@@ -679,7 +679,9 @@ __global__ void __launch_bounds__(kFilterThreads) sample_filtered_kernel(
         atomicAdd(&sh.hm[kk >> 8], e);
       }
       z = block_sum(z, sh);
-      const float thr = top_p * z;
+      // top_p <= 0 keeps only the first token, as the reference's "cumsum < top_p, first always
+      // kept" does; z >= 1 (the top token's term), so the floor stays positive.
+      const float thr = fmaxf(top_p, 1e-30f) * z;
       if (warp == 0) {
         float above;
         const int c1 = find_from_top(sh.hm, thr, &above);

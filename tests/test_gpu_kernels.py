@@ -776,6 +776,7 @@ def test_sample_filtered_draws_stay_in_the_kept_set(vocab, levels):
     ks[1::3] = -1
     ps = (torch.rand(rows, generator=g) * 0.95 + 0.04).to(torch.float32)
     ps[2::3] = 1.0
+    ps[3] = 0.0  # keeps only the first token (the reference's forced first entry)
     state = torch.zeros(2, dtype=torch.int64, device=DEV)
     ld, td, kd, pd = logits.to(DEV), temps.to(DEV), ks.to(DEV), ps.to(DEV)
     keep = []
@@ -785,8 +786,9 @@ def test_sample_filtered_draws_stay_in_the_kept_set(vocab, levels):
             keep.append(None)
             continue
         # top_p + 1e-4: a draw may sit exactly on the boundary that float sums in another order decide
-        keep.append(kept_set(logits[r], t, int(ks[r]), min(1.0, float(ps[r]) + 1e-4)
-                             if float(ps[r]) < 1.0 else 1.0))
+        p_r = float(ps[r])
+        keep.append(kept_set(logits[r], t, int(ks[r]), p_r if p_r <= 0.0 else (min(1.0, p_r + 1e-4)
+                                                                                if p_r < 1.0 else 1.0)))
     for _ in range(8):
         tok = kernels.sample_filtered(ld, td, kd, pd, 99, state).cpu()
         for r in range(rows):
