@@ -4,17 +4,21 @@
 // mini_vllm/layers/attention.py:162-170): out[b, hq] = softmax_j(scale q[b,hq].K[b,j,hq/G])
 // V[b,j,hq/G] over j < L_b, key j at slot block_tables[b, j/BS]*BS + j%BS; L_b == 0 gives zeros.
 //
-// The CUDA-core kernel spends ~450 warp instructions per 8-token tile on unpacking bf16 pairs,
-// dot products, cross-lane reductions and the P.V update.  Here the two products run on tcgen05
-// with the G query heads of a KV head as the (padded) N dimension:
+// The CUDA-core kernel spends two FMAs per cache byte and query head plus the cross-lane score
+// reductions, so with four or more query heads per KV head it runs out of issue slots; here the
+// two products run on tcgen05 with the G query heads of a KV head as the (padded) N dimension:
 //     S^T [128 tokens x 16] = K_tile [128 x 128] . Q_h^T        (A = K tile, K-major)
 //     O^T [128 dims  x 16] += V_tile^T [128 x 128] . P^T          (A = V tile read MN-major)
 // both with M = 128, N = 16, K = 16 steps, fp32 in TMEM.  The K and V tiles arrive by TMA in the
 // same 128-byte-swizzled layout the prefill kernel uses; Q (G rows of the head, rest zero) comes
 // with each tile.  Softmax: thread = token = TMEM lane of S^T, the per-head max and sum across
 // the 128 tokens by warp shuffles and a 4-warp exchange in shared memory; P^T (bf16 hi + lo,
-// ~16 significant bits) goes to shared memory in the K-major layout of the B operand.  O is
-// rescaled lazily (the reference maximum moves only when a tile exceeds it by 2^8).
+// ~16 significant bits; for 2G <= 16 the two parts are rows [0, G) and [G, 2G) of one operand,
+// so one PV pass gives both) goes to shared memory in the K-major layout of the B operand.  O is
+// rescaled lazily (the reference maximum moves only when a tile exceeds it by 2^8).  V rows past
+// the context are zeroed before the PV product (P is 0 there; the cache may hold NaN bits).
+// FP8 caches: QK in kind::f8f6f4 on the staged e4m3 K bytes with Q as two exact e4m3 terms, and
+// converter warps 10-13 turning V into f16 (details with the constants below).
 //
 // Work: a unit is (sequence b, KV head h, 128-token tile t), 64 KiB of K+V.  The grid is one CTA
 // per SM; CTA c takes the contiguous unit range [c*upc, (c+1)*upc) of the (b, h, t)-ordered list
@@ -23,7 +27,7 @@
 // by the last of its CTAs to arrive (ticket), which merges the partial (m, l, O) of the others.
 // Warp 0 issues TMA, warp 1 owns TMEM and issues the MMAs, warps 2-5 run the softmax, warps 6-9
 // the per-(b, h) epilogues (normalise O and store, or publish a partial and merge), so a pair
-// boundary never stalls the softmax.
+// boundary never stalls the softmax; FP8 adds warps 10-13 (Q split, V conversion).
 // Every wait is bounded; no cluster launch, no multicast.
 #include "hl_common.cuh"
 
