@@ -378,7 +378,6 @@ def small_kernels(args, g):
     (BF16 and FP8, decode batch of 256 and a 16384-token prefill), the standalone BF16 store,
     the all-layer BF16->FP8 cache copy, the decode pack kernel on a full packet, add+RMSNorm,
     SiLU*mul and the greedy argmax.  A few GB on the device at most."""
-    import numpy as np
     import torch
 
     from hilda_vllm_b200 import kernels

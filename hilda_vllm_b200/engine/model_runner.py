@@ -31,7 +31,7 @@ from hilda_vllm_b200.layers import nvlink_allreduce
 from hilda_vllm_b200.layers.attention import Attention
 from hilda_vllm_b200.layers.nvlink_allreduce import NvlinkAllReduce
 from hilda_vllm_b200.models.qwen3 import Qwen3ForCausalLM
-from hilda_vllm_b200.utils.context import get_context, reset_context, set_context
+from hilda_vllm_b200.utils.context import reset_context, set_context
 from hilda_vllm_b200.utils.loader import has_checkpoint, load_model, random_init
 
 MODEL_REGISTRY = {"qwen3": Qwen3ForCausalLM}

@@ -8,7 +8,6 @@ tie with it within two bf16 ulps of the top logit (bf16 logits of a random-init 
 hold exact ties at the top, where any rounding difference upstream picks the other token);
 every accepted tie is printed."""
 import json
-import shutil
 from pathlib import Path
 
 import pytest

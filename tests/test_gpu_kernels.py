@@ -2,7 +2,6 @@
 golden fixtures).  Tolerances: integer / byte outputs bit-exact; BF16 attention within
 rtol 2e-2 / atol 2e-3 of the fp32 oracle, FP8-KV attention within atol 6e-2 (BASELINE
 north_star); elementwise layer kernels within 1 bf16 ulp of the reference modules."""
-import json
 
 import numpy as np
 import pytest
@@ -11,7 +10,6 @@ import torch
 from hilda_vllm_b200 import kernels
 from oracle import attention as oattn
 from oracle import kv_store
-from oracle.decode_pack import ReferenceDecodeBuffers
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -331,7 +329,6 @@ def test_prefill_simt_paged_with_prefix_chunks():
 def test_pack_kernel_replays_reference_trace(golden_dir, seq_block_size, name):
     from tests.test_trace_parity import _load, _replay
     from hilda_vllm_b200.engine.decode_packer import DecodePacker, packet_capacity_bytes
-    from hilda_vllm_b200.engine.sequence import SequenceStatus
 
     trace = _load(golden_dir, name)
     meta = trace["meta"]

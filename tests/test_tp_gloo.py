@@ -2,10 +2,8 @@
 weight loaders (the reference's TP layout, mini_vllm/layers/linear.py), the all-reduce after
 o_proj/down_proj, the vocabulary-sharded LM head gather (embed_head.py:56-66), the greedy
 (max, index) merge that replaces the logits gather, and the torchrun-mode control plane."""
-import os
 import socket
 
-import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp

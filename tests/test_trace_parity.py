@@ -7,7 +7,6 @@ through this package's host code and checks, bit for bit:
   - the decode graph buffers: DecodePacker packets applied with the oracle's restatement of
     the pack kernel == the reference prepare_decode buffers (and the oracle's restatement of
     prepare_decode == the recorded reference buffers, which pins that restatement)."""
-import itertools
 import json
 from types import SimpleNamespace
 
