@@ -24,6 +24,7 @@ import torch
 import torch.distributed as dist
 
 from hilda_vllm_b200 import kernels
+from hilda_vllm_b200.engine.control_plane import ShmChannel
 from hilda_vllm_b200.engine.decode_packer import DecodePacker, packet_capacity_bytes
 from hilda_vllm_b200.engine.scheduler import ScheduledSequence
 from hilda_vllm_b200.engine.sequence import Sequence
@@ -36,19 +37,6 @@ from hilda_vllm_b200.utils.loader import has_checkpoint, load_model, random_init
 
 MODEL_REGISTRY = {"qwen3": Qwen3ForCausalLM}
 MAX_GRAPH_BS = 512
-
-
-def rpc_send(group, method: str, *args) -> None:
-    """Rank 0 side of the torchrun-mode control plane: broadcast (method, args) to all ranks
-    over a gloo group (the spawn mode uses the reference's shared memory + events instead)."""
-    dist.broadcast_object_list([[method, *args]], src=0, group=group)
-
-
-def rpc_recv(group):
-    box = [None]
-    dist.broadcast_object_list(box, src=0, group=group)
-    method, *args = box[0]
-    return method, args
 
 
 def sampling_settings(seqs: list[Sequence]):
@@ -174,9 +162,11 @@ class ModelRunner:
             dist.init_process_group("nccl", f"tcp://127.0.0.1:{port}", world_size=self.world_size, rank=rank,
                                     device_id=torch.device("cuda", int(os.getenv("LOCAL_RANK", rank))))
         self.rpc_group = None
+        self.chan = None
         if self.world_size > 1 and self.external:
-            # Ranks launched by torchrun: the control plane is a gloo group (object broadcast
-            # from rank 0) instead of the shared-memory block + events of the spawn mode.
+            # Ranks launched by torchrun: the control plane is a shared-memory channel polled by
+            # the ranks (ShmChannel) instead of the spawn mode's block + inherited events; a gloo
+            # group carries its name once.
             self.rpc_group = dist.new_group(backend="gloo")
         local = int(os.getenv("LOCAL_RANK", rank))
         torch.cuda.set_device(local)
@@ -215,8 +205,17 @@ class ModelRunner:
                 dist.barrier()
                 self.shm = SharedMemory(name="hilda_b200")
                 self.loop()
-        elif self.world_size > 1 and rank > 0:
-            self.loop()
+        elif self.world_size > 1:
+            box = [None]
+            if rank == 0:
+                self.chan = ShmChannel.create(self.world_size)
+                box = [self.chan.name]
+            dist.broadcast_object_list(box, src=0, group=self.rpc_group)
+            if rank > 0:
+                self.chan = ShmChannel.attach(box[0], rank, self.world_size)
+            dist.barrier(group=self.rpc_group)
+            if rank > 0:
+                self.loop()
 
     # ------------------------------------------------------------------ TP control plane
     def exit(self):
@@ -225,6 +224,9 @@ class ModelRunner:
             dist.barrier()
             if self.rank == 0:
                 self.shm.unlink()
+        if self.chan is not None:
+            self.chan.close()  # rank 0 removes the segment; mapped views stay valid
+            self.chan = None
         self.graphs = {}
         self.graph_pool = None
         torch.cuda.synchronize()
@@ -246,7 +248,7 @@ class ModelRunner:
     def read_shm(self):
         assert self.world_size > 1 and self.rank > 0
         if self.external:
-            return rpc_recv(self.rpc_group)
+            return self.chan.recv()
         self.event.wait()
         n = int.from_bytes(self.shm.buf[0:4], "little")
         method, *args = pickle.loads(self.shm.buf[4:n + 4])
@@ -256,7 +258,7 @@ class ModelRunner:
     def write_shm(self, method, *args):
         assert self.world_size > 1 and self.rank == 0
         if self.external:
-            rpc_send(self.rpc_group, method, *args)
+            self.chan.send(method, *args)
             return
         data = pickle.dumps([method, *args])
         self.shm.buf[0:4] = len(data).to_bytes(4, "little")

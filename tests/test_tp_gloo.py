@@ -21,7 +21,8 @@ def _worker(rank, world, port, queue):
         torch.manual_seed(0)
         from transformers import Qwen3Config
 
-        from hilda_vllm_b200.engine.model_runner import merge_shard_argmax, rpc_recv, rpc_send
+        from hilda_vllm_b200.engine.control_plane import ShmChannel
+        from hilda_vllm_b200.engine.model_runner import merge_shard_argmax
         from hilda_vllm_b200.layers.embed_head import ParallelLMHead
         from hilda_vllm_b200.layers.linear import MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear
         from hilda_vllm_b200.utils.loader import random_weights
@@ -66,14 +67,24 @@ def _worker(rank, world, port, queue):
             dist.all_gather(all_val, val)
             dist.all_gather(all_idx, idx)
             merged = merge_shard_argmax(torch.stack(all_val), torch.stack(all_idx))
-        # control plane
+        # control plane (torchrun mode): the segment name crosses once over gloo, calls through it
         group = dist.new_group(backend="gloo")
+        box = [None]
         if rank == 0:
-            rpc_send(group, "run", [1, 2, 3], {"a": 1})
+            chan = ShmChannel.create(world, size=1 << 20)
+            box = [chan.name]
+        dist.broadcast_object_list(box, src=0, group=group)
+        if rank > 0:
+            chan = ShmChannel.attach(box[0], rank, world)
+        dist.barrier(group=group)
+        if rank == 0:
+            chan.send("run", [1, 2, 3], {"a": 1})
             msg = ("run", [[1, 2, 3], {"a": 1}])
         else:
-            method, args = rpc_recv(group)
+            method, args = chan.recv()
             msg = (method, args)
+        dist.barrier(group=group)
+        chan.close()
         queue.put((rank, z, m, full_logits, merged, msg))
         dist.destroy_process_group()
     except Exception as exc:  # pragma: no cover - surfaced by the parent
