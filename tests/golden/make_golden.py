@@ -348,9 +348,12 @@ def golden_sampler(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("HILDA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("HILDA_REFERENCE"),
+                    help="checkout of kirsten-1/hilda-vllm (or set HILDA_REFERENCE)")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference /path/to/hilda-vllm (or set HILDA_REFERENCE)")
     sys.path.insert(0, args.reference)
     only = set(filter(None, args.only.split(",")))
     if not only or "store" in only:
