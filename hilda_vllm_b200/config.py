@@ -40,7 +40,8 @@ class Config:
     kv_cache_scale: float = 1.0
     # "spawn": rank 0 starts ranks 1..tp-1 itself (the reference's way, shared-memory RPC);
     # "external": every rank is already running (torchrun) and calls LLM(...) itself; rank 0
-    # drives, the others serve the model-runner loop inside the constructor (gloo RPC).
+    # drives, the others serve the model-runner loop inside the constructor (calls through a
+    # polled shared-memory segment whose name crosses once over gloo).
     distributed_executor: str = "spawn"
     # Tensor parallelism: reduce decode-sized o_proj / down_proj outputs with the fused NVLink
     # all-reduce + add + RMSNorm kernel (False: NCCL all-reduce as the reference does).
