@@ -62,7 +62,7 @@ def parse():
     ap.add_argument("--kv", default="auto", choices=["auto", "fp8"], help="KV cache dtype for c5")
     ap.add_argument("--profile", default="",
                     choices=["", "decode-kernel", "decode-kernel-tc", "decode-steps", "prefill-kernel", "small-kernels",
-                             "allreduce", "gemm"],
+                             "allreduce"],
                     help="run a short profiling case instead of the benchmark: the CUDA profiler range "
                          "(cudaProfilerStart/Stop, for ncu --profile-from-start off) covers --steps "
                          "launches of the decode kernel alone (decode-kernel), of the prefill kernel "
@@ -552,56 +552,6 @@ def allreduce_profile(args):
     dist.destroy_process_group()
 
 
-def gemm_profile(args):
-    """The decode-step projections at config-2 shapes (M = 256 rows): the tcgen05 GEMM
-    (hl_gemm_bf16) against torch.matmul (cuBLAS).  Each variant runs over 28 distinct weight
-    copies per shape (as many as the model's layers, so weights come from HBM, not L2) captured
-    in one CUDA graph; replays timed with CUDA events."""
-    import torch
-
-    from hilda_vllm_b200 import kernels
-
-    dev = torch.device("cuda", 0)
-    shapes = {"qkv": (4096, 1024), "o_proj": (1024, 2048), "gate_up": (6144, 1024), "down": (1024, 3072),
-              "lm_head": (151936, 1024)}
-    m = NUM_SEQS
-    x = {k: torch.randn(m, kk, dtype=torch.bfloat16, device=dev) for k, (n, kk) in shapes.items()}
-    res = {"profile": "gemm", "m": m}
-    stream = torch.cuda.current_stream()
-    for name, (n, k) in shapes.items():
-        copies = 28 if name != "lm_head" else 1
-        ws = [torch.randn(n, k, dtype=torch.bfloat16, device=dev) * 0.02 for _ in range(copies)]
-        out = torch.empty(m, n if name != "gate_up" else n, dtype=torch.bfloat16, device=dev)
-        variants = {"cublas": lambda w: torch.matmul(x[name], w.t(), out=out),
-                    "tcgen05": lambda w: kernels.linear(x[name], w, out=out)}
-        if name == "gate_up":
-            out_h = torch.empty(m, n // 2, dtype=torch.bfloat16, device=dev)
-            variants["tcgen05_silu"] = lambda w: kernels.linear(x[name], w, out=out_h, epilogue=kernels.GEMM_SILU_MUL)
-        for vname, fn in variants.items():
-            for w in ws[:3]:
-                fn(w)
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()  # replayed, so the numbers are GPU time, not launch time
-            with torch.cuda.graph(graph):
-                for w in ws:
-                    fn(w)
-            graph.replay()
-            torch.cuda.synchronize()
-            reps = 5
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(reps):
-                graph.replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            del graph
-            us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
-            res[f"{name}_{vname}_us"] = round(us, 2)
-            res[f"{name}_{vname}_weight_tbps"] = round(n * k * 2 / us / 1e6, 2)
-        del ws
-    print(json.dumps(res))
-
-
 def run_profile(args):
     """Short, self-contained cases for ncu (one GPU)."""
     import torch
@@ -610,9 +560,6 @@ def run_profile(args):
 
     if args.profile == "allreduce":
         allreduce_profile(args)
-        return
-    if args.profile == "gemm":
-        gemm_profile(args)
         return
     torch.cuda.set_device(0)
     g = torch.Generator().manual_seed(args.seed)
@@ -694,14 +641,12 @@ def run_profile(args):
                                                                block_table=bt, precise_p=False),
                     "tc_one_head_precise": lambda: kernels.varlen_prefill(q, kc, vc, cuq, cuk, max(chunks), max(kl),
                                                                           d ** -0.5, block_table=bt,
-                                                                          one_head_per_cta=True),
-                    "simt": lambda: kernels.varlen_prefill_simt(q, kc, vc, cuq, cuk, max(chunks), max(kl), d ** -0.5,
-                                                                block_table=bt)}
+                                                                          one_head_per_cta=True)}
         stream = torch.cuda.current_stream()
         for name, fn in variants.items():
             fn()
             torch.cuda.synchronize()
-            reps = args.steps if name != "simt" else 1
+            reps = args.steps
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             if name == "tc_precise":
                 torch.cuda.profiler.start()

@@ -95,13 +95,6 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ],
     ),
     "hl_varlen_prefill_read_errors": (c_int, [c_vp]),
-    "hl_varlen_prefill_simt": (
-        c_int,
-        [
-            c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_int,
-            c_int, c_int, c_int, c_int, c_i64, c_f32, c_vp, c_i64, c_vp,
-        ],
-    ),
     "hl_pack_decode_batch": (
         c_int,
         [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_vp],
@@ -118,8 +111,6 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hl_allreduce_signal_bytes": (c_i64, []),
     "hl_allreduce_add_rmsnorm": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_i64, c_f32,
                                          c_vp, c_vp, c_i64, c_vp]),
-    "hl_gemm_workspace_size": (c_i64, [c_int, c_int, c_int, c_int]),
-    "hl_gemm_bf16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_i64, c_vp]),
     "hl_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_vp]),
     "hl_sample": (c_int, [c_vp, c_i64, c_int, c_int, c_i64, c_vp, ctypes.c_uint64, c_vp, c_vp, c_vp, c_vp]),
     "hl_sample_filtered": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_vp, ctypes.c_uint64, c_vp, c_vp,

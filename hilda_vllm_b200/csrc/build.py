@@ -26,12 +26,10 @@ SOURCES = [
     "store_kv.cu",
     "paged_decode.cu",
     "paged_decode_tc.cu",
-    "varlen_prefill.cu",
     "prefill_tc.cu",
     "pack_decode.cu",
     "layer_ops.cu",
     "allreduce.cu",
-    "gemm_tc.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -8,8 +8,10 @@ Mirrors mini_vllm/engine/model_runner.py (ModelRunner) for the non-speculative p
     the host sends one small packet per step instead of rewriting every slot;
   - capture_cudagraph / run_model (:735-832): one graph per batch bucket [1,2,4,8,16,...,512];
     each graph holds the pack kernel, the whole model, the LM head and the device sampler
-    (greedy argmax or Gumbel-max temperature sampling; top-k / top-p rows use the host
-    sampler), so a decode step is: one packet copy, one graph replay, one token copy back;
+    (greedy argmax, Gumbel-max temperature sampling, and on one GPU the top-k / top-p filters
+    of hl_sample_filtered; under tensor parallelism top-k / top-p rows gather their logits to
+    rank 0, which samples them with the same kernel), so a decode step is: one packet copy,
+    one graph replay, one token copy back;
   - convert_prefill_to_decode_cache (:483-502): one launch for all layers;
   - the tensor-parallel RPC through shared memory (:82-130) with rank 0 driving.
 """

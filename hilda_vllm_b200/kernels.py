@@ -197,44 +197,6 @@ def decode_errors(workspace: torch.Tensor) -> int:
 
 
 # ------------------------------------------------------------------------ prefill attention
-def varlen_prefill_simt(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
-                        cu_seqlens_k: torch.Tensor, max_seqlen_q: int, max_seqlen_k: int, softmax_scale: float,
-                        block_table: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Causal varlen attention with a bottom-right-aligned mask, on the CUDA-core kernel
-    (hl_varlen_prefill_simt; kept for comparison — the engine uses varlen_prefill).
-
-    Same arguments as the reference's flash_attn_varlen_func call
-    (mini_vllm/layers/attention.py:149-160): q [Tq, Hq, D]; with block_table, k/v are the paged
-    caches [NB, BS, Hk, D]; without, k/v are [Tk, Hk, D].  Returns [Tq, Hq, D] bf16."""
-    _cuda(q, k, v, cu_seqlens_q, cu_seqlens_k, block_table, out)
-    tq, hq, hd = q.shape
-    assert q.stride(2) == 1 and q.stride(1) == hd
-    assert cu_seqlens_q.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32
-    assert cu_seqlens_q.is_contiguous() and cu_seqlens_k.is_contiguous()
-    num_seqs = cu_seqlens_q.numel() - 1
-    if block_table is not None:
-        nb, bsz, hk, hd2 = k.shape
-        assert k.is_contiguous() and v.is_contiguous()
-        assert block_table.dtype == torch.int32 and block_table.stride(1) == 1
-        bt_ptr, bt_stride, k_rs, v_rs = block_table.data_ptr(), block_table.stride(0), 0, 0
-    else:
-        _, hk, hd2 = k.shape
-        assert k.stride(2) == 1 and k.stride(1) == hd2 and v.stride(2) == 1 and v.stride(1) == hd2
-        nb, bsz = 0, 0
-        bt_ptr, bt_stride, k_rs, v_rs = None, 0, k.stride(0), v.stride(0)
-    assert hd == hd2
-    if out is None:
-        out = torch.empty(tq, hq, hd, dtype=torch.bfloat16, device=q.device)
-    if num_seqs <= 0 or tq == 0:
-        return out
-    lib = _lib.load()
-    check(lib.hl_varlen_prefill_simt(q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k_rs, v_rs,
-                                cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), bt_ptr, bt_stride, num_seqs,
-                                int(max_seqlen_q), int(max_seqlen_k), hq, hk, hd, bsz, nb, float(softmax_scale),
-                                out.data_ptr(), out.stride(0), _stream(q)), "hl_varlen_prefill_simt")
-    return out
-
-
 def varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
                    cu_seqlens_k: torch.Tensor, max_seqlen_q: int, max_seqlen_k: int, softmax_scale: float,
                    block_table: torch.Tensor | None = None, out: torch.Tensor | None = None,
@@ -366,11 +328,6 @@ def qk_norm_rope_store(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, h
           "hl_qk_norm_rope_store")
 
 
-GEMM_PLAIN = 0
-GEMM_SILU_MUL = 1
-_gemm_ws: dict = {}
-
-
 def sample(logits: torch.Tensor, temperatures: torch.Tensor | None, seed: int, step_state: torch.Tensor | None,
            out: torch.Tensor | None = None, index_offset: int = 0,
            out_values: torch.Tensor | None = None) -> torch.Tensor:
@@ -413,41 +370,6 @@ def sample_filtered(logits: torch.Tensor, temperatures: torch.Tensor | None, top
     check(lib.hl_sample_filtered(logits.data_ptr(), logits.stride(0), rows, vocab, _p(temperatures), _p(top_ks),
                                  _p(top_ps), int(seed) & 0xFFFFFFFFFFFFFFFF, _p(step_state), out.data_ptr(),
                                  _stream(logits)), "hl_sample_filtered")
-    return out
-
-
-def gemm_workspace(m: int, n: int, k: int, epilogue: int, device) -> torch.Tensor:
-    """A zeroed workspace for hl_gemm_bf16 of this shape, cached per (shape, device) so the
-    addresses stay fixed for CUDA-graph capture."""
-    key = (m, n, k, epilogue, str(device))
-    ws = _gemm_ws.get(key)
-    if ws is None:
-        nbytes = int(_lib.load().hl_gemm_workspace_size(m, n, k, epilogue))
-        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
-        _gemm_ws[key] = ws
-    return ws
-
-
-def linear(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
-           epilogue: int = GEMM_PLAIN) -> torch.Tensor:
-    """out = x @ weight.T on the tcgen05 GEMM (x [M, K], weight [N, K], bf16).  With
-    GEMM_SILU_MUL, weight is [2I, K] (gate rows, then up rows) and out = silu(x@gate.T) * (x@up.T)
-    [M, I]."""
-    _cuda(x, weight, out)
-    assert x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and x.dim() == 2
-    assert x.stride(1) == 1 and weight.stride(1) == 1
-    m, k = x.shape
-    n = weight.shape[0] if epilogue == GEMM_PLAIN else weight.shape[0] // 2
-    assert weight.shape[1] == k
-    if out is None:
-        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
-    assert out.shape == (m, n) and out.stride(1) == 1
-    if m == 0:
-        return out
-    ws = gemm_workspace(m, n, k, epilogue, x.device)
-    check(_lib.load().hl_gemm_bf16(x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(),
-                                   out.stride(0), m, n, k, epilogue, ws.data_ptr(), ws.numel(), _stream(x)),
-          "hl_gemm_bf16")
     return out
 
 

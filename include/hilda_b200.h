@@ -197,18 +197,6 @@ int hl_varlen_prefill(const void* q, int64_t q_row_stride, int64_t total_q,
 /* Error bits of the tensor-core prefill kernel (bit 0: an mbarrier wait timed out).  Synchronous. */
 int hl_varlen_prefill_read_errors(int32_t* errors_out);
 
-/* The same prefill on CUDA cores (fp32 FMA, one CTA per 64 query rows x head x sequence):
- * the small reference implementation kept for comparison; same semantics and arguments as
- * hl_varlen_prefill minus total_q / total_k / precise_p. */
-int hl_varlen_prefill_simt(const void* q, int64_t q_row_stride,
-                           const void* k, const void* v, int64_t k_row_stride, int64_t v_row_stride,
-                           const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
-                           const int32_t* block_tables, int64_t bt_stride,
-                           int num_seqs, int max_seqlen_q, int max_seqlen_k,
-                           int num_q_heads, int num_kv_heads, int head_dim,
-                           int block_size, int64_t num_blocks, float softmax_scale,
-                           void* out, int64_t out_row_stride, void* stream);
-
 /* ------------------------------------------------------------------------------------
  * Decode-batch packing on the GPU.
  * Replaces the host loop of ModelRunner.prepare_decode and its block-table row sync,
@@ -313,23 +301,6 @@ int hl_argmax(const void* logits, int64_t row_stride, int rows, int vocab, int64
  * (mini_vllm/layers/embed_head.py:56-66). */
 int hl_argmax_shard(const void* logits, int64_t row_stride, int rows, int vocab, int64_t index_offset,
                     int64_t* out_tokens, float* out_values, void* stream);
-
-/* ------------------------------------------------------------------------------------
- * Projection GEMM on tcgen05: D[M, N] = A[M, K] . B[N, K]^T, bf16 in / fp32 accumulate / bf16
- * out, every matrix row-major with the given row strides (elements).  Replaces the nn.Linear
- * products of the decode step (F.linear in mini_vllm/layers/linear.py and the LM head,
- * embed_head.py:56-66): A = activations, B = the weight [out_features, in_features].
- * HL_GEMM_SILU_MUL: B has 2N rows (gate rows [0, N), up rows [N, 2N) as in
- * MergedColumnParallelLinear) and D = SiLU(A.gate^T) * (A.up^T) with the reference's
- * SiluAndMul rounding (activation.py:12-16).  K % 64 == 0; 16-byte aligned operands and strides.
- * The launch uses programmatic dependent launch: weight tiles are fetched before waiting for the
- * previous kernel on the stream.  workspace: hl_gemm_workspace_size bytes, zeroed once (split-K
- * tickets return to zero). */
-#define HL_GEMM_PLAIN 0
-#define HL_GEMM_SILU_MUL 1
-int64_t hl_gemm_workspace_size(int M, int N, int K, int epilogue);
-int hl_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int M, int N,
-                 int K, int epilogue, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------
  * Tensor-parallel all-reduce over NVLink peer memory fused with add + RMSNorm.

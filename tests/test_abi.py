@@ -64,9 +64,6 @@ def test_invalid_arguments_are_rejected_without_gpu():
     rc = lib.hl_varlen_prefill(p, 2048, 100, p, p, 0, 0, 100, p, p, None, 0, 2, 8, 16, 8, 64, 256, 0, 0.1, p, 2048, 1,
                                None)
     assert rc == 1 and b"head_dim" in lib.hl_last_error_string()
-    rc = lib.hl_varlen_prefill_simt(p, 2048, p, p, 0, 0, p, p, None, 0, 2, 8, 8, 16, 8, 64, 256, 0, 0.1, p, 2048,
-                                    None)
-    assert rc == 1
     assert lib.hl_pack_decode_batch(p, 8, 16, 256, p, p, p, p, p, p, p, p, 4, 4, None) == 1  # packet too small
     assert lib.hl_pack_decode_batch(p, 64, 2000, 256, p, p, p, p, p, p, p, p, 4, 4, None) == 1  # graph batch too big
     assert lib.hl_rmsnorm(p, 1000, None, p, p, 1000, 4, 1000, 1e-6, None) == 1  # hidden not multiple of 256

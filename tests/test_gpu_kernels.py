@@ -231,7 +231,7 @@ def test_decode_cuda_core_kernel_at_high_gqa_ratio(hq, hk):
 
 
 @pytest.mark.parametrize("case", ["one_long", "mixed_long", "many_short", "g16"])
-def test_decode_tensor_core_against_oracle_and_simt(case):
+def test_decode_tensor_core_against_oracle_and_cuda_core(case):
     """The tcgen05 decode kernel (hl_paged_decode_tc) against the fp32 oracle and the
     CUDA-core kernel: one 20k-token sequence (each KV head's tiles spread over ~18 CTAs, merged
     by the last one), long and short sequences mixed, many short ones, and G = 16."""
@@ -259,8 +259,8 @@ def test_decode_tensor_core_against_oracle_and_simt(case):
         want = oattn.paged_decode(q[idx], k, v, bt[idx], ln[idx], 128 ** -0.5)
         assert_close(out[idx], want, **BF16_TOL, what=f"tensor-core decode {case} trial {trial}")
     if hq // hk <= 8:  # the CUDA-core kernel covers GQA ratios 1, 2, 4, 8
-        simt = kernels.paged_decode(qd, kd, vd, btd, lnd, 128 ** -0.5, workspace=ws)
-        assert_close(out.float().cpu(), simt.float().cpu(), rtol=2e-2, atol=2e-3, what="tensor-core vs CUDA-core")
+        cc = kernels.paged_decode(qd, kd, vd, btd, lnd, 128 ** -0.5, workspace=ws)
+        assert_close(out.float().cpu(), cc.float().cpu(), rtol=2e-2, atol=2e-3, what="tensor-core vs CUDA-core")
     for i, n in enumerate(lens):
         if n == 0:
             assert torch.all(out[i] == 0)
@@ -284,44 +284,6 @@ def test_decode_fp8(hq, hk, scaled, tc):
     want = oattn.paged_decode(q, kq, vq, bt, ln, 128 ** -0.5, ks, vs, fp8=True)
     assert_close(out, want, rtol=2e-2, atol=6e-2, what="fp8")
     assert_close(out, want, **BF16_TOL, what="fp8 (tight)")
-
-
-# ----------------------------------------------------------------------------- prefill
-@pytest.mark.parametrize("hq,hk", [(16, 8), (32, 8), (8, 1)])
-def test_prefill_simt_contiguous(hq, hk):
-    g = torch.Generator().manual_seed(11 + hq)
-    lens = [1, 5, 64, 64, 130, 257, 31]
-    cu = torch.tensor([0] + np.cumsum(lens).tolist(), dtype=torch.int32)
-    t = int(cu[-1])
-    qkv = torch.randn(t, (hq + 2 * hk) * 128, generator=g).bfloat16()
-    q = qkv[:, :hq * 128].view(t, hq, 128)
-    k = qkv[:, hq * 128:(hq + hk) * 128].view(t, hk, 128)
-    v = qkv[:, (hq + hk) * 128:].view(t, hk, 128)
-    qd = qkv.to(DEV)
-    out = kernels.varlen_prefill_simt(qd[:, :hq * 128].view(t, hq, 128),
-                                      qd[:, hq * 128:(hq + hk) * 128].view(t, hk, 128),
-                                      qd[:, (hq + hk) * 128:].view(t, hk, 128), cu.to(DEV), cu.to(DEV), max(lens),
-                                      max(lens), 128 ** -0.5)
-    want = oattn.varlen_prefill(q, k, v, cu, cu, 128 ** -0.5)
-    assert_close(out, want, **BF16_TOL, what="prefill contiguous (CUDA cores)")
-
-
-def test_prefill_simt_paged_with_prefix_chunks():
-    """Chunked prefill over cached prefixes: queries are the chunk, keys = prefix + chunk
-    from the paged cache (block_table set), bottom-right causal mask."""
-    g = torch.Generator().manual_seed(12)
-    hq, hk, bs, nb = 16, 8, 256, 40
-    starts = [0, 256, 100, 512, 2048, 3]
-    chunks = [64, 128, 1, 300, 512, 700]
-    kl = [s + c for s, c in zip(starts, chunks)]
-    k, v, bt, _ = make_paged(g, len(kl), hk, 128, nb, bs, kl)
-    cuq = torch.tensor([0] + np.cumsum(chunks).tolist(), dtype=torch.int32)
-    cuk = torch.tensor([0] + np.cumsum(kl).tolist(), dtype=torch.int32)
-    q = torch.randn(int(cuq[-1]), hq, 128, generator=g).bfloat16()
-    out = kernels.varlen_prefill_simt(q.to(DEV), k.to(DEV), v.to(DEV), cuq.to(DEV), cuk.to(DEV), max(chunks),
-                                      max(kl), 128 ** -0.5, block_table=bt.to(DEV))
-    want = oattn.varlen_prefill(q, k, v, cuq, cuk, 128 ** -0.5, block_table=bt)
-    assert_close(out, want, **BF16_TOL, what="prefill paged (CUDA cores)")
 
 
 # ----------------------------------------------------------------------------- packing
@@ -511,38 +473,6 @@ def test_sample_matches_softmax_distribution():
     want = torch.softmax(base.bfloat16().float() / T, -1).double()
     n = rows * launches
     assert float((freq - want).abs().max()) < 5 * float((want * (1 - want) / n).sqrt().max()) + 1e-4
-
-
-# ----------------------------------------------------------------------------- tcgen05 GEMM
-@pytest.mark.parametrize("m,n,k", [(256, 4096, 1024), (256, 1024, 2048), (256, 1024, 3072), (1, 1024, 1024),
-                                   (300, 1000, 128), (256, 151936, 1024), (512, 6144, 1024)])
-def test_gemm_matches_fp32_reference(m, n, k):
-    """hl_gemm_bf16 against an fp32 matmul of the same bf16 operands (split-K shapes, ragged M/N,
-    the LM head, a 512-row batch)."""
-    g = torch.Generator().manual_seed(m + n + k)
-    x = (torch.randn(m, k, generator=g) * 0.5).bfloat16()
-    w = (torch.randn(n, k, generator=g) * 0.05).bfloat16()
-    got = kernels.linear(x.to(DEV), w.to(DEV))
-    torch.cuda.synchronize()
-    want = (x.float().to(DEV) @ w.float().to(DEV).T).cpu()
-    assert_close(got, want, rtol=1e-2, atol=1e-2, what=f"gemm {m}x{n}x{k}")
-    again = kernels.linear(x.to(DEV), w.to(DEV))  # split-K tickets reset
-    assert torch.equal(again.cpu(), got.cpu())
-
-
-@pytest.mark.parametrize("m", [256, 64])
-def test_gemm_silu_mul_epilogue(m):
-    """GEMM with the SiLU*mul epilogue == gate_up GEMM followed by the SiluAndMul kernel (up to
-    the accumulation order of the GEMM)."""
-    g = torch.Generator().manual_seed(m)
-    inter, k = 3072, 1024
-    x = (torch.randn(m, k, generator=g) * 0.5).bfloat16().to(DEV)
-    w = (torch.randn(2 * inter, k, generator=g) * 0.05).bfloat16().to(DEV)
-    got = kernels.linear(x, w, epilogue=kernels.GEMM_SILU_MUL)
-    want = kernels.silu_mul(kernels.linear(x, w))
-    torch.cuda.synchronize()
-    assert got.shape == (m, inter)
-    assert_close(got, want, rtol=2e-2, atol=2e-3, what="gemm + silu_mul")
 
 
 # ----------------------------------------------------------------------------- flash-attn pin

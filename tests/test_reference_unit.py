@@ -11,8 +11,8 @@ import torch
 from hilda_vllm_b200.engine.block_manager import BlockManager
 from hilda_vllm_b200.engine.scheduler import Scheduler
 from hilda_vllm_b200.engine.sequence import Sequence, SequenceStatus
-from hilda_vllm_b200.layers.sampler import Sampler
 from hilda_vllm_b200.sampling_params import SamplingParams
+from oracle.sampler import kept_set
 
 
 @pytest.fixture(autouse=True)
@@ -207,22 +207,18 @@ def test_prefill_respects_running_sequences_when_counting_max_num_seqs():
     assert npre is True and [x.seq for x in nxt] == [w1]
 
 
-# ---- test_sampler.py
+# ---- test_sampler.py (the reference's filter semantics, through the oracle restatement that
+# checks hl_sample_filtered on the GPU)
 def test_top_k_masks_out_lower_ranked_logits():
-    logits = torch.tensor([[5.0, 4.0, 3.0, 2.0]])
-    m = Sampler._apply_top_k(logits.clone(), torch.tensor([2], dtype=torch.int32))
-    assert torch.isneginf(m[0, 2]) and torch.isneginf(m[0, 3]) and m[0, 0] == 5.0 and m[0, 1] == 4.0
+    logits = torch.tensor([5.0, 4.0, 3.0, 2.0])
+    assert kept_set(logits, 1.0, 2, 1.0).tolist() == [True, True, False, False]
 
 
 def test_top_p_masks_tail_outside_probability_mass():
-    logits = torch.log(torch.tensor([[0.5, 0.3, 0.15, 0.05]]))
-    m = Sampler._apply_top_p(logits.clone(), torch.tensor([0.81]))
-    assert not torch.isneginf(m[0, 0]) and not torch.isneginf(m[0, 1])
-    assert torch.isneginf(m[0, 2]) and torch.isneginf(m[0, 3])
+    logits = torch.log(torch.tensor([0.5, 0.3, 0.15, 0.05]))
+    assert kept_set(logits, 1.0, -1, 0.81).tolist() == [True, True, False, False]
 
 
 def test_top_p_uses_strict_boundary():
-    logits = torch.log(torch.tensor([[0.5, 0.3, 0.15, 0.05]]))
-    m = Sampler._apply_top_p(logits.clone(), torch.tensor([0.8]))
-    assert not torch.isneginf(m[0, 0])
-    assert torch.isneginf(m[0, 1]) and torch.isneginf(m[0, 2]) and torch.isneginf(m[0, 3])
+    logits = torch.log(torch.tensor([0.5, 0.3, 0.15, 0.05]))
+    assert kept_set(logits, 1.0, -1, 0.8).tolist() == [True, False, False, False]
