@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ],
     ),
     "hl_paged_decode_noalloc_capacity": (c_i64, []),
+    "hl_paged_decode_noalloc_read_errors": (c_int, [c_vp, c_vp]),
     "hl_paged_decode_read_errors": (c_int, [c_vp, c_vp, c_vp]),
     "hl_varlen_prefill": (
         c_int,
@@ -95,6 +96,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ],
     ),
     "hl_varlen_prefill_read_errors": (c_int, [c_vp]),
+    "hl_varlen_prefill_copy_errors_async": (c_int, [c_vp, c_vp]),
     "hl_pack_decode_batch": (
         c_int,
         [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_vp],
@@ -103,6 +105,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hl_qk_norm_rope": (c_int, [c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_f32, c_vp]),
     "hl_qk_norm_rope_store": (c_int, [c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_f32, c_vp,
                                       c_vp, c_int, c_vp, c_i64, c_vp, c_vp, c_vp]),
+    "hl_qk_norm_rope_store_mirrored": (c_int, [c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp,
+                                               c_f32, c_vp, c_vp, c_int, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "hl_device_alloc": (c_int, [c_i64, c_vp]),
     "hl_device_free": (c_int, [c_vp]),
     "hl_ipc_get_handle": (c_int, [c_vp, c_vp]),

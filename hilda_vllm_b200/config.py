@@ -53,6 +53,10 @@ class Config:
     # was put in the same decode batch (scheduler.py:326-340); True drops that token instead
     # (correct outputs; block decisions then differ from the reference in that case).
     drop_preempted_decode_token: bool = False
+    # When nothing can run because the head of the waiting queue cannot get its blocks, let
+    # chunked prefills further back that already hold blocks proceed (the reference raises
+    # "no runnable prefill or decode work" there); False reproduces the reference.
+    unblock_prefill_head: bool = True
 
     def __post_init__(self):
         assert os.path.isdir(self.model)

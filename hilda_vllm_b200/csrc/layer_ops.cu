@@ -93,9 +93,12 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat
 // token whose slot is in range the post-RoPE k head and the v head are written to row `slot`
 // of the paged cache, as bf16 bytes (kStoreBf16) or as e4m3 of x / scale[h] (kStoreFp8) —
 // the same bytes the separate store kernels write from the rotated qkv rows.
+// kStoreFp8Mirror writes the e4m3 rows and, in the same pass, the bf16 rows into a second pair
+// of caches (the FP8 mode's BF16 prefill cache), so that cache holds every token's K/V too.
 constexpr int kNoStore = 0;
 constexpr int kStoreBf16 = 1;
 constexpr int kStoreFp8 = 2;
+constexpr int kStoreFp8Mirror = 3;
 
 template <int KV>
 __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row_stride, int num_tokens,
@@ -104,7 +107,8 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row
                                     const int64_t* __restrict__ positions, float eps, void* __restrict__ k_cache,
                                     void* __restrict__ v_cache, const int32_t* __restrict__ slot_mapping,
                                     int64_t num_slots, const float* __restrict__ k_scale,
-                                    const float* __restrict__ v_scale) {
+                                    const float* __restrict__ v_scale, __nv_bfloat16* __restrict__ k_mirror,
+                                    __nv_bfloat16* __restrict__ v_mirror) {
   // Let the next kernel (the decode attention, launched as a programmatic dependent) start its
   // prologue now; it waits for this grid's writes before it reads q or the newest K/V slot.
   asm volatile("griddepcontrol.launch_dependents;");
@@ -130,6 +134,7 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row
         *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(v_cache) + off) = a;
       } else {
         *reinterpret_cast<uint2*>(static_cast<uint8_t*>(v_cache) + off) = quant8_e4m3(a, v_scale ? v_scale[hv] : 1.f);
+        if constexpr (KV == kStoreFp8Mirror) *reinterpret_cast<uint4*>(v_mirror + off) = a;
       }
       return;
     }
@@ -197,6 +202,7 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row
           *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(k_cache) + off) = rot;
         } else {
           *reinterpret_cast<uint2*>(static_cast<uint8_t*>(k_cache) + off) = quant8_e4m3(rot, k_scale ? k_scale[hk] : 1.f);
+          if constexpr (KV == kStoreFp8Mirror) *reinterpret_cast<uint4*>(k_mirror + off) = rot;
         }
       }
     }
@@ -884,18 +890,35 @@ extern "C" int hl_qk_norm_rope_store(void* qkv, int64_t row_stride, int num_toke
                                      const float* cos_sin, const int64_t* positions, float eps, void* k_cache,
                                      void* v_cache, int kv_dtype, const int32_t* slot_mapping, int64_t num_slots,
                                      const float* k_scale, const float* v_scale, void* stream) {
+  return hl_qk_norm_rope_store_mirrored(qkv, row_stride, num_tokens, num_q_heads, num_kv_heads, head_dim, q_weight,
+                                        k_weight, cos_sin, positions, eps, k_cache, v_cache, kv_dtype, slot_mapping,
+                                        num_slots, k_scale, v_scale, nullptr, nullptr, stream);
+}
+
+extern "C" int hl_qk_norm_rope_store_mirrored(void* qkv, int64_t row_stride, int num_tokens, int num_q_heads,
+                                              int num_kv_heads, int head_dim, const void* q_weight,
+                                              const void* k_weight, const float* cos_sin, const int64_t* positions,
+                                              float eps, void* k_cache, void* v_cache, int kv_dtype,
+                                              const int32_t* slot_mapping, int64_t num_slots, const float* k_scale,
+                                              const float* v_scale, void* k_mirror, void* v_mirror, void* stream) {
   clear_error();
   if (num_tokens == 0) return HL_OK;
   HL_CHECK_ARG(qkv && q_weight && k_weight && cos_sin && positions && num_tokens > 0, "hl_qk_norm_rope: bad args");
   HL_CHECK_ARG(head_dim == 128, "hl_qk_norm_rope: head_dim must be 128");
   HL_CHECK_ARG(aligned16(qkv) && row_stride % 8 == 0, "hl_qk_norm_rope: 16-byte alignment required");
   const bool store = k_cache != nullptr;
+  const bool mirror = k_mirror != nullptr || v_mirror != nullptr;
   if (store) {
     HL_CHECK_ARG(v_cache && slot_mapping && num_slots > 0, "hl_qk_norm_rope_store: cache arguments missing");
     HL_CHECK_ARG(kv_dtype == HL_KV_BF16 || kv_dtype == HL_KV_FP8_E4M3, "hl_qk_norm_rope_store: bad kv_dtype");
     HL_CHECK_ARG(aligned16(k_cache) && aligned16(v_cache), "hl_qk_norm_rope_store: 16-byte aligned caches required");
   } else {
     HL_CHECK_ARG(!v_cache, "hl_qk_norm_rope_store: v_cache without k_cache");
+  }
+  if (mirror) {
+    HL_CHECK_ARG(store && kv_dtype == HL_KV_FP8_E4M3 && k_mirror && v_mirror,
+                 "hl_qk_norm_rope_store_mirrored: bf16 mirror caches go with an FP8 store (both k and v)");
+    HL_CHECK_ARG(aligned16(k_mirror) && aligned16(v_mirror), "hl_qk_norm_rope_store_mirrored: 16-byte alignment");
   }
   const int heads = num_q_heads + (store ? 2 : 1) * num_kv_heads;
   const int64_t groups = int64_t(num_tokens) * heads;
@@ -909,15 +932,20 @@ extern "C" int hl_qk_norm_rope_store(void* qkv, int64_t row_stride, int num_toke
   if (!store) {
     qk_norm_rope_kernel<kNoStore><<<(unsigned)blocks, threads, 0, s>>>(
         q, row_stride, num_tokens, num_q_heads, num_kv_heads, qwt, kwt, cos_sin, positions, eps, nullptr, nullptr,
-        nullptr, 0, nullptr, nullptr);
+        nullptr, 0, nullptr, nullptr, nullptr, nullptr);
   } else if (kv_dtype == HL_KV_BF16) {
     qk_norm_rope_kernel<kStoreBf16><<<(unsigned)blocks, threads, 0, s>>>(
         q, row_stride, num_tokens, num_q_heads, num_kv_heads, qwt, kwt, cos_sin, positions, eps, k_cache, v_cache,
-        slot_mapping, num_slots, nullptr, nullptr);
-  } else {
+        slot_mapping, num_slots, nullptr, nullptr, nullptr, nullptr);
+  } else if (!mirror) {
     qk_norm_rope_kernel<kStoreFp8><<<(unsigned)blocks, threads, 0, s>>>(
         q, row_stride, num_tokens, num_q_heads, num_kv_heads, qwt, kwt, cos_sin, positions, eps, k_cache, v_cache,
-        slot_mapping, num_slots, k_scale, v_scale);
+        slot_mapping, num_slots, k_scale, v_scale, nullptr, nullptr);
+  } else {
+    qk_norm_rope_kernel<kStoreFp8Mirror><<<(unsigned)blocks, threads, 0, s>>>(
+        q, row_stride, num_tokens, num_q_heads, num_kv_heads, qwt, kwt, cos_sin, positions, eps, k_cache, v_cache,
+        slot_mapping, num_slots, k_scale, v_scale, static_cast<__nv_bfloat16*>(k_mirror),
+        static_cast<__nv_bfloat16*>(v_mirror));
   }
   HL_CHECK_LAUNCH("hl_qk_norm_rope");
   return HL_OK;

@@ -835,3 +835,14 @@ extern "C" int hl_paged_decode_noalloc(const void* q, int64_t q_row_stride, cons
                          max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, head_dim, block_size,
                          num_blocks, softmax_scale, out, out_row_stride, scratch, kNoAllocScratchBytes, stream);
 }
+
+// Error bits the most recent hl_paged_decode_noalloc call on the current device left in the
+// scratch array's error word (each call starts it from zero).  Synchronises `stream`.
+extern "C" int hl_paged_decode_noalloc_read_errors(int32_t* errors_out, void* stream) {
+  clear_error();
+  HL_CHECK_ARG(errors_out, "hl_paged_decode_noalloc_read_errors: null pointer");
+  uint8_t* scratch = nullptr;
+  int rc = hl::scratch_for_current_device(&scratch);
+  if (rc != HL_OK) return rc;
+  return hl_paged_decode_read_errors(scratch, errors_out, stream);
+}

@@ -66,6 +66,7 @@ struct TcParams {
   const int32_t* cu_k;
   const int32_t* block_tables;
   int64_t bt_stride;
+  int64_t num_blocks;
   int paged;
   int block_size;
   int num_q_heads;
@@ -75,7 +76,7 @@ struct TcParams {
   int64_t out_row_stride;
 };
 
-__device__ int g_prefill_errors;  // bit 0: an mbarrier wait timed out
+__device__ int g_prefill_errors;  // bit 0: an mbarrier wait timed out; bit 1: a block id out of range
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100 version bits.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
@@ -229,7 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1) varlen_prefill_tc_kernel(const __
         int row;
         if (p.paged) {
           const int blk = p.block_tables[int64_t(s) * p.bt_stride + kj / p.block_size];
-          row = blk * p.block_size + (kj % p.block_size);  // a bad (-1) block reads zeros (out of range)
+          // An out-of-range block reads zeros (TMA fill) and is recorded (error bit 1).
+          if (blk < 0 || blk >= p.num_blocks) atomicOr(&g_prefill_errors, 2);
+          row = blk * p.block_size + (kj % p.block_size);
         } else {
           row = k_begin + kj;
         }
@@ -610,7 +613,9 @@ __global__ void __launch_bounds__(kThreads2, 1) varlen_prefill_pair_kernel(const
         int row;
         if (p.paged) {
           const int blk = p.block_tables[int64_t(s) * p.bt_stride + kj / p.block_size];
-          row = blk * p.block_size + (kj % p.block_size);  // a bad (-1) block reads zeros (out of range)
+          // An out-of-range block reads zeros (TMA fill) and is recorded (error bit 1).
+          if (blk < 0 || blk >= p.num_blocks) atomicOr(&g_prefill_errors, 2);
+          row = blk * p.block_size + (kj % p.block_size);
         } else {
           row = k_begin + kj;
         }
@@ -956,6 +961,7 @@ extern "C" int hl_varlen_prefill(const void* q, int64_t q_row_stride, int64_t to
   prm.cu_k = cu_seqlens_k;
   prm.block_tables = block_tables;
   prm.bt_stride = bt_stride;
+  prm.num_blocks = block_tables ? num_blocks : 0;
   prm.paged = block_tables != nullptr;
   prm.block_size = block_size;
   prm.num_q_heads = num_q_heads;
@@ -981,6 +987,18 @@ extern "C" int hl_varlen_prefill_read_errors(int32_t* errors_out) {
   cudaError_t e = cudaMemcpyFromSymbol(errors_out, g_prefill_errors, sizeof(int32_t));
   if (e != cudaSuccess) {
     set_error("hl_varlen_prefill_read_errors: %s", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
+  return HL_OK;
+}
+
+extern "C" int hl_varlen_prefill_copy_errors_async(int32_t* dst, void* stream) {
+  clear_error();
+  HL_CHECK_ARG(dst, "hl_varlen_prefill_copy_errors_async: null pointer");
+  cudaError_t e = cudaMemcpyFromSymbolAsync(dst, g_prefill_errors, sizeof(int32_t), 0, cudaMemcpyDefault,
+                                            static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("hl_varlen_prefill_copy_errors_async: %s", cudaGetErrorString(e));
     return HL_ERR_CUDA;
   }
   return HL_OK;

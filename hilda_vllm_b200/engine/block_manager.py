@@ -5,6 +5,16 @@ mini_vllm/engine/block_manager.py:8-115: blocks are taken from the head of a FIF
 freed blocks go to its tail, a full block's hash is xxh64(previous block hash as 8
 little-endian bytes || token ids as int64 bytes), and a cached block is reused only when its
 stored token ids equal the request's.
+
+One departure, in what a reused block counts for: the reference registers a block's hash when
+the block is allocated, before any of its KV rows exist, and counts every hit as computed
+(block_manager.py:58-80, then scheduler.py:184 starts the prefill after the hits).  With chunked
+prefill the owner may not have reached that block yet, so a second sequence with the same prefix
+would start its prefill after rows nobody has written.  Here each block records whether its rows
+are written (or are written by a chunk scheduled earlier in the same step: the KV store of a step
+runs before its attention in every layer); hits still share the same block ids, but
+num_cached_tokens only counts the leading run of written blocks, and the sequence computes the
+rest itself, into the shared blocks.
 """
 from collections import deque
 
@@ -21,6 +31,7 @@ class Block:
         self.ref_count = 0
         self.hash = -1
         self.token_ids: list[int] = []
+        self.computed = False  # every row of the block is written (or scheduled to be, this step)
 
     def update(self, hash: int, token_ids: list[int]):
         self.hash = hash
@@ -30,12 +41,16 @@ class Block:
         self.ref_count = 1
         self.hash = -1
         self.token_ids = []
+        self.computed = False
 
 
 class BlockManager:
 
-    def __init__(self, num_blocks: int, block_size: int):
+    def __init__(self, num_blocks: int, block_size: int, count_unwritten_hits: bool = False):
         self.block_size = block_size
+        # True reproduces the reference: every hit counts as computed, written or not.
+        self.count_unwritten_hits = count_unwritten_hits
+        self.unwritten_hits = 0  # hits that were not counted (diagnostics)
         self.blocks: list[Block] = [Block(i) for i in range(num_blocks)]
         self.hash_to_block_id: dict[int, int] = {}
         self.deferred_hashes: list[tuple] = []  # (seq, page index, block id)
@@ -70,6 +85,7 @@ class BlockManager:
         assert not seq.block_table
         prev_hash = -1
         missed = False
+        counting = True  # hits still count as computed tokens (no unwritten block before them)
         for i in range(seq.num_blocks):
             token_ids = seq.block(i)
             full = len(token_ids) == self.block_size
@@ -80,12 +96,18 @@ class BlockManager:
             if missed:
                 block = self._allocate_block(self.free_block_ids[0])
             else:
-                seq.num_cached_tokens += self.block_size
+                if counting and not self.blocks[cached_id].computed and not self.count_unwritten_hits:
+                    counting = False
+                    self.unwritten_hits += 1
+                if counting:
+                    seq.num_cached_tokens += self.block_size
                 if cached_id in self.used_block_ids:
                     block = self.blocks[cached_id]
                     block.ref_count += 1
                 else:
+                    written = self.blocks[cached_id].computed  # a freed block keeps its rows
                     block = self._allocate_block(cached_id)
+                    block.computed = written
             if prev_hash != -1:
                 block.update(prev_hash, token_ids)
                 self.hash_to_block_id[prev_hash] = block.block_id
@@ -105,6 +127,13 @@ class BlockManager:
         needs_block = len(seq) % self.block_size == 1
         return len(self.free_block_ids) >= needs_block
 
+    def mark_computed(self, seq: Sequence, end: int) -> None:
+        """Blocks of `seq` wholly below token `end` have their rows written once this step runs
+        (called when a prefill chunk ending at `end` is scheduled)."""
+        table = seq.block_table
+        for i in range(seq.num_computed_tokens // self.block_size, min(end // self.block_size, len(table))):
+            self.blocks[table[i]].computed = True
+
     def may_append(self, seq: Sequence) -> None:
         table = seq.block_table
         last = self.blocks[table[-1]]
@@ -113,7 +142,10 @@ class BlockManager:
             # The newest token starts a new page.
             block = self._allocate_block(self.free_block_ids[0])
             table.append(block.block_id)
-        elif phase == 0 and last.hash == -1:
+        elif phase == 0:
+            # The newest token, written by this decode step, completes the last page.
+            last.computed = True
+        if phase == 0 and last.hash == -1:
             # The last page just filled up: register it in the prefix cache.
             token_ids = seq.block(seq.num_blocks - 1)
             if PLACEHOLDER in token_ids:

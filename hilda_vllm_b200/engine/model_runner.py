@@ -424,6 +424,12 @@ class ModelRunner:
         for module in self.attention_layers():
             module.decode_workspace = self.decode_workspace
         self.logits_buf = None
+        # Error words of the attention kernels (decode: word 0 of its workspace, prefill: the
+        # library's device word), copied to the host with each step's tokens and checked after
+        # the step's synchronisation: a bounded wait that gave up or a block id outside the pool
+        # leaves output rows unwritten, so the step must not return tokens.
+        self.err_bufs = [torch.zeros(2, dtype=torch.int32, device="cpu", pin_memory=True) for _ in range(2)]
+        self.decode_err_word = self.decode_workspace[:4].view(torch.int32)
 
     # ------------------------------------------------------------------ batch preparation
     def prepare_prefill(self, seqs: list[ScheduledSequence]):
@@ -600,6 +606,7 @@ class ModelRunner:
         self.io_bytes["d2h"] += 8 * bs
         if self.allreduce is not None:
             self.allreduce.copy_error_word()
+        self._queue_error_words(par)
         self.done_events[par].record()
         reset_context()
 
@@ -608,7 +615,26 @@ class ModelRunner:
         self.done_events[par].synchronize()
         if self.allreduce is not None:
             self.allreduce.check_errors()
+        self._check_error_words(par)
         return self.tokens_bufs[par][:bs].tolist()
+
+    def _queue_error_words(self, par: int) -> None:
+        """Queues device->host copies of the decode and prefill error words on the current stream."""
+        buf = self.err_bufs[par]
+        buf[0:1].copy_(self.decode_err_word, non_blocking=True)
+        kernels.copy_prefill_errors_async(buf[1:2])
+
+    def _check_error_words(self, par: int) -> None:
+        """Raises if an attention kernel recorded an error (after _queue_error_words and a sync)."""
+        dec, pre = (int(x) for x in self.err_bufs[par].tolist())
+        if dec or pre:
+            what = []
+            if (dec | pre) & 1:
+                what.append("a bounded wait for a tile copy timed out")
+            if (dec | pre) & 2:
+                what.append("a block table entry was outside the KV pool")
+            raise RuntimeError(f"attention kernel error on rank {self.rank} (decode word {dec}, prefill word {pre}): "
+                               + "; ".join(what) + "; outputs of that step are invalid")
 
     def _sample_rows(self, logits: torch.Tensor, samp) -> list[int]:
         """Tokens for rows of full-vocabulary logits (rank 0): greedy argmax, or a device draw with
@@ -638,9 +664,11 @@ class ModelRunner:
         if self.rank == 0:
             token_ids = [None] * n_sched
             if rows:
+                self._queue_error_words(0)
                 sub = logits[rows] if len(rows) != logits.shape[0] else logits
-                for i, t in zip(rows, self._sample_rows(sub.contiguous(), samp)):
+                for i, t in zip(rows, self._sample_rows(sub.contiguous(), samp)):  # synchronises
                     token_ids[i] = t
+                self._check_error_words(0)
         reset_context()
         return token_ids
 
@@ -684,10 +712,12 @@ class ModelRunner:
         self.io_bytes["d2h"] += 8 * bs
         if self.allreduce is not None:
             self.allreduce.copy_error_word()
+        self._queue_error_words(0)
         self.copy_done.record()
         self.copy_done.synchronize()
         if self.allreduce is not None:
             self.allreduce.check_errors()
+        self._check_error_words(0)
         reset_context()
         return self.tokens_host[:bs].tolist()
 

@@ -46,6 +46,7 @@ class Scheduler:
         self.max_num_batched_tokens = config.max_num_batched_tokens
         self.eos = config.eos
         self.drop_preempted_decode_token = bool(getattr(config, "drop_preempted_decode_token", False))
+        self.unblock_prefill_head = bool(getattr(config, "unblock_prefill_head", True))
         self.enable_chunked_prefill = config.enable_chunked_prefill
         self.chunked_prefill_size = config.chunked_prefill_size
         self.chunked_prefill_min_size = config.chunked_prefill_min_size
@@ -141,7 +142,9 @@ class Scheduler:
         return aligned if aligned > 0 else chunk_size
 
     # ------------------------------------------------------------------ scheduling
-    def _schedule_prefill(self) -> list[ScheduledSequence]:
+    def _schedule_prefill(self, skip_blocked: bool = False) -> list[ScheduledSequence]:
+        """skip_blocked: a sequence that cannot get its blocks is passed over instead of ending the
+        scan, so sequences behind it that already hold blocks (chunked prefills in progress) can run."""
         out: list[ScheduledSequence] = []
         admitted = 0
         active = len(self.running)
@@ -157,6 +160,8 @@ class Scheduler:
                     if self.debug_prefill:
                         print(f"[PREFILL] blocked on allocation: seq_id={seq.seq_id} len={len(seq)} "
                               f"free_blocks={len(self.block_manager.free_block_ids)} required_blocks={seq.num_blocks}")
+                    if skip_blocked:
+                        continue
                     break
                 self.block_manager.allocate(seq)
                 seq.num_computed_tokens = seq.num_cached_tokens
@@ -173,6 +178,7 @@ class Scheduler:
                 continue
             admitted += 1
             batched += chunk
+            self.block_manager.mark_computed(seq, seq.num_computed_tokens + chunk)
             out.append(ScheduledSequence(seq, chunk))
         return out
 
@@ -229,6 +235,14 @@ class Scheduler:
         if self.waiting:
             self.prefill_no_schedulable_steps += 1
         scheduled = self._schedule_decode()
+        if not scheduled and self.waiting and self.unblock_prefill_head:
+            # The head of the queue cannot get its blocks while nothing runs, but chunked prefills
+            # further back hold theirs: the reference stops here (the error below); let those
+            # finish instead, which frees blocks for the head once they complete.
+            scheduled = self._schedule_prefill(skip_blocked=True)
+            if scheduled:
+                self.last_step_was_prefill = True
+                return scheduled, True
         if not scheduled:
             raise RuntimeError("scheduler found no runnable prefill or decode work: "
                                f"running={len(self.running)} waiting={len(self.waiting)} "

@@ -243,6 +243,14 @@ def prefill_errors() -> int:
     return int(val.value)
 
 
+def copy_prefill_errors_async(dst: torch.Tensor) -> None:
+    """Queues a copy of the prefill kernel's error word into dst (an int32 element of pinned host
+    or device memory) on the current stream."""
+    assert dst.dtype == torch.int32 and dst.numel() >= 1
+    check(_lib.load().hl_varlen_prefill_copy_errors_async(dst.data_ptr(), torch.cuda.current_stream().cuda_stream),
+          "hl_varlen_prefill_copy_errors_async")
+
+
 # ------------------------------------------------------------------------ decode packing
 def pack_decode_batch(packet: torch.Tensor, graph_batch: int, block_size: int, slot_seq_ids: torch.Tensor,
                       slot_bt_lens: torch.Tensor, next_tokens: torch.Tensor, input_ids: torch.Tensor,
@@ -302,11 +310,14 @@ def qk_norm_rope(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, head_di
 def qk_norm_rope_store(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, head_dim: int,
                        q_weight: torch.Tensor, k_weight: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Tensor,
                        eps: float, k_cache: torch.Tensor, v_cache: torch.Tensor, slot_mapping: torch.Tensor,
-                       k_scale: torch.Tensor | None = None, v_scale: torch.Tensor | None = None) -> None:
+                       k_scale: torch.Tensor | None = None, v_scale: torch.Tensor | None = None,
+                       k_mirror: torch.Tensor | None = None, v_mirror: torch.Tensor | None = None) -> None:
     """qk_norm_rope plus the KV-cache store of the rotated k heads and the v heads, in one
     launch.  Caches are [NB, BS, Hk, D] bf16 (store_kvcache) or float8_e4m3fn (the FP8 store,
-    per-head scales optional); slot -1 skips a token."""
-    _cuda(qkv, q_weight, k_weight, cos_sin, positions, k_cache, v_cache, slot_mapping, k_scale, v_scale)
+    per-head scales optional); slot -1 skips a token.  With an FP8 store, k_mirror / v_mirror
+    (bf16 caches of the same shape) receive the bf16 rows in the same launch."""
+    _cuda(qkv, q_weight, k_weight, cos_sin, positions, k_cache, v_cache, slot_mapping, k_scale, v_scale, k_mirror,
+          v_mirror)
     assert qkv.stride(1) == 1 and cos_sin.dtype == torch.float32 and cos_sin.is_contiguous()
     assert positions.dtype == torch.int64 and positions.is_contiguous()
     assert slot_mapping.dtype == torch.int32 and slot_mapping.is_contiguous() and slot_mapping.numel() >= qkv.shape[0]
@@ -321,11 +332,22 @@ def qk_norm_rope_store(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, h
         assert sc is None or (sc.dtype == torch.float32 and sc.is_contiguous() and sc.numel() == num_kv_heads)
     num_slots = k_cache.numel() // (num_kv_heads * head_dim)
     lib = _lib.load()
-    check(lib.hl_qk_norm_rope_store(qkv.data_ptr(), qkv.stride(0), qkv.shape[0], num_q_heads, num_kv_heads, head_dim,
-                                    q_weight.data_ptr(), k_weight.data_ptr(), cos_sin.data_ptr(), positions.data_ptr(),
-                                    float(eps), k_cache.data_ptr(), v_cache.data_ptr(), kv_dtype,
-                                    slot_mapping.data_ptr(), num_slots, _p(k_scale), _p(v_scale), _stream(qkv)),
-          "hl_qk_norm_rope_store")
+    if k_mirror is None and v_mirror is None:
+        check(lib.hl_qk_norm_rope_store(qkv.data_ptr(), qkv.stride(0), qkv.shape[0], num_q_heads, num_kv_heads,
+                                        head_dim, q_weight.data_ptr(), k_weight.data_ptr(), cos_sin.data_ptr(),
+                                        positions.data_ptr(), float(eps), k_cache.data_ptr(), v_cache.data_ptr(),
+                                        kv_dtype, slot_mapping.data_ptr(), num_slots, _p(k_scale), _p(v_scale),
+                                        _stream(qkv)), "hl_qk_norm_rope_store")
+        return
+    assert kv_dtype == 1 and k_mirror is not None and v_mirror is not None
+    for m in (k_mirror, v_mirror):
+        assert m.dtype == torch.bfloat16 and m.is_contiguous() and m.shape == k_cache.shape
+    check(lib.hl_qk_norm_rope_store_mirrored(qkv.data_ptr(), qkv.stride(0), qkv.shape[0], num_q_heads, num_kv_heads,
+                                             head_dim, q_weight.data_ptr(), k_weight.data_ptr(), cos_sin.data_ptr(),
+                                             positions.data_ptr(), float(eps), k_cache.data_ptr(), v_cache.data_ptr(),
+                                             kv_dtype, slot_mapping.data_ptr(), num_slots, _p(k_scale), _p(v_scale),
+                                             k_mirror.data_ptr(), v_mirror.data_ptr(), _stream(qkv)),
+          "hl_qk_norm_rope_store_mirrored")
 
 
 def sample(logits: torch.Tensor, temperatures: torch.Tensor | None, seed: int, step_state: torch.Tensor | None,

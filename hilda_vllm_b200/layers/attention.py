@@ -46,14 +46,19 @@ class Attention(nn.Module):
         self.decode_workspace: torch.Tensor | None = None
 
     def _store_target(self, context):
-        """(k_cache, v_cache, k_scale, v_scale) this step's new K/V go to, or None before the
-        KV pool exists (the reference's forward skips the store then, attention.py:146)."""
+        """(k_cache, v_cache, k_scale, v_scale, mirror) this step's new K/V go to, or None before
+        the KV pool exists (the reference's forward skips the store then, attention.py:146).
+        FP8 decode steps also write the bf16 rows into the BF16 prefill cache (mirror), which the
+        reference does not (attention.py:133): a block filled during decode can later be a
+        prefix-cache hit whose BF16 rows the prefill reads and the prefill->decode copy re-quantises,
+        and with the mirror those rows are the real ones instead of whatever the block held before."""
         if self.kv_cache_dtype == "fp8" and self.prefill_k_cache.numel() and self.decode_k_cache.numel():
             if context.is_prefill:
-                return self.prefill_k_cache, self.prefill_v_cache, None, None
-            return self.decode_k_cache, self.decode_v_cache, self.k_scale, self.v_scale
+                return self.prefill_k_cache, self.prefill_v_cache, None, None, None
+            return (self.decode_k_cache, self.decode_v_cache, self.k_scale, self.v_scale,
+                    (self.prefill_k_cache, self.prefill_v_cache))
         if self.k_cache.numel() and self.v_cache.numel():
-            return self.k_cache, self.v_cache, None, None
+            return self.k_cache, self.v_cache, None, None, None
         return None
 
     def rotate_and_store(self, qkv, q_weight, k_weight, cos_sin, positions, eps) -> bool:
@@ -66,9 +71,11 @@ class Attention(nn.Module):
             kernels.qk_norm_rope(qkv, self.num_heads, self.num_kv_heads, self.head_dim, q_weight, k_weight, cos_sin,
                                  positions, eps)
             return False
-        k_cache, v_cache, k_scale, v_scale = target
+        k_cache, v_cache, k_scale, v_scale, mirror = target
+        k_mirror, v_mirror = mirror if mirror is not None else (None, None)
         kernels.qk_norm_rope_store(qkv, self.num_heads, self.num_kv_heads, self.head_dim, q_weight, k_weight, cos_sin,
-                                   positions, eps, k_cache, v_cache, context.slot_mapping, k_scale, v_scale)
+                                   positions, eps, k_cache, v_cache, context.slot_mapping, k_scale, v_scale,
+                                   k_mirror=k_mirror, v_mirror=v_mirror)
         return True
 
     def _prefill(self, q, k, v, k_cache, v_cache, context):
@@ -93,6 +100,7 @@ class Attention(nn.Module):
             if not kv_stored:
                 store_kvcache_fp8(k, v, self.decode_k_cache, self.decode_v_cache, context.slot_mapping,
                                   self.k_scale, self.v_scale)
+                store_kvcache(k, v, self.prefill_k_cache, self.prefill_v_cache, context.slot_mapping)
             return self._decode(q, self.decode_k_cache, self.decode_v_cache, context, self.k_scale, self.v_scale)
 
         k_cache, v_cache = self.k_cache, self.v_cache

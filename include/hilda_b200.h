@@ -159,6 +159,12 @@ int hl_paged_decode_noalloc(const void* q, int64_t q_row_stride,
 /* Size in bytes of the scratch array behind hl_paged_decode_noalloc. */
 int64_t hl_paged_decode_noalloc_capacity(void);
 
+/* Error bits (as hl_paged_decode_read_errors) of the most recent hl_paged_decode_noalloc call on
+ * the current device: each call clears the word before its launch, so read it after the call
+ * whose status matters and before the next one.  Synchronises `stream`; allocates nothing.  Like
+ * hl_paged_decode_noalloc it has no counterpart in the reference. */
+int hl_paged_decode_noalloc_read_errors(int32_t* errors_out, void* stream);
+
 /* Reads the error word the decode kernel keeps in its workspace (bit 0: an mbarrier wait
  * timed out; bit 1: a block id was out of range).  Synchronous: copies 4 bytes to host. */
 int hl_paged_decode_read_errors(const void* workspace, int32_t* errors_out, void* stream);
@@ -194,8 +200,15 @@ int hl_varlen_prefill(const void* q, int64_t q_row_stride, int64_t total_q,
                       int block_size, int64_t num_blocks, float softmax_scale,
                       void* out, int64_t out_row_stride, int precise_p, void* stream);
 
-/* Error bits of the tensor-core prefill kernel (bit 0: an mbarrier wait timed out).  Synchronous. */
+/* Error bits of the tensor-core prefill kernel (bit 0: an mbarrier wait timed out; bit 1: a
+ * block id of a key tile was out of range, the tile read as zeros).  Sticky for the process on
+ * the current device.  Synchronous.  Replaces, as a status the host reads, the Python assertions
+ * of mini_vllm/layers/attention.py:86-89. */
 int hl_varlen_prefill_read_errors(int32_t* errors_out);
+
+/* The same 4 bytes copied asynchronously on `stream` into dst (pinned host or device memory),
+ * so a caller can fetch them together with a step's other results without an extra sync. */
+int hl_varlen_prefill_copy_errors_async(int32_t* dst, void* stream);
 
 /* ------------------------------------------------------------------------------------
  * Decode-batch packing on the GPU.
@@ -285,6 +298,21 @@ int hl_qk_norm_rope_store(void* qkv, int64_t row_stride, int num_tokens, int num
                           const int64_t* positions, float eps, void* k_cache, void* v_cache, int kv_dtype,
                           const int32_t* slot_mapping, int64_t num_slots, const float* k_scale,
                           const float* v_scale, void* stream);
+
+/* hl_qk_norm_rope_store with an FP8 store (kv_dtype = HL_KV_FP8_E4M3) that also writes the
+ * rotated bf16 K rows and the V rows into k_mirror / v_mirror (bf16 caches of the same
+ * [num_slots, Hk*128] row layout): the FP8 mode's BF16 prefill cache then holds the decode-step
+ * tokens as well.  The reference's decode step writes only the FP8 cache
+ * (mini_vllm/layers/attention.py:133), so a prefix-cache hit on a block filled during decode
+ * (block_manager.py may_append registers it) followed by the prefill->decode copy
+ * (model_runner.py:484-502) reads stale BF16 rows; with the mirror both caches agree.
+ * k_mirror = v_mirror = NULL makes it exactly hl_qk_norm_rope_store. */
+int hl_qk_norm_rope_store_mirrored(void* qkv, int64_t row_stride, int num_tokens, int num_q_heads,
+                                   int num_kv_heads, int head_dim, const void* q_weight, const void* k_weight,
+                                   const float* cos_sin, const int64_t* positions, float eps, void* k_cache,
+                                   void* v_cache, int kv_dtype, const int32_t* slot_mapping, int64_t num_slots,
+                                   const float* k_scale, const float* v_scale, void* k_mirror, void* v_mirror,
+                                   void* stream);
 
 /* out = silu(in[:, :I]) * in[:, I:2I]  (SiluAndMul, mini_vllm/layers/activation.py:12-16). */
 int hl_silu_mul(const void* in, int64_t in_stride, void* out, int64_t out_stride, int rows,

@@ -39,6 +39,17 @@ def quantize_e4m3(x_bf16: torch.Tensor, scale: torch.Tensor | None) -> torch.Ten
     return torch.from_numpy(out).reshape(shape)
 
 
+def quantize_e4m3_torch(x_bf16: torch.Tensor, scale: torch.Tensor | None) -> torch.Tensor:
+    """quantize_e4m3 in torch on any device: clamp(x / scale[h], -448, 448) cast to e4m3 (round to
+    nearest even), as uint8 bytes.  The clamp is what saturates: a plain cast turns overflow into
+    NaN.  Equal to the C restatement on every finite bf16 input (checked exhaustively on the CPU),
+    so a GPU-resident oracle can quantise without a host round trip."""
+    x = x_bf16.float()
+    if scale is not None:
+        x = x / scale.float().to(x.device).view(*([1] * (x.dim() - 2)), -1, 1)
+    return torch.clamp(x, -448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8)
+
+
 def dequantize_e4m3(q_u8: torch.Tensor, scale: torch.Tensor | None) -> torch.Tensor:
     """uint8 e4m3 bytes [..., Hk, D] -> fp32 value * scale[h]."""
     x = q_u8.view(torch.float8_e4m3fn).float()

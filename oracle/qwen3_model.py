@@ -18,12 +18,13 @@ import torch
 import torch.nn.functional as F
 
 from oracle import attention as oattn
+from oracle import kv_store
 
 
 class Qwen3Oracle:
 
     def __init__(self, hf_config, weights: dict[str, torch.Tensor], num_blocks: int, block_size: int,
-                 device="cpu", dtype=torch.bfloat16):
+                 device="cpu", dtype=torch.bfloat16, kv_fp8: bool = False, kv_scale: float = 1.0):
         c = hf_config
         self.c = c
         self.device = torch.device(device)
@@ -51,6 +52,17 @@ class Qwen3Oracle:
         shape = (c.num_hidden_layers, num_blocks, block_size, self.hk, self.d)
         self.k_cache = torch.zeros(shape, dtype=dtype, device=self.device)
         self.v_cache = torch.zeros(shape, dtype=dtype, device=self.device)
+        # FP8 KV mode (attention.py:114-141, model_runner.py:186-194, 483-502): the bf16 caches above
+        # are the prefill cache, k8/v8 the e4m3 decode cache with per-head scales.  Prefill writes
+        # and reads bf16; convert() quantises prompt rows into the decode cache; a decode step
+        # stores its new row quantised (and, as intended, in bf16 too, so the prefill cache holds
+        # every token) and attends over the dequantised e4m3 cache.
+        self.kv_fp8 = kv_fp8
+        if kv_fp8:
+            self.k8 = torch.zeros(shape, dtype=torch.uint8, device=self.device)
+            self.v8 = torch.zeros(shape, dtype=torch.uint8, device=self.device)
+            self.k_scale = torch.full((self.hk,), float(kv_scale), dtype=torch.float32, device=self.device)
+            self.v_scale = torch.full((self.hk,), float(kv_scale), dtype=torch.float32, device=self.device)
 
     # -- layers (reference arithmetic) --
     def rms(self, x, w):
@@ -80,9 +92,26 @@ class Qwen3Oracle:
         kf[sm[keep]] = k.reshape(k.shape[0], -1)[keep]
         vf[sm[keep]] = v.reshape(v.shape[0], -1)[keep]
 
+    def convert(self, slots):
+        """FP8 mode: quantise the bf16 prefill-cache rows at `slots` into the e4m3 decode cache of
+        every layer (copy_kvcache_fp8, attention.py:55-56)."""
+        sl = torch.as_tensor(slots, dtype=torch.long, device=self.device)
+        for layer in range(self.c.num_hidden_layers):
+            for src, dst, sc in ((self.k_cache, self.k8, self.k_scale), (self.v_cache, self.v8, self.v_scale)):
+                rows = src[layer].view(-1, self.hk, self.d)[sl]
+                dst[layer].view(-1, self.hk, self.d)[sl] = kv_store.quantize_e4m3_torch(rows, sc)
+
     def attention(self, layer, q, k, v, ctx):
         self.store(layer, k, v, ctx["slot_mapping"])
         scale = self.d ** -0.5
+        if self.kv_fp8 and not ctx["is_prefill"]:
+            sm = ctx["slot_mapping"].to(self.device).long()
+            keep = sm >= 0
+            for src, dst, sc in ((k, self.k8, self.k_scale), (v, self.v8, self.v_scale)):
+                dst[layer].view(-1, self.hk, self.d)[sm[keep]] = kv_store.quantize_e4m3_torch(src[keep], sc)
+            o = oattn.paged_decode(q, self.k8[layer], self.v8[layer], ctx["block_tables"], ctx["context_lens"], scale,
+                                   self.k_scale, self.v_scale, fp8=True)
+            return o.to(self.dtype)
         if ctx["is_prefill"]:
             if ctx.get("block_tables") is not None:
                 o = oattn.varlen_prefill(q, self.k_cache[layer], self.v_cache[layer], ctx["cu_seqlens_q"],

@@ -238,3 +238,26 @@ def test_top_k_1_equals_greedy_oracle(tmp_path, golden_dir):
                                                                          ignore_eos=True), use_tqdm=False)]
     llm.exit()
     assert top1 == greedy
+
+
+def test_block_outside_the_pool_makes_generate_raise(tmp_path, golden_dir):
+    """The attention kernels' error words reach the caller: a block id outside the KV pool (put at
+    the head of the free list) is rejected by the decode kernel's bounds check before any load, the
+    error word travels back with the step's tokens, and LLM.generate raises instead of returning
+    tokens computed from unwritten rows."""
+    from hilda_vllm_b200.engine.block_manager import Block
+
+    d = tiny_dir(tmp_path, golden_dir)
+    llm = LLM(str(d), load_format="random", seed=7, max_num_seqs=4, max_model_len=1024, max_num_batched_tokens=2048,
+              kvcache_block_cap=16, gpu_memory_utilization=0.3)
+    bm = llm.scheduler.block_manager
+    nb = len(bm.blocks)
+    bad = nb + 5
+    bm.blocks.extend(Block(i) for i in range(nb, bad + 1))
+    bm.free_block_ids.appendleft(bad)
+    try:
+        with pytest.raises(RuntimeError, match="outside the KV pool"):
+            llm.generate([list(range(1, 40))], SamplingParams(greedy=True, max_tokens=6, ignore_eos=True),
+                         use_tqdm=False)
+    finally:
+        llm.exit()

@@ -372,10 +372,12 @@ def test_qk_norm_rope_matches_reference_modules(golden_dir):
 
 
 @pytest.mark.parametrize("kv,hq,hk,n", [("bf16", 16, 8, 300), ("fp8", 16, 8, 257), ("fp8s", 8, 2, 64),
-                                        ("bf16", 4, 1, 1)])
+                                        ("bf16", 4, 1, 1), ("fp8m", 16, 8, 129), ("fp8sm", 8, 2, 64)])
 def test_fused_rope_store_equals_rope_then_store(kv, hq, hk, n):
     """hl_qk_norm_rope_store == hl_qk_norm_rope followed by the store kernel, byte for byte, in
-    the qkv rows and in both caches (strided rows, skipped slots, untouched cache rows)."""
+    the qkv rows and in both caches (strided rows, skipped slots, untouched cache rows).  "m" cases:
+    the FP8 store with bf16 mirror caches (hl_qk_norm_rope_store_mirrored), whose mirror rows must
+    equal the BF16 store of the same rotated rows."""
     from hilda_vllm_b200.layers.rotary_embedding import RotaryEmbedding
     g = torch.Generator().manual_seed(n + hq)
     d, nb, bs = 128, 8, 256
@@ -389,8 +391,9 @@ def test_fused_rope_store_equals_rope_then_store(kv, hq, hk, n):
     slots = slots.to(DEV)
     cos_sin = RotaryEmbedding(d, d, 4096, 1000000.0).cos_sin_cache.to(DEV).contiguous()
     fp8 = kv != "bf16"
-    ks = (torch.rand(hk, generator=g) + 0.3).to(DEV) if kv == "fp8s" else None
-    vs = (torch.rand(hk, generator=g) + 0.3).to(DEV) if kv == "fp8s" else None
+    mirrored = kv.endswith("m")
+    ks = (torch.rand(hk, generator=g) + 0.3).to(DEV) if kv.startswith("fp8s") else None
+    vs = (torch.rand(hk, generator=g) + 0.3).to(DEV) if kv.startswith("fp8s") else None
     dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
     init = torch.randn(nb, bs, hk, d, generator=g).to(dt)
     caches = [[init.clone().to(DEV), init.clone().to(DEV)] for _ in range(2)]
@@ -403,16 +406,24 @@ def test_fused_rope_store_equals_rope_then_store(kv, hq, hk, n):
     kernels.qk_norm_rope(rows[0], hq, hk, d, qw, kw, cos_sin, pos, 1e-6)
     k = rows[0][:, hq * d:(hq + hk) * d].view(n, hk, d)
     v = rows[0][:, (hq + hk) * d:].view(n, hk, d)
+    minit = torch.randn(nb, bs, hk, d, generator=g).bfloat16()
+    mirrors = [[minit.clone().to(DEV), minit.clone().to(DEV)] for _ in range(2)] if mirrored else [[None, None]] * 2
     if fp8:
         kernels.store_kvcache_fp8(k, v, caches[0][0], caches[0][1], slots, ks, vs)
+        if mirrored:
+            kernels.store_kvcache(k, v, mirrors[0][0], mirrors[0][1], slots)
     else:
         kernels.store_kvcache(k, v, caches[0][0], caches[0][1], slots)
     kernels.qk_norm_rope_store(rows[1], hq, hk, d, qw, kw, cos_sin, pos, 1e-6, caches[1][0], caches[1][1], slots,
-                               ks, vs)
+                               ks, vs, k_mirror=mirrors[1][0], v_mirror=mirrors[1][1])
     assert rows[1].stride(0) == width + 64
     assert torch.equal(rows[0].contiguous().view(torch.int16), rows[1].contiguous().view(torch.int16))
     for a, b in zip(caches[0], caches[1]):
         assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+    if mirrored:
+        for a, b in zip(mirrors[0], mirrors[1]):
+            assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+        assert not torch.equal(mirrors[1][0].cpu().view(torch.int16), minit.view(torch.int16))  # rows were written
 
 
 def test_silu_mul_matches_reference_module(golden_dir):

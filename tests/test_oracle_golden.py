@@ -49,6 +49,17 @@ def test_e4m3_c_oracle_matches_torch_exhaustively():
     assert ((dec == tdec) | both_nan).all()
 
 
+def test_e4m3_torch_quantiser_equals_c_oracle():
+    """quantize_e4m3_torch (the GPU-resident oracle's quantiser) equals the C restatement on every
+    finite bf16 value, with per-head scales."""
+    allb = torch.arange(0, 65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    vals = allb[torch.isfinite(allb.float())]
+    n = vals.numel() // 4 * 4
+    x = vals[:n].view(-1, 4, 1).expand(-1, 4, 16).contiguous().view(-1, 4, 16)
+    for sc in (None, torch.tensor([1.0, 0.37, 3.5, 1e-3])):
+        assert torch.equal(kv_store.quantize_e4m3_torch(x, sc), kv_store.quantize_e4m3(x, sc))
+
+
 def test_fp8_store_and_copy_oracles_agree():
     g = torch.Generator().manual_seed(5)
     key = (torch.randn(6, 2, 128, generator=g) * 40).bfloat16()

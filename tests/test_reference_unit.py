@@ -124,9 +124,28 @@ def test_allocate_reuses_cached_full_prefix_block():
     m = BlockManager(num_blocks=4, block_size=2)
     s1, s2 = Sequence([1, 2, 3]), Sequence([1, 2, 9])
     m.allocate(s1)
+    # Departure from the reference: a hit counts as computed only once its rows are written (or
+    # scheduled to be, as the scheduler marks s1's prefill chunk here).
+    m.mark_computed(s1, len(s1))
     m.allocate(s2)
     shared = s1.block_table[0]
     assert s2.block_table[0] == shared and s2.num_cached_tokens == 2 and m.blocks[shared].ref_count == 2
+
+
+def test_hit_on_unwritten_block_is_shared_but_not_counted():
+    """The reference counts a hit on a block whose owner has not computed it yet (a chunked
+    prefill still before it) as cached, so the second sequence would start after rows nobody
+    wrote; here the block is shared all the same but the sequence computes it itself."""
+    Sequence.block_size = 2
+    m = BlockManager(num_blocks=6, block_size=2)
+    s1, s2 = Sequence([1, 2, 3, 4, 5]), Sequence([1, 2, 3, 4, 9])
+    m.allocate(s1)
+    m.mark_computed(s1, 2)  # s1's first chunk covers block 0 only
+    m.allocate(s2)
+    assert s2.block_table[:2] == s1.block_table[:2] and s2.num_cached_tokens == 2
+    s3 = Sequence([1, 2, 3, 4, 7])
+    m.allocate(s3)
+    assert s3.block_table[:2] == s1.block_table[:2] and s3.num_cached_tokens == 2
 
 
 def test_deallocate_returns_blocks_to_free_pool():
@@ -222,3 +241,35 @@ def test_top_p_masks_tail_outside_probability_mass():
 def test_top_p_uses_strict_boundary():
     logits = torch.log(torch.tensor([0.5, 0.3, 0.15, 0.05]))
     assert kept_set(logits, 1.0, -1, 0.8).tolist() == [True, False, False, False]
+
+
+# ---- this build's additions to the scheduler (each departs from the reference only where the
+# reference would stop with an error)
+@pytest.mark.parametrize("unblock", [True, False])
+def test_held_chunked_prefill_runs_when_the_queue_head_cannot_allocate(unblock):
+    """A (6 tokens, 3 blocks) is prefilled in chunks of 2 and goes back to the end of the queue;
+    B (4 tokens, 2 blocks) is then at the head but only 1 block is free and nothing runs.  The
+    reference raises "no runnable work"; with unblock_prefill_head A's next chunk runs instead,
+    and once A is done and finishes, B gets its blocks."""
+    Sequence.block_size = 2
+    s = Scheduler(make_config(max_num_batched_tokens=2, num_kvcache_blocks=4, max_num_seqs=4,
+                              unblock_prefill_head=unblock))
+    a = Sequence([1, 2, 3, 4, 5, 6], SamplingParams(max_tokens=1, ignore_eos=True))
+    b = Sequence([7, 8, 9, 10], SamplingParams(max_tokens=1, ignore_eos=True))
+    s.add(a)
+    s.add(b)
+    first, is_prefill = s.schedule()
+    assert is_prefill and [(x.seq, x.token_chunk_size) for x in first] == [(a, 2)]
+    s.postprocess(first, [None], True)
+    assert list(s.waiting) == [b, a] and len(s.block_manager.free_block_ids) == 1
+    if not unblock:
+        with pytest.raises(RuntimeError, match="no runnable prefill or decode work"):
+            s.schedule()
+        return
+    seen = []
+    while not s.is_finished():
+        sched, is_prefill = s.schedule()
+        seen.append([(x.seq.seq_id, x.token_chunk_size) for x in sched if x.seq is not None])
+        toks = [77 if (x.seq is not None and (not is_prefill or x.requires_sampling)) else None for x in sched]
+        s.postprocess(sched, toks, is_prefill)
+    assert seen[0] == [(a.seq_id, 2)] and a.is_finished and b.is_finished

@@ -31,7 +31,9 @@ def _load(golden_dir, name):
 def _replay(trace, seq_block_size, on_step=None):
     meta = trace["meta"]
     seq_block_size(meta["block_size"])
-    cfg = SimpleNamespace(**meta["cfg"])
+    # The reference stops with "no runnable work" where this scheduler would let held chunked
+    # prefills proceed; the traces pin the reference's behaviour, so that escape is off here.
+    cfg = SimpleNamespace(**meta["cfg"], unblock_prefill_head=False)
     sched = Scheduler(cfg)
     prompts, params = meta["prompts"], meta["params"]
     seqs = {}
