@@ -56,13 +56,14 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"],
-                    help="c2 (default, the headline): BASELINE configs[1]; c3: FP8 KV with a capped pool; "
-                         "c4: mixed chunked prefill + decode with shared prefixes; c5: Qwen3-8B (TP over --gpus)")
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"],
+                    help="c2 (default, the headline): BASELINE configs[1]; c1: the single-op KV store + paged "
+                         "decode of configs[0]; c3: FP8 KV with a capped pool; c4: mixed chunked prefill + "
+                         "decode with shared prefixes; c5: Qwen3-8B (TP over --gpus)")
     ap.add_argument("--kv", default="auto", choices=["auto", "fp8"], help="KV cache dtype for c5")
     ap.add_argument("--profile", default="",
                     choices=["", "decode-kernel", "decode-kernel-tc", "decode-steps", "prefill-kernel", "small-kernels",
-                             "allreduce"],
+                             "allreduce", "reference-kernels"],
                     help="run a short profiling case instead of the benchmark: the CUDA profiler range "
                          "(cudaProfilerStart/Stop, for ncu --profile-from-start off) covers --steps "
                          "launches of the decode kernel alone (decode-kernel), of the prefill kernel "
@@ -208,6 +209,20 @@ def run_reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def run_c1_reference(args):
+    """--impl reference --workload c1: the config-1 op on the host cores (CPU oracle)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    cpu = c1_cpu_sample(args.seed, reps=max(args.steps, 1))
+    line = {"impl": "reference", "metric": "config-1 single op (KV store + paged decode, 8 seqs): ops/s",
+            "value": cpu["value"], "unit": "ops/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 / cpu["value"], 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) cache, q and new K/V)",
+            "config": {"workload": "c1: BASELINE configs[0] on the host cores"}, "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": "ops/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- GPU arm
 def run_ours(args):
     import torch
@@ -297,6 +312,9 @@ def run_ours(args):
                 "samples": len(samples), "avg_launch_us": round(1e6 * ktime / max(1, len(samples)), 2),
                 "bytes_per_launch_avg": int(kbytes / max(1, len(samples)))}
 
+    # ---- the reference's own attention kernels (flash-attn) beside ours, same inputs, this GPU ----
+    ref_kernels = reference_kernel_ab(args.seed, reps=10) if world == 1 else None
+
     # ---- end-to-end through the public API ----
     e2e = None
     if not args.no_e2e:
@@ -363,13 +381,62 @@ def run_ours(args):
         "decode_ms_per_batch_step": round(sweep_s * 1e3 / steps_per_sweep, 4),
         "roofline": roofline,
         "kv_weight_roofline": job_roofline,
+        "reference_kernels": ref_kernels,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "clocks": clocks,
         "gpu_launches": launches_per_step * steps_per_sweep * args.steps,
     }
-    print(json.dumps(line), flush=True)
+    completions = [o["token_ids"] for o in outs] if e2e else None
+    if world == 1:
+        if completions is not None:
+            line["parity"] = greedy_parity(llm, prompts, completions, "this engine's prefill path (same GPU)")
+        print(json.dumps(line), flush=True)
+        llm.exit()
+        return
+    # Tensor parallel: tear the TP engine down, then check its greedy tokens on rank 0's GPU with a
+    # single-GPU engine of the same seeded weights.
+    import gc
+
     llm.exit()
+    del runner, llm
+    gc.collect()
+    torch.cuda.empty_cache()
+    if completions is not None:
+        from hilda_vllm_b200 import LLM as _LLM
+        ref = _LLM(str(CFG_DIR), load_format="random", seed=args.seed, max_num_seqs=64, max_model_len=MAX_MODEL_LEN,
+                   max_num_batched_tokens=16384, enforce_eager=True, kvcache_block_cap=256, gpu_memory_utilization=0.5)
+        line["parity"] = greedy_parity(ref, prompts, completions, "a 1-GPU engine with the same weights")
+        ref.exit()
+    print(json.dumps(line), flush=True)
+
+
+def greedy_parity(engine, prompts, completions, against: str, seqs: int = 8, steps: int = 32) -> dict:
+    """Teacher-forced check of the first `steps` decode tokens (plus the prefill token) of the first
+    `seqs` sequences: engine.score_next_tokens(prompt + first s tokens) must pick token s, or hold it
+    within two bf16 ulps of its top logit (a tie: bf16 logits of a random-init model often tie)."""
+    import math
+
+    lists, targets = [], []
+    for p, c in zip(prompts[:seqs], completions[:seqs]):
+        for k in range(min(steps + 1, len(c))):
+            lists.append(list(p) + list(c[:k]))
+            targets.append(int(c[k]))
+    res = engine.score_next_tokens(lists, targets)
+    exact = ties = bad = 0
+    for r, t in zip(res, targets):
+        if r["argmax"] == t:
+            exact += 1
+            continue
+        top = r["top_logit"]
+        ulp = 2.0 ** (math.floor(math.log2(abs(top))) - 7) if top != 0 else 2.0 ** -133
+        if top - r["target_logit"] <= 2 * ulp:
+            ties += 1
+        else:
+            bad += 1
+    n = len(targets)
+    return {"seqs": seqs, "steps": steps, "checked": n, "exact": exact, "ties": ties, "bad": bad,
+            "ok": bad == 0 and exact >= 0.9 * n, "against": against + ", teacher-forced"}
 
 
 def small_kernels(args, g):
@@ -552,6 +619,238 @@ def allreduce_profile(args):
     dist.destroy_process_group()
 
 
+def _paged_case(g, lens, hq, hk, dev, bs=256, fp8=False):
+    """Seeded paged-decode inputs: contiguous random pages per sequence (-1 padded tables)."""
+    import torch
+
+    d = 128
+    nblk = [max(1, -(-int(n) // bs)) for n in lens]
+    mb = max(nblk)
+    perm = torch.randperm(sum(nblk), generator=g).tolist()
+    tables, off = [], 0
+    for n in nblk:
+        tables.append(perm[off:off + n] + [-1] * (mb - n))
+        off += n
+    kc = torch.randn(sum(nblk), bs, hk, d, generator=g).bfloat16().to(dev)
+    vc = torch.randn(sum(nblk), bs, hk, d, generator=g).bfloat16().to(dev)
+    if fp8:
+        kc, vc = kc.to(torch.float8_e4m3fn), vc.to(torch.float8_e4m3fn)
+    q = torch.randn(len(lens), hq, d, generator=g).bfloat16().to(dev)
+    bt = torch.tensor(tables, dtype=torch.int32, device=dev)
+    ln = torch.tensor([int(n) for n in lens], dtype=torch.int32, device=dev)
+    return q, kc, vc, bt, ln
+
+
+def _time_flushed(fn, reps, flush):
+    """Mean seconds of fn() over reps launches, each timed alone with CUDA events on the current
+    stream after a write of `flush` (larger than L2) so no launch finds the previous one's data in L2."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(reps):
+        flush.add_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        total += e0.elapsed_time(e1) / 1e3
+    return total / reps
+
+
+def reference_kernel_ab(seed: int = 0, reps: int = 20) -> dict:
+    """This repository's attention kernels against the reference's own (flash-attn 2.x, called with
+    the reference's exact signatures, mini_vllm/layers/attention.py:149-170) on identical inputs on
+    this GPU: decode at the config-1 shapes (8 sequences, contexts U[16, 1024]), at config-2 mid-job
+    (256 sequences, contexts U[65, 1087]) and at the config-5 layout (Qwen3-8B heads, GQA 4,
+    contexts U[512, 1280]); varlen chunked prefill at the config-4 shape (8 chunks of 4096-8192 new
+    tokens over a 2048-token cached prefix, paged).  Each launch timed alone, L2 flushed before it."""
+    import itertools
+
+    import torch
+
+    from hilda_vllm_b200 import kernels
+
+    try:
+        from flash_attn import flash_attn_varlen_func, flash_attn_with_kvcache
+    except Exception as exc:  # pragma: no cover - depends on the installed wheel
+        return {"unavailable": f"flash-attn not importable: {type(exc).__name__}"}
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator().manual_seed(seed)
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)  # 256 MB > 126 MB of L2
+    scale = 128 ** -0.5
+    res = {"timing": "CUDA events per launch, L2 flushed (256 MB write) before each launch, mean of "
+                     f"{reps}", "reference": "flash-attn 2.x with the reference's call signatures"}
+    decode_cases = {
+        "decode_c1": ([int(x) for x in torch.randint(16, 1025, (8,), generator=g)], 16, 8),
+        "decode_c2_mid": ([int(x) for x in torch.randint(PROMPT_LEN + 1, PROMPT_LEN + OUTPUT_LEN, (NUM_SEQS,),
+                                                         generator=g)], 16, 8),
+        "decode_c5_layout": ([int(x) for x in torch.randint(512, 1281, (NUM_SEQS,), generator=g)], 32, 8),
+    }
+    for name, (lens, hq, hk) in decode_cases.items():
+        q, kc, vc, bt, ln = _paged_case(g, lens, hq, hk, dev)
+        out = torch.empty_like(q)
+        ws = kernels.make_decode_workspace(len(lens), hq, 128, bt.shape[1], 256, dev)
+        ours = _time_flushed(lambda: kernels.paged_decode(q, kc, vc, bt, ln, scale, out=out, workspace=ws), reps,
+                             flush)
+        q4 = q.unsqueeze(1)
+        ref = _time_flushed(lambda: flash_attn_with_kvcache(q4, kc, vc, cache_seqlens=ln, block_table=bt,
+                                                            softmax_scale=scale, causal=True), reps, flush)
+        nbytes = sum(lens) * hk * 128 * 2 * 2 + len(lens) * hq * 128 * 2 * 2
+        res[name] = {"seqs": len(lens), "hq": hq, "hk": hk, "ours_us": round(ours * 1e6, 2),
+                     "reference_us": round(ref * 1e6, 2), "speedup": round(ref / ours, 3),
+                     "ours_gbs": round(nbytes / ours / 1e9, 1), "reference_gbs": round(nbytes / ref / 1e9, 1)}
+        del q, kc, vc, bt, ln, out, ws
+    # config-4 prefill shape
+    hq, hk, bs, prefix = 16, 8, 256, 2048
+    chunks = [int(x) for x in torch.randint(4096, 8193, (8,), generator=g)]
+    kl = [prefix + c for c in chunks]
+    _, kc, vc, bt, _ = _paged_case(g, kl, hq, hk, dev)
+    tq = sum(chunks)
+    q = torch.randn(tq, hq, 128, generator=g).bfloat16().to(dev)
+    cuq = torch.tensor([0] + list(itertools.accumulate(chunks)), dtype=torch.int32, device=dev)
+    cuk = torch.tensor([0] + list(itertools.accumulate(kl)), dtype=torch.int32, device=dev)
+    flops = sum(4 * hq * 128 * (c * prefix + c * (c + 1) // 2) for c in chunks)
+    ours = _time_flushed(lambda: kernels.varlen_prefill(q, kc, vc, cuq, cuk, max(chunks), max(kl), scale,
+                                                        block_table=bt), max(3, reps // 4), flush)
+    ref = _time_flushed(lambda: flash_attn_varlen_func(q, kc, vc, max_seqlen_q=max(chunks), cu_seqlens_q=cuq,
+                                                       max_seqlen_k=max(kl), cu_seqlens_k=cuk, softmax_scale=scale,
+                                                       causal=True, block_table=bt), max(3, reps // 4), flush)
+    res["prefill_c4"] = {"tokens": tq, "ours_us": round(ours * 1e6, 1), "reference_us": round(ref * 1e6, 1),
+                         "speedup": round(ref / ours, 3), "ours_tflops": round(flops / ours / 1e12, 1),
+                         "reference_tflops": round(flops / ref / 1e12, 1)}
+    return res
+
+
+def run_c1(args):
+    """BASELINE configs[0] as a single op: the KV store of one new token per sequence plus paged
+    decode attention, 8 sequences, contexts U[16, 1024], Qwen3-0.6B heads (16 Q / 8 KV, D 128),
+    64 blocks of 256, BF16, N(0, 1) values, scale 1/sqrt(128), new token at position L - 1.
+    value: ops/s with every input in HBM (store + decode per op, L2 flushed before each op: the
+    64 MB cache would otherwise stay in the 126 MB L2).  e2e: the same op through the C ABI with
+    the per-op inputs (q, new k/v, slot mapping, block tables, context lengths) in pinned host
+    memory, copied in, and the output copied back, inside the timed region."""
+    import torch
+
+    from hilda_vllm_b200 import kernels
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    b, hq, hk, d, nb, bs = 8, 16, 8, 128, 64, 256
+    g = torch.Generator().manual_seed(args.seed)
+    lens = torch.randint(16, 1025, (b,), generator=g)
+    perm = torch.randperm(nb, generator=g).tolist()
+    tables, off = [], 0
+    for n in lens.tolist():
+        k = -(-n // bs)
+        tables.append(perm[off:off + k] + [-1] * (4 - k))
+        off += k
+    kc = torch.randn(nb, bs, hk, d, generator=g).bfloat16().to(dev)
+    vc = torch.randn(nb, bs, hk, d, generator=g).bfloat16().to(dev)
+    host = {"q": torch.randn(b, hq, d, generator=g).bfloat16(), "k": torch.randn(b, hk, d, generator=g).bfloat16(),
+            "v": torch.randn(b, hk, d, generator=g).bfloat16(), "bt": torch.tensor(tables, dtype=torch.int32),
+            "ln": lens.to(torch.int32),
+            "slots": torch.tensor([t[(n - 1) // bs] * bs + (n - 1) % bs for t, n in zip(tables, lens.tolist())],
+                                  dtype=torch.int32)}
+    host = {k: v.pin_memory() for k, v in host.items()}
+    devt = {k: v.to(dev) for k, v in host.items()}
+    out = torch.empty(b, hq, d, dtype=torch.bfloat16, device=dev)
+    out_host = torch.empty_like(out, device="cpu").pin_memory()
+    ws = kernels.make_decode_workspace(b, hq, d, 4, bs, dev)
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)
+
+    def op():
+        kernels.store_kvcache(devt["k"], devt["v"], kc, vc, devt["slots"])
+        kernels.paged_decode(devt["q"], kc, vc, devt["bt"], devt["ln"], d ** -0.5, out=out, workspace=ws)
+
+    def op_e2e():
+        for k in host:
+            devt[k].copy_(host[k], non_blocking=True)
+        op()
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        op()
+        op_e2e()
+    sampler = ClockSampler(0)
+    sampler.start()
+    t_dev = _time_flushed(op, args.steps, flush)
+    t_e2e = _time_flushed(op_e2e, args.steps, flush)
+    t_dec = _time_flushed(lambda: kernels.paged_decode(devt["q"], kc, vc, devt["bt"], devt["ln"], d ** -0.5, out=out,
+                                                       workspace=ws), args.steps, flush)
+    clocks = sampler.stop()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    nbytes = int(lens.sum()) * hk * d * 2 * 2 + b * hq * d * 2 * 2
+    cpu = None
+    if not args.no_cpu:
+        cpu = c1_cpu_sample(args.seed)
+    line = {"metric": "config-1 single op (KV store + paged decode, 8 seqs): ops/s", "value": round(1 / t_dev, 1),
+            "unit": "ops/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_dev * 1e3, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) cache, q and new K/V)",
+            "config": {"workload": "c1: BASELINE configs[0], store + decode of 8 sequences, contexts U[16,1024], "
+                                   "16 Q / 8 KV heads, 64 blocks of 256",
+                       "l2": "flushed before every op (256 MB write): the 64 MB cache fits in L2"},
+            "roofline": {"bound": "hbm", "achieved": round(nbytes / t_dec / 1e9, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(nbytes / t_dec / 1e9 / hbm_peak, 4), "traffic": None,
+                         "kernel": "paged_decode_kernel<bf16,G=2,Hk=8>", "avg_launch_us": round(t_dec * 1e6, 2),
+                         "note": "8 sequences: 17 MB per launch, latency-bound (one wave of 32 CTAs)",
+                         "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "of fallback"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(1 / t_e2e, 1), "unit": "ops/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": out_host.numel() * 2, "us_per_op": round(t_e2e * 1e6, 2)},
+            "clocks": clocks, "gpu_launches": 2 * args.steps}
+    print(json.dumps(line), flush=True)
+
+
+def c1_cpu_sample(seed: int, reps: int = 20) -> dict:
+    """The config-1 op on the host cores through the CPU oracle (the reference's store scatter and
+    fp32 attention restatement), mean seconds per op over reps."""
+    import torch
+
+    from oracle import attention as oattn
+    from oracle import kv_store
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    b, hq, hk, d, nb, bs = 8, 16, 8, 128, 64, 256
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(16, 1025, (b,), generator=g)
+    perm = torch.randperm(nb, generator=g).tolist()
+    tables, off = [], 0
+    for n in lens.tolist():
+        k = -(-n // bs)
+        tables.append(perm[off:off + k] + [-1] * (4 - k))
+        off += k
+    kc = torch.randn(nb, bs, hk, d, generator=g).bfloat16()
+    vc = torch.randn(nb, bs, hk, d, generator=g).bfloat16()
+    q = torch.randn(b, hq, d, generator=g).bfloat16()
+    kn = torch.randn(b, hk, d, generator=g).bfloat16()
+    vn = torch.randn(b, hk, d, generator=g).bfloat16()
+    bt = torch.tensor(tables, dtype=torch.int32)
+    slots = torch.tensor([t[(n - 1) // bs] * bs + (n - 1) % bs for t, n in zip(tables, lens.tolist())],
+                         dtype=torch.int32)
+    kv_store.store_kvcache(kn, vn, kc, vc, slots)
+    oattn.paged_decode(q, kc, vc, bt, lens, d ** -0.5)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        kv_store.store_kvcache(kn, vn, kc, vc, slots)
+        oattn.paged_decode(q, kc, vc, bt, lens, d ** -0.5)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(1 / dt, 2), "unit": "ops/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{reps} ops of the config-1 store + decode through the CPU oracle (fp32 attention), "
+                      f"{dt * 1e3:.2f} ms per op"}
+
+
 def run_profile(args):
     """Short, self-contained cases for ncu (one GPU)."""
     import torch
@@ -560,6 +859,9 @@ def run_profile(args):
 
     if args.profile == "allreduce":
         allreduce_profile(args)
+        return
+    if args.profile == "reference-kernels":
+        print(json.dumps({"profile": "reference-kernels", **reference_kernel_ab(args.seed, max(args.steps, 5))}))
         return
     torch.cuda.set_device(0)
     g = torch.Generator().manual_seed(args.seed)
@@ -804,6 +1106,12 @@ def main():
     args = parse()
     if args.profile:
         run_profile(args)
+        return
+    if args.workload == "c1":
+        if args.impl == "reference":
+            run_c1_reference(args)
+        else:
+            run_c1(args)
         return
     if args.workload != "c2" and args.impl == "ours":
         run_workload(args)

@@ -113,6 +113,13 @@ class BlockManager:
                 self.hash_to_block_id[prev_hash] = block.block_id
             seq.block_table.append(block.block_id)
 
+    def allocate_uncached(self, seq: Sequence) -> None:
+        """Fresh blocks for every page of `seq`, outside the prefix cache (no lookup, no hash
+        registered): for one-off scoring passes that must neither reuse nor publish rows."""
+        assert not seq.block_table
+        for _ in range(seq.num_blocks):
+            seq.block_table.append(self._allocate_block(self.free_block_ids[0]).block_id)
+
     def deallocate(self, seq: Sequence) -> None:
         for block_id in reversed(seq.block_table):
             block = self.blocks[block_id]

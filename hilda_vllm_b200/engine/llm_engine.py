@@ -211,6 +211,44 @@ class LLMEngine:
             pbar.close()
         return [{"text": self.tokenizer.decode(outputs[seq.seq_id]), "token_ids": outputs[seq.seq_id]} for seq in seqs]
 
+    # ------------------------------------------------------------------ scoring
+    def score_next_tokens(self, token_lists: list[list[int]], targets: list[int]) -> list[dict]:
+        """For each token list, the model's next-token logits after its last token, summarised:
+        the greedy choice (argmax, lowest id among equal maxima), the top logit and the logit of
+        the given target token.  Prefill-only passes on fresh blocks (no prefix-cache reuse) run
+        while the engine has no requests of its own; lists are packed into batches of at most
+        max_num_batched_tokens tokens.  This is a teacher-forced check of generated tokens: feed a
+        prompt plus the first s generated tokens and ask whether token s is the model's choice."""
+        from hilda_vllm_b200.engine.scheduler import ScheduledSequence
+
+        assert self.scheduler.is_finished() and self._inflight is None, "score_next_tokens needs an idle engine"
+        assert len(token_lists) == len(targets)
+        bm = self.scheduler.block_manager
+        budget = self.config.max_num_batched_tokens
+        out: list[dict] = []
+        i = 0
+        while i < len(token_lists):
+            batch = []
+            used = 0
+            while i < len(token_lists) and len(batch) < self.config.max_num_seqs:
+                seq = Sequence(list(token_lists[i]), SamplingParams(greedy=True, max_tokens=1))
+                if used + len(seq) > budget or len(bm.free_block_ids) < seq.num_blocks:
+                    break
+                bm.allocate_uncached(seq)
+                batch.append(ScheduledSequence(seq, len(seq)))
+                used += len(seq)
+                i += 1
+            if not batch:
+                raise RuntimeError(f"score_next_tokens: list {i} ({len(token_lists[i])} tokens) does not fit the "
+                                   f"batch budget ({budget}) or the KV pool")
+            try:
+                res = self.model_runner.score(batch, targets[i - len(batch):i])
+            finally:
+                for sched in batch:
+                    bm.deallocate(sched.seq)
+            out.extend(res)
+        return out
+
     # ------------------------------------------------------------------ statistics
     @staticmethod
     def _init_generate_stats(seqs):

@@ -672,6 +672,29 @@ class ModelRunner:
         reset_context()
         return token_ids
 
+    def score(self, scheduled_seqs: list[ScheduledSequence], targets: list[int]) -> list[dict]:
+        """One prefill pass over whole sequences; per sequence the greedy token, the top logit and
+        the target token's logit at the last position (LLMEngine.score_next_tokens)."""
+        meta = prefill_metadata(scheduled_seqs, self.block_size)
+        return self.call("execute_score", meta, list(targets))
+
+    @torch.inference_mode()
+    def execute_score(self, meta: dict, targets: list[int]):
+        input_ids, positions = self._upload_prefill(meta)
+        hidden = self.model(input_ids, positions)
+        logits = self._gather_logits(self.model.lm_head.local_logits(hidden))
+        res = None
+        if self.rank == 0:
+            logits = logits.float()
+            top, arg = logits.max(-1)
+            tgt = logits.gather(1, torch.tensor(targets, dtype=torch.int64, device=logits.device).view(-1, 1))
+            self._queue_error_words(0)
+            res = [{"argmax": int(a), "top_logit": float(t), "target_logit": float(x)}
+                   for a, t, x in zip(kernels.argmax(logits.bfloat16()).tolist(), top.tolist(), tgt.view(-1).tolist())]
+            self._check_error_words(0)
+        reset_context()
+        return res
+
     @torch.inference_mode()
     def execute_decode(self, packet: np.ndarray, bs: int, graph_bs: int, real: list[int], samp, temps=None):
         self._upload_temps(temps, 0)

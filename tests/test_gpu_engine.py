@@ -261,3 +261,35 @@ def test_block_outside_the_pool_makes_generate_raise(tmp_path, golden_dir):
                          use_tqdm=False)
     finally:
         llm.exit()
+
+
+def test_score_next_tokens_confirms_greedy_decode(tmp_path, golden_dir):
+    """LLM.score_next_tokens (prefill passes on fresh blocks) re-derives each greedy decode token
+    teacher-forced: prompt + the first s generated tokens must score token s as its argmax (or a
+    bf16 tie), and the engine accepts new requests afterwards."""
+    import math
+
+    d = tiny_dir(tmp_path, golden_dir)
+    g = torch.Generator().manual_seed(8)
+    prompts = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (5, 77, 300)]
+    llm = LLM(str(d), load_format="random", seed=7, max_num_seqs=8, max_model_len=1024, max_num_batched_tokens=2048,
+              kvcache_block_cap=32, gpu_memory_utilization=0.3)
+    outs = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(greedy=True, max_tokens=12, ignore_eos=True),
+                                                 use_tqdm=False)]
+    lists = [p + c[:k] for p, c in zip(prompts, outs) for k in range(12)]
+    targets = [c[k] for c in outs for k in range(12)]
+    free_before = len(llm.scheduler.block_manager.free_block_ids)
+    res = llm.score_next_tokens(lists, targets)
+    assert len(llm.scheduler.block_manager.free_block_ids) == free_before  # blocks returned
+    exact = 0
+    for r, t in zip(res, targets):
+        if r["argmax"] == t:
+            exact += 1
+            assert r["target_logit"] == r["top_logit"]
+        else:
+            top = r["top_logit"]
+            assert top - r["target_logit"] <= 2 * 2.0 ** (math.floor(math.log2(abs(top))) - 7)
+    assert exact >= 0.9 * len(targets)
+    again = llm.generate(prompts[:1], SamplingParams(greedy=True, max_tokens=12, ignore_eos=True), use_tqdm=False)
+    llm.exit()
+    assert again[0]["token_ids"] == outs[0]
