@@ -643,7 +643,9 @@ def _paged_case(g, lens, hq, hk, dev, bs=256, fp8=False):
 
 def _time_flushed(fn, reps, flush):
     """Mean seconds of fn() over reps launches, each timed alone with CUDA events on the current
-    stream after a write of `flush` (larger than L2) so no launch finds the previous one's data in L2."""
+    stream right after a read-modify-write of `flush` (larger than L2), so no launch finds the
+    previous one's data in L2.  The flush keeps the GPU busy while the host enqueues the start
+    event and fn's launches, so the events time GPU work, not the host's launch latency."""
     import torch
 
     stream = torch.cuda.current_stream()
@@ -651,9 +653,8 @@ def _time_flushed(fn, reps, flush):
     torch.cuda.synchronize()
     total = 0.0
     for _ in range(reps):
-        flush.add_(1)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
+        flush.add_(1)
         e0.record(stream)
         fn()
         e1.record(stream)
@@ -681,9 +682,9 @@ def reference_kernel_ab(seed: int = 0, reps: int = 20) -> dict:
         return {"unavailable": f"flash-attn not importable: {type(exc).__name__}"}
     dev = torch.device("cuda", torch.cuda.current_device())
     g = torch.Generator().manual_seed(seed)
-    flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)  # 256 MB > 126 MB of L2
+    flush = torch.zeros(128 << 20, dtype=torch.float32, device=dev)  # 512 MB > 126 MB of L2
     scale = 128 ** -0.5
-    res = {"timing": "CUDA events per launch, L2 flushed (256 MB write) before each launch, mean of "
+    res = {"timing": "CUDA events per launch, L2 flushed (512 MB read-modify-write) before each launch, mean of "
                      f"{reps}", "reference": "flash-attn 2.x with the reference's call signatures"}
     decode_cases = {
         "decode_c1": ([int(x) for x in torch.randint(16, 1025, (8,), generator=g)], 16, 8),
@@ -764,7 +765,7 @@ def run_c1(args):
     out = torch.empty(b, hq, d, dtype=torch.bfloat16, device=dev)
     out_host = torch.empty_like(out, device="cpu").pin_memory()
     ws = kernels.make_decode_workspace(b, hq, d, 4, bs, dev)
-    flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)
+    flush = torch.zeros(128 << 20, dtype=torch.float32, device=dev)  # 512 MB > 126 MB of L2
 
     def op():
         kernels.store_kvcache(devt["k"], devt["v"], kc, vc, devt["slots"])
@@ -799,7 +800,7 @@ def run_c1(args):
             "dtype": "bf16", "data": "synthetic (seeded N(0,1) cache, q and new K/V)",
             "config": {"workload": "c1: BASELINE configs[0], store + decode of 8 sequences, contexts U[16,1024], "
                                    "16 Q / 8 KV heads, 64 blocks of 256",
-                       "l2": "flushed before every op (256 MB write): the 64 MB cache fits in L2"},
+                       "l2": "flushed before every op (512 MB read-modify-write): the 64 MB cache fits in L2"},
             "roofline": {"bound": "hbm", "achieved": round(nbytes / t_dec / 1e9, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(nbytes / t_dec / 1e9 / hbm_peak, 4), "traffic": None,
                          "kernel": "paged_decode_kernel<bf16,G=2,Hk=8>", "avg_launch_us": round(t_dec * 1e6, 2),
@@ -908,10 +909,24 @@ def run_profile(args):
         elem = 1 if fp8 else 2
         nbytes = int(lens.sum()) * hk * d * elem * 2 + b * hq * d * 4
         us = e0.elapsed_time(e1) * 1e3 / args.steps
-        print(json.dumps({"profile": args.profile, "workload": args.workload, "kv": "fp8" if fp8 else "bf16",
-                          "hq": hq, "hk": hk, "launches": args.steps, "bytes_per_launch": nbytes,
-                          "cache_gb": round(2 * kc.numel() * elem / 1e9, 2), "us_per_launch": round(us, 2),
-                          "gb_per_s": round(nbytes / us / 1e3, 1)}))
+        res = {"profile": args.profile, "workload": args.workload, "kv": "fp8" if fp8 else "bf16",
+               "hq": hq, "hk": hk, "launches": args.steps, "bytes_per_launch": nbytes,
+               "cache_gb": round(2 * kc.numel() * elem / 1e9, 2), "us_per_launch": round(us, 2),
+               "gb_per_s": round(nbytes / us / 1e3, 1)}
+        if not tc:
+            # The split-K grid kernel on the same inputs (outside the profiler range).
+            for _ in range(3):
+                kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws, split_grid=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(max(args.steps, 10)):
+                kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws, split_grid=True)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us2 = e0.elapsed_time(e1) * 1e3 / max(args.steps, 10)
+            res["split_grid_us_per_launch"] = round(us2, 2)
+            res["split_grid_gb_per_s"] = round(nbytes / us2 / 1e3, 1)
+        print(json.dumps(res))
         return
     if args.profile == "prefill-kernel":
         # BASELINE config-4 prefill shape: 8 sequences of 4096..8192 new tokens over a 2048-token

@@ -130,6 +130,8 @@ def replay_against_oracle(hf, seed, events, num_blocks, block_size=256, kv_fp8=F
         with torch.no_grad():
             logits = model.logits(model.forward(ids, pos, ctx), ctx)
         check(logits, [t for _, t in live], f"decode {n}")
+    del model
+    torch.cuda.empty_cache()  # the oracle's pool is as large as the engine's: give it back
     for t in ties:
         print(f"bf16 logit tie at {t[0]} row {t[1]}: engine token {t[2]:.3g} below the top logit")
     assert not bad, f"engine tokens that are not an oracle argmax (where, row, token, argmax, gap, ulp): {bad[:10]}"
@@ -143,6 +145,8 @@ def run_engine(model_dir, prompts, params, **kw):
     stats = dict(llm.last_generate_stats)
     num_blocks = llm.config.num_kvcache_blocks
     llm.exit()
+    del llm
+    torch.cuda.empty_cache()
     return outs, rec.events, stats, num_blocks
 
 
@@ -197,7 +201,7 @@ def test_c4_chunked_prefill_over_shared_prefixes_matches_oracle():
     params = [params[i] for i in order]
     outs, events, stats, nb = run_engine(CFG_06B, prompts, params, seed=0, max_num_seqs=16, max_model_len=4096,
                                          max_num_batched_tokens=4096, chunked_prefill_size=1024,
-                                         gpu_memory_utilization=0.5)
+                                         kvcache_block_cap=96, gpu_memory_utilization=0.5)
     assert [len(o["token_ids"]) for o in outs] == [p.max_tokens for p in params]
     prefix_chunks = sum(1 for kind, rows, _ in events if kind == "prefill" for r in rows if r["start"] > 0)
     assert prefix_chunks > 0, "no chunk started after position 0"
