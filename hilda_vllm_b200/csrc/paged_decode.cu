@@ -73,11 +73,15 @@ struct DecodeParams {
   uint8_t* ws;
 };
 
+template <bool FP8, int G>
+constexpr int ctas_per_sm() { return G <= 2 ? 3 : (G <= 4 ? 2 : 1); }
+
 template <bool FP8, int HK>
 struct Traits {
   static constexpr int kElem = FP8 ? 1 : 2;
+  static constexpr int kTileB = kTileBytes;  // bytes per K (and per V) stage
   static constexpr int kRowBytes = HK * kHeadDim * kElem;  // one token, all local KV heads
-  static constexpr int kT = kTileBytes / kRowBytes < kSplit ? kTileBytes / kRowBytes : kSplit;  // tokens per tile
+  static constexpr int kT = kTileB / kRowBytes < kSplit ? kTileB / kRowBytes : kSplit;  // tokens per tile
   static constexpr int kPhases = 8 / HK;                    // warps sharing one KV head
   static constexpr int kTPW = kT / kPhases;                 // tokens per warp per tile
   static constexpr int kTPH = kTPW / 2;                     // tokens per half-warp per tile
@@ -190,7 +194,7 @@ __device__ __forceinline__ void decode_tile(FullTag, const uint8_t* Ks, int tile
   constexpr int kTPW = Tr::kTPW;
   constexpr int kTPH = Tr::kTPH;
   constexpr int kRow = Tr::kRowBytes;
-  const uint8_t* Vs = Ks + kTileBytes;
+  const uint8_t* Vs = Ks + Tr::kTileB;
   // Partial q.k over this lane's 8 dimensions, packed fp32x2 FMAs; sc[j * kTPH + i].
   float sc[G * kTPH];
   bool valid[kTPH];
@@ -255,9 +259,10 @@ __device__ __forceinline__ void decode_tile(FullTag, const uint8_t* Ks, int tile
 }
 
 template <bool FP8, int G, int HK>
-__global__ void __launch_bounds__(kDecodeThreads, (G <= 2 ? 3 : (G <= 4 ? 2 : 1)))
+__global__ void __launch_bounds__(kDecodeThreads, ctas_per_sm<FP8, G>())
 paged_decode_kernel(const DecodeParams p) {
   using Tr = Traits<FP8, HK>;
+  constexpr int kTileBytes = Tr::kTileB;
   constexpr int kT = Tr::kT;
   constexpr int kRow = Tr::kRowBytes;
   constexpr int kHq = HK * G;
@@ -537,7 +542,12 @@ paged_decode_kernel(const DecodeParams p) {
 // a sequence cut by share boundaries is finished by the last of its CTAs to arrive (ticket),
 // which merges the partial (m, l, O) the others published, in CTA order (deterministic).
 // ------------------------------------------------------------------------------------------
-constexpr int kPersistMaxCtas = 448;  // >= SMs x CTAs per SM on B200 (148 x 3); sizes the workspace
+// The workspace holds two partial (m, l, O) slots of Hq heads per CTA; grid x Hq is capped at
+// kPersistHeadSlots = SMs x CTAs per SM x Hq of the widest case on B200 (148 x 4 x 16 covers GQA 2
+// with 8 KV heads at 3 CTAs per SM; GQA 4 and 8 run 2 and 1 CTAs per SM with 32 and 64 heads).
+constexpr int kPersistHeadSlots = 148 * 4 * 16;
+
+constexpr int kMinUnitsPerCta = 8;
 
 __host__ __device__ constexpr int64_t persist_part_floats(int hq) { return int64_t(hq) * (kHeadDim + 2); }
 
@@ -566,9 +576,10 @@ struct SeqCursor {
 };
 
 template <bool FP8, int G, int HK>
-__global__ void __launch_bounds__(kDecodeThreads, (G <= 2 ? 3 : (G <= 4 ? 2 : 1)))
+__global__ void __launch_bounds__(kDecodeThreads, ctas_per_sm<FP8, G>())
 paged_decode_persistent_kernel(const DecodeParams p) {
   using Tr = Traits<FP8, HK>;
+  constexpr int kTileBytes = Tr::kTileB;
   constexpr int kT = Tr::kT;
   constexpr int kRow = Tr::kRowBytes;
   constexpr int kHq = HK * G;
@@ -579,7 +590,8 @@ paged_decode_persistent_kernel(const DecodeParams p) {
   int* s_flag = s_bad + kStages;                        // merger election
   int64_t* s_range = reinterpret_cast<int64_t*>(s_flag + 4);  // start, end, units per CTA, first unit of b
   int* s_cur = reinterpret_cast<int*>(s_range + 4);           // b, t, L, tiles of the first unit
-  float* scr = reinterpret_cast<float*>(s_cur + 8);            // cross-phase merge area (HK < 8)
+  SeqCursor<kT>* s_pcur = reinterpret_cast<SeqCursor<kT>*>(s_cur + 8);  // the producer's cursor
+  float* scr = reinterpret_cast<float*>(s_pcur + 1);                     // cross-phase merge area (HK < 8)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -611,7 +623,10 @@ paged_decode_persistent_kernel(const DecodeParams p) {
       if (lane >= o) incl += v;
     }
     const int64_t total = __shfl_sync(0xffffffffu, incl, 31);
-    const int64_t upc = total > 0 ? (total + grid - 1) / grid : 1;
+    // Equal shares, but at least kMinUnitsPerCta tiles each: a small batch then runs on fewer
+    // CTAs instead of cutting every sequence into many parts that must be merged.
+    int64_t upc = total > 0 ? (total + grid - 1) / grid : 1;
+    upc = upc < kMinUnitsPerCta ? kMinUnitsPerCta : upc;
     const int64_t start = min(total, int64_t(cta) * upc);
     const int64_t end = min(total, start + upc);
     if (lane == 0) {
@@ -648,17 +663,15 @@ paged_decode_persistent_kernel(const DecodeParams p) {
     fence_mbar_init();
   }
   __syncthreads();
-  const int64_t start = s_range[0];
-  const int n_units = int(s_range[1] - start);
-  const int64_t upc = s_range[2];
+  const int n_units = int(s_range[1] - s_range[0]);
   if (n_units <= 0) return;
   SeqCursor<kT> cur{s_cur[0], s_cur[1], s_cur[2], s_cur[3], s_range[3]};
 
   // Producer (thread 0): issues unit i into stage i % kStages.  A tile whose block id is out of
   // range is not loaded: its stage is marked bad (the consumers skip it) and the barrier phase is
-  // completed by a plain arrive.
-  SeqCursor<kT> pcur = cur;
+  // completed by a plain arrive.  Its cursor lives in shared memory (only thread 0 touches it).
   auto issue = [&](int i) {
+    SeqCursor<kT> pcur = *s_pcur;
     const int st = i % kStages;
     const int tok0 = pcur.t * kT;
     const int64_t block = p.block_tables[int64_t(pcur.b) * p.bt_stride + tok0 / p.block_size];
@@ -674,26 +687,26 @@ paged_decode_persistent_kernel(const DecodeParams p) {
       bulk_g2s(smem + st * 2 * kTileBytes + kTileBytes, p.v_cache + slot * kRow, kT * kRow, &full[st]);
     }
     pcur.next(p);
+    *s_pcur = pcur;
   };
-  int issued = 0;
   if (tid == 0) {
-    for (; issued < kStages && issued < n_units; ++issued) issue(issued);
+    *s_pcur = cur;
+    for (int i = 0; i < kStages && i < n_units; ++i) issue(i);
   }
 
   const float ks_h = (FP8 && p.k_scale) ? p.k_scale[h] : 1.0f;
   const float qf = p.scale_log2 * ks_h;
   const float vs = (FP8 && p.v_scale) ? p.v_scale[h] : 1.0f;
-  float2 qs[G][4];
-  float m[G], l[G];
-  float2 acc[G][4];
-  int seg_b = -1;
   bool timed_out = false;
 
-  for (int i = 0; i < n_units; ++i) {
-    const int stage = i % kStages;
-    if (cur.b != seg_b) {
-      // A new segment: this sequence's queries (pre-scaled for the base-2 softmax) and a fresh state.
-      seg_b = cur.b;
+  // One pass of the outer loop per segment (the part of one sequence in this share), so the query
+  // registers of a segment are dead once its tiles are done.
+  for (int i = 0; i < n_units;) {
+    float m[G], l[G];
+    float2 acc[G][4];
+    {
+      // This sequence's queries, pre-scaled for the base-2 softmax, and a fresh softmax state.
+      float2 qs[G][4];
       const __nv_bfloat16* qb = p.q + int64_t(cur.b) * p.q_row_stride;
 #pragma unroll
       for (int j = 0; j < G; ++j) {
@@ -707,25 +720,30 @@ paged_decode_persistent_kernel(const DecodeParams p) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[j][c] = make_float2(0.f, 0.f);
       }
+      const int seg_end = min(n_units, i + (cur.tiles - cur.t));
+      for (; i < seg_end; ++i, ++cur.t) {
+        const int stage = i % kStages;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], (i / kStages) & 1));
+        if (ok && !s_bad[stage]) {
+          const uint8_t* Ks = smem + stage * 2 * kTileBytes;
+          const int tile_tok0 = cur.t * kT;
+          if (tile_tok0 + kT <= cur.L)
+            decode_tile<FP8, G, HK>(BoolTag<true>{}, Ks, tile_tok0, cur.L, phase, hw, ln, h, qs, m, l, acc);
+          else
+            decode_tile<FP8, G, HK>(BoolTag<false>{}, Ks, tile_tok0, cur.L, phase, hw, ln, h, qs, m, l, acc);
+        }
+        // Every warp is done with this stage: refill it (or leave together on a timeout).
+        if (__syncthreads_or(!ok)) {
+          timed_out = true;
+          break;
+        }
+        if (tid == 0 && i + kStages < n_units) issue(i + kStages);
+      }
     }
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], (i / kStages) & 1));
-    if (ok && !s_bad[stage]) {
-      const uint8_t* Ks = smem + stage * 2 * kTileBytes;
-      const int tile_tok0 = cur.t * kT;
-      if (tile_tok0 + kT <= cur.L)
-        decode_tile<FP8, G, HK>(BoolTag<true>{}, Ks, tile_tok0, cur.L, phase, hw, ln, h, qs, m, l, acc);
-      else
-        decode_tile<FP8, G, HK>(BoolTag<false>{}, Ks, tile_tok0, cur.L, phase, hw, ln, h, qs, m, l, acc);
-    }
-    // Every warp is done with this stage: refill it (or leave together on a timeout).
-    if (__syncthreads_or(!ok)) {
-      timed_out = true;
-      break;
-    }
-    if (tid == 0 && issued < n_units) issue(issued++);
-
+    if (timed_out) break;
+    --cur.t;  // back to the segment's last tile
     const bool seq_end = cur.t == cur.tiles - 1;
-    if (seq_end || i == n_units - 1) {
+    {
       // ---------------------------------------------------------------- segment epilogue
       {  // the two half-warps hold disjoint tokens of the same D-slice
         float m2[G], l2[G];
@@ -774,6 +792,7 @@ paged_decode_persistent_kernel(const DecodeParams p) {
         }
       }
       __nv_bfloat16* out_b = p.out + int64_t(cur.b) * p.out_row_stride;
+      const int64_t start = s_range[0], upc = s_range[2];
       const int64_t pf = cur.first, pl = cur.first + cur.tiles - 1;
       const bool whole = pf >= start && seq_end;
       if (whole) {
@@ -817,33 +836,51 @@ paged_decode_persistent_kernel(const DecodeParams p) {
         __syncthreads();
         if (*s_flag) {
           __threadfence();
+          // One pass over the parts, four at a time: their loads are independent, so a part costs
+          // one L2 round trip per group of four instead of two dependent ones each.
           for (int idx = tid; idx < kHq * (kHeadDim / 8); idx += kDecodeThreads) {
             const int hq = idx / (kHeadDim / 8);
             const int d0 = (idx % (kHeadDim / 8)) * 8;
-            float mx = -INFINITY;
-            for (int cc = c_first; cc <= c_last; ++cc) {
-              const float* q = parts + (int64_t(cc) * 2 + (pf < int64_t(cc) * upc ? 0 : 1)) * persist_part_floats(kHq);
-              mx = fmaxf(mx, __ldcg(q + hq));
-            }
-            float lsum = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            if (mx != -INFINITY) {
-              for (int cc = c_first; cc <= c_last; ++cc) {
-                const float* q = parts + (int64_t(cc) * 2 + (pf < int64_t(cc) * upc ? 0 : 1)) * persist_part_floats(kHq);
-                const float mc = __ldcg(q + hq);
-                if (mc == -INFINITY) continue;
-                const float c = exp2f(mc - mx);
-                lsum += __ldcg(q + kHq + hq) * c;
-                const float4* src = reinterpret_cast<const float4*>(q + 2 * kHq + hq * kHeadDim + d0);
-                const float4 a = __ldcg(src), bq = __ldcg(src + 1);
-                o[0] += a.x * c;
-                o[1] += a.y * c;
-                o[2] += a.z * c;
-                o[3] += a.w * c;
-                o[4] += bq.x * c;
-                o[5] += bq.y * c;
-                o[6] += bq.z * c;
-                o[7] += bq.w * c;
+            float mx = -INFINITY, lsum = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int c0 = c_first; c0 <= c_last; c0 += 4) {
+              float mc[4], lc[4];
+              float4 oa[4], ob[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                mc[k] = -INFINITY;
+                lc[k] = 0.f;
+                oa[k] = ob[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                const int cc = c0 + k;
+                if (cc <= c_last) {
+                  const float* q = parts + (int64_t(cc) * 2 + (pf < int64_t(cc) * upc ? 0 : 1)) *
+                                               persist_part_floats(kHq);
+                  mc[k] = __ldcg(q + hq);
+                  lc[k] = __ldcg(q + kHq + hq);
+                  const float4* src = reinterpret_cast<const float4*>(q + 2 * kHq + hq * kHeadDim + d0);
+                  oa[k] = __ldcg(src);
+                  ob[k] = __ldcg(src + 1);
+                }
               }
+              const float mn = fmaxf(fmaxf(mx, fmaxf(mc[0], mc[1])), fmaxf(mc[2], mc[3]));
+              if (mn == -INFINITY) continue;  // nothing but empty parts so far
+              const float f = exp2f(mx - mn);
+              lsum *= f;
+#pragma unroll
+              for (int d = 0; d < 8; ++d) o[d] *= f;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float c = exp2f(mc[k] - mn);  // 0 for an empty part (m = -inf)
+                lsum += lc[k] * c;
+                o[0] += oa[k].x * c;
+                o[1] += oa[k].y * c;
+                o[2] += oa[k].z * c;
+                o[3] += oa[k].w * c;
+                o[4] += ob[k].x * c;
+                o[5] += ob[k].y * c;
+                o[6] += ob[k].z * c;
+                o[7] += ob[k].w * c;
+              }
+              mx = mn;
             }
             const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
 #pragma unroll
@@ -867,14 +904,15 @@ paged_decode_persistent_kernel(const DecodeParams p) {
 
 template <bool FP8, int G, int HK>
 constexpr size_t persist_smem_bytes() {
-  return size_t(kStages) * 2 * kTileBytes + kStages * sizeof(uint64_t) + (kStages + 4) * sizeof(int) +
-         4 * sizeof(int64_t) + 8 * sizeof(int) + (Traits<FP8, HK>::kPhases > 1 ? size_t(8) * G * 16 * 10 * 4 : 0);
+  return size_t(kStages) * 2 * Traits<FP8, HK>::kTileB + kStages * sizeof(uint64_t) + (kStages + 4) * sizeof(int) +
+         4 * sizeof(int64_t) + 8 * sizeof(int) + sizeof(SeqCursor<Traits<FP8, HK>::kT>) +
+         (Traits<FP8, HK>::kPhases > 1 ? size_t(8) * G * 16 * 10 * 4 : 0);
 }
 
 template <bool FP8, int G, int HK>
 int launch_decode_persistent(const DecodeParams& p, cudaStream_t stream) {
   constexpr size_t smem = persist_smem_bytes<FP8, G, HK>();
-  constexpr int kPerSm = G <= 2 ? 3 : (G <= 4 ? 2 : 1);
+  constexpr int kPerSm = ctas_per_sm<FP8, G>();
   // Per device: the shared-memory opt-in and the grid (SMs x CTAs per SM).  The first call on a
   // device happens before any graph capture (the engine's eager warm-up).
   static std::atomic<int> grid_of[kMaxDecodeDevices];
@@ -894,7 +932,8 @@ int launch_decode_persistent(const DecodeParams& p, cudaStream_t stream) {
       set_error("hl_paged_decode: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
       return HL_ERR_CUDA;
     }
-    grid = sms * kPerSm < kPersistMaxCtas ? sms * kPerSm : kPersistMaxCtas;
+    constexpr int kMaxGrid = kPersistHeadSlots / (HK * G);
+    grid = sms * kPerSm < kMaxGrid ? sms * kPerSm : kMaxGrid;
     grid_of[dev].store(grid, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
@@ -917,7 +956,7 @@ int launch_decode_persistent(const DecodeParams& p, cudaStream_t stream) {
 
 template <bool FP8, int G, int HK>
 int launch_decode(const DecodeParams& p, cudaStream_t stream) {
-  constexpr size_t smem = size_t(kStages) * 2 * kTileBytes + kStages * sizeof(uint64_t) + 16;
+  constexpr size_t smem = size_t(kStages) * 2 * Traits<FP8, HK>::kTileB + kStages * sizeof(uint64_t) + 16;
   // The shared-memory opt-in is per device; the first call on a device happens before any graph
   // capture (the engine's eager warm-up).
   static std::atomic<bool> configured[kMaxDecodeDevices];
@@ -1005,7 +1044,7 @@ extern "C" int64_t hl_paged_decode_workspace_size(int batch, int num_q_heads, in
   const int64_t S = max_splits_for(max_blocks_per_seq, block_size);
   const int64_t rows = int64_t(batch) * S * num_q_heads;
   const int64_t simt = kWsMlOff + align256(rows * int64_t(sizeof(float2))) + rows * head_dim * int64_t(sizeof(float));
-  const int64_t persist = kWsMlOff + int64_t(kPersistMaxCtas) * 2 * persist_part_floats(num_q_heads) * 4;
+  const int64_t persist = kWsMlOff + int64_t(2) * kPersistHeadSlots * (kHeadDim + 2) * 4;
   const int64_t tc = decode_tc_workspace_bytes(batch, num_q_heads);
   const int64_t cc = simt > persist ? simt : persist;
   return cc > tc ? cc : tc;
