@@ -312,7 +312,7 @@ def run_ours(args):
                 "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "of fallback (6650 GB/s)",
                 "samples": len(samples), "avg_launch_us": round(1e6 * ktime / max(1, len(samples)), 2),
                 "bytes_per_launch_avg": int(kbytes / max(1, len(samples))),
-                "split_grid_kernel": {"avg_launch_us": round(1e6 * ktime_split / max(1, len(samples)), 2),
+                "persistent_kernel": {"avg_launch_us": round(1e6 * ktime_split / max(1, len(samples)), 2),
                                       "frac": round(kbytes / ktime_split / 1e9 / hbm_peak, 4)}}
 
     # ---- the reference's own attention kernels (flash-attn) beside ours, same inputs, this GPU ----
@@ -917,18 +917,18 @@ def run_profile(args):
                "cache_gb": round(2 * kc.numel() * elem / 1e9, 2), "us_per_launch": round(us, 2),
                "gb_per_s": round(nbytes / us / 1e3, 1)}
         if not tc:
-            # The split-K grid kernel on the same inputs (outside the profiler range).
+            # The persistent kernel on the same inputs (outside the profiler range).
             for _ in range(3):
-                kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws, split_grid=True)
+                kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws, persistent=True)
             torch.cuda.synchronize()
             e0.record(stream)
             for _ in range(max(args.steps, 10)):
-                kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws, split_grid=True)
+                kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws, persistent=True)
             e1.record(stream)
             torch.cuda.synchronize()
             us2 = e0.elapsed_time(e1) * 1e3 / max(args.steps, 10)
-            res["split_grid_us_per_launch"] = round(us2, 2)
-            res["split_grid_gb_per_s"] = round(nbytes / us2 / 1e3, 1)
+            res["persistent_us_per_launch"] = round(us2, 2)
+            res["persistent_gb_per_s"] = round(nbytes / us2 / 1e3, 1)
             # More shapes, both kernels, each launch timed alone after an L2 flush.
             flush = torch.zeros(128 << 20, dtype=torch.float32, device=dev)
             extra = {"uniform_576x256": [576] * NUM_SEQS, "c1_8seqs": [int(x) for x in torch.randint(16, 1025, (8,), generator=g)],
@@ -940,7 +940,7 @@ def run_profile(args):
                 row = {}
                 for variant, split in (("persistent", False), ("split_grid", True)):
                     t = _time_flushed(lambda: kernels.paged_decode(q2, kc2, vc2, bt2, ln2, d ** -0.5, out=o2, workspace=ws2,
-                                                                   split_grid=split), 10, flush)
+                                                                   persistent=not split), 10, flush)
                     nb2 = sum(lens2) * hk * d * elem * 2 + len(lens2) * hq * d * 4
                     row[variant] = {"us": round(t * 1e6, 2), "gb_per_s": round(nb2 / t / 1e9, 1)}
                 res[name] = row

@@ -78,7 +78,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_int, c_int, c_int, c_int, c_i64, c_f32, c_vp, c_i64, c_vp, c_i64, c_vp,
         ],
     ),
-    "hl_paged_decode_splitk": (
+    "hl_paged_decode_persistent": (
         c_int,
         [
             c_vp, c_i64, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_i64, c_int, c_vp, c_int,

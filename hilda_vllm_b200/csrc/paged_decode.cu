@@ -1083,7 +1083,7 @@ extern "C" int hl_paged_decode_tc(const void* q, int64_t q_row_stride, const voi
                            stream);
 }
 
-extern "C" int hl_paged_decode_splitk(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+extern "C" int hl_paged_decode_persistent(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
                                       int kv_dtype, const float* k_scale, const float* v_scale,
                                       const int32_t* block_tables, int64_t bt_stride, int max_blocks_per_seq,
                                       const int32_t* context_lens, int batch, int num_q_heads, int num_kv_heads,
@@ -1172,7 +1172,7 @@ int paged_decode_impl(int mode, const void* q, int64_t q_row_stride, const void*
                             max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, block_size,
                             num_blocks, p.scale_log2, out, out_row_stride, workspace, s);
   }
-  const bool split = mode == 2;
+  const bool split = mode != 2;  // mode 2: the persistent kernel (comparison entry point)
   if (fp8) return dispatch_g<true>(g, num_kv_heads, split, p, s);
   return dispatch_g<false>(g, num_kv_heads, split, p, s);
 }

@@ -841,11 +841,11 @@ class ModelRunner:
         v_cache = layer.decode_v_cache if self.use_fp8_kv_cache else layer.v_cache
         elem = 1 if self.use_fp8_kv_cache else 2
 
-        def timed(split_grid: bool) -> float:
+        def timed(persistent: bool) -> float:
             def launch():
                 kernels.paged_decode(q, k_cache, v_cache, bt, ctx, layer.scale, out=out,
                                      workspace=self.decode_workspace, k_scale=layer.k_scale, v_scale=layer.v_scale,
-                                     split_grid=split_grid)
+                                     persistent=persistent)
 
             for _ in range(3):
                 launch()
@@ -863,7 +863,7 @@ class ModelRunner:
             return e0.elapsed_time(e1) / 1e3 / reps
 
         t = timed(False)
-        t_split = timed(True)  # the split-K grid kernel on the same live cache, for comparison
+        t_split = timed(True)  # the persistent kernel on the same live cache, for comparison
         lens = ctx.tolist()
         nbytes = sum(lens) * hk * d * elem * 2 + bs * hq * d * 2 * 2
         return nbytes, t, t_split

@@ -157,9 +157,10 @@ def test_decode_gqa_layouts_and_edge_lengths(hq, hk):
 
 
 @pytest.mark.parametrize("hq,hk,fp8", [(16, 8, False), (8, 1, False), (16, 8, True), (8, 8, False)])
-def test_decode_split_grid_kernel_against_oracle(hq, hk, fp8):
-    """The split-K grid kernel (hl_paged_decode_splitk, kept for comparison with the default
-    persistent kernel) against the oracle, on edge lengths, twice in a row on one workspace."""
+def test_decode_persistent_kernel_against_oracle(hq, hk, fp8):
+    """The persistent CUDA-core kernel (hl_paged_decode_persistent, kept for comparison with the
+    default split-K grid kernel) against the oracle, on edge lengths, twice in a row on one
+    workspace."""
     g = torch.Generator().manual_seed(50 + hq + hk)
     k, v, bt, ln = make_paged(g, len(EDGE_LENS), hk, 128, sum(-(-n // 256) for n in EDGE_LENS) + 2, 256, EDGE_LENS)
     q = torch.randn(len(EDGE_LENS), hq, 128, generator=g).bfloat16()
@@ -174,8 +175,8 @@ def test_decode_split_grid_kernel_against_oracle(hq, hk, fp8):
     for _ in range(2):
         out = kernels.paged_decode(q.to(DEV), kd, vd, bt.to(DEV), ln.to(DEV), 128 ** -0.5, workspace=ws,
                                    k_scale=None if ks is None else ks.to(DEV),
-                                   v_scale=None if vs is None else vs.to(DEV), split_grid=True)
-        assert_close(out, want, **(dict(rtol=2e-2, atol=6e-2) if fp8 else BF16_TOL), what="split-K grid kernel")
+                                   v_scale=None if vs is None else vs.to(DEV), persistent=True)
+        assert_close(out, want, **(dict(rtol=2e-2, atol=6e-2) if fp8 else BF16_TOL), what="persistent kernel")
     assert kernels.decode_errors(ws) == 0
 
 
