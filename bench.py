@@ -285,9 +285,8 @@ def run_ours(args):
 
     # ---- decode-kernel roofline leg: the kernel alone on the live cache across a sweep ----
     _, samples = device_sweep(probe_every=64)
-    kbytes = sum(b for b, _, _ in samples)
-    ktime = sum(t for _, t, _ in samples)
-    ktime_split = sum(t for _, _, t in samples)
+    kbytes = sum(b for b, _ in samples)
+    ktime = sum(t for _, t in samples)
     peaks = {}
     peak_path = ROOT / "MEASURED_PEAKS.json"
     if peak_path.exists():
@@ -311,9 +310,7 @@ def run_ours(args):
                 "kernel": f"paged_decode_kernel<bf16,G={g_ratio},Hk={hk}>",
                 "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "of fallback (6650 GB/s)",
                 "samples": len(samples), "avg_launch_us": round(1e6 * ktime / max(1, len(samples)), 2),
-                "bytes_per_launch_avg": int(kbytes / max(1, len(samples))),
-                "persistent_kernel": {"avg_launch_us": round(1e6 * ktime_split / max(1, len(samples)), 2),
-                                      "frac": round(kbytes / ktime_split / 1e9 / hbm_peak, 4)}}
+                "bytes_per_launch_avg": int(kbytes / max(1, len(samples)))}
 
     # ---- the reference's own attention kernels (flash-attn) beside ours, same inputs, this GPU ----
     ref_kernels = reference_kernel_ab(args.seed, reps=10) if world == 1 else None
@@ -916,35 +913,6 @@ def run_profile(args):
                "hq": hq, "hk": hk, "launches": args.steps, "bytes_per_launch": nbytes,
                "cache_gb": round(2 * kc.numel() * elem / 1e9, 2), "us_per_launch": round(us, 2),
                "gb_per_s": round(nbytes / us / 1e3, 1)}
-        if not tc:
-            # The persistent kernel on the same inputs (outside the profiler range).
-            for _ in range(3):
-                kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws, persistent=True)
-            torch.cuda.synchronize()
-            e0.record(stream)
-            for _ in range(max(args.steps, 10)):
-                kernels.paged_decode(q, kc, vc, bt, ln, d ** -0.5, out=out, workspace=ws, persistent=True)
-            e1.record(stream)
-            torch.cuda.synchronize()
-            us2 = e0.elapsed_time(e1) * 1e3 / max(args.steps, 10)
-            res["persistent_us_per_launch"] = round(us2, 2)
-            res["persistent_gb_per_s"] = round(nbytes / us2 / 1e3, 1)
-            # More shapes, both kernels, each launch timed alone after an L2 flush.
-            flush = torch.zeros(128 << 20, dtype=torch.float32, device=dev)
-            extra = {"uniform_576x256": [576] * NUM_SEQS, "c1_8seqs": [int(x) for x in torch.randint(16, 1025, (8,), generator=g)],
-                     "uniform_4096x64": [4096] * 64}
-            for name, lens2 in extra.items():
-                q2, kc2, vc2, bt2, ln2 = _paged_case(g, lens2, hq, hk, dev, fp8=fp8)
-                ws2 = kernels.make_decode_workspace(len(lens2), hq, d, bt2.shape[1], bs, dev)
-                o2 = torch.empty_like(q2)
-                row = {}
-                for variant, split in (("persistent", False), ("split_grid", True)):
-                    t = _time_flushed(lambda: kernels.paged_decode(q2, kc2, vc2, bt2, ln2, d ** -0.5, out=o2, workspace=ws2,
-                                                                   persistent=not split), 10, flush)
-                    nb2 = sum(lens2) * hk * d * elem * 2 + len(lens2) * hq * d * 4
-                    row[variant] = {"us": round(t * 1e6, 2), "gb_per_s": round(nb2 / t / 1e9, 1)}
-                res[name] = row
-                del q2, kc2, vc2, bt2, ln2, ws2, o2
         print(json.dumps(res))
         return
     if args.profile == "prefill-kernel":

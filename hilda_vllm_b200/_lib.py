@@ -78,13 +78,6 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_int, c_int, c_int, c_int, c_i64, c_f32, c_vp, c_i64, c_vp, c_i64, c_vp,
         ],
     ),
-    "hl_paged_decode_persistent": (
-        c_int,
-        [
-            c_vp, c_i64, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_i64, c_int, c_vp, c_int,
-            c_int, c_int, c_int, c_int, c_i64, c_f32, c_vp, c_i64, c_vp, c_i64, c_vp,
-        ],
-    ),
     "hl_paged_decode_noalloc": (
         c_int,
         [

@@ -530,430 +530,6 @@ paged_decode_kernel(const DecodeParams p) {
   if (tid == 0) tickets[b] = 0;  // ready for the next launch
 }
 
-// ------------------------------------------------------------------------------------------
-// Persistent variant: a fixed grid (CTAs per SM x SMs) walks the batch's tiles as one list.
-//
-// A unit is one kT-token tile of one sequence with all local KV heads (the same tile the
-// split kernel stages).  The units of the batch, sequence after sequence, are cut into equal
-// contiguous shares, one per CTA, so every CTA moves the same number of bytes whatever the mix
-// of context lengths, and its copy engine streams tiles back to back across sequence
-// boundaries (no CTA launch, set-up or pipeline refill between splits).  A share covers
-// segments of sequences: a segment that is a whole sequence is normalised and stored directly;
-// a sequence cut by share boundaries is finished by the last of its CTAs to arrive (ticket),
-// which merges the partial (m, l, O) the others published, in CTA order (deterministic).
-// ------------------------------------------------------------------------------------------
-// The workspace holds two partial (m, l, O) slots of Hq heads per CTA; grid x Hq is capped at
-// kPersistHeadSlots = SMs x CTAs per SM x Hq of the widest case on B200 (148 x 4 x 16 covers GQA 2
-// with 8 KV heads at 3 CTAs per SM; GQA 4 and 8 run 2 and 1 CTAs per SM with 32 and 64 heads).
-constexpr int kPersistHeadSlots = 148 * 4 * 16;
-
-constexpr int kMinUnitsPerCta = 8;
-
-__host__ __device__ constexpr int64_t persist_part_floats(int hq) { return int64_t(hq) * (kHeadDim + 2); }
-
-__device__ __forceinline__ int clamp_len(const DecodeParams& p, int b) {
-  int L = p.context_lens[b];
-  const int lmax = p.max_blocks * p.block_size;
-  return L < 0 ? 0 : (L > lmax ? lmax : L);
-}
-
-template <int KT>
-struct SeqCursor {
-  int b, t, L, tiles;
-  int64_t first;  // global index of the sequence's first unit
-  __device__ __forceinline__ void next(const DecodeParams& p) {
-    if (++t < tiles) return;
-    first += tiles;
-    t = 0;
-    for (++b; b < p.batch; ++b) {
-      L = clamp_len(p, b);
-      tiles = (L + KT - 1) / KT;
-      if (tiles > 0) return;
-    }
-    L = 0;
-    tiles = 1;
-  }
-};
-
-template <bool FP8, int G, int HK>
-__global__ void __launch_bounds__(kDecodeThreads, ctas_per_sm<FP8, G>())
-paged_decode_persistent_kernel(const DecodeParams p) {
-  using Tr = Traits<FP8, HK>;
-  constexpr int kTileBytes = Tr::kTileB;
-  constexpr int kT = Tr::kT;
-  constexpr int kRow = Tr::kRowBytes;
-  constexpr int kHq = HK * G;
-
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * 2 * kTileBytes);
-  int* s_bad = reinterpret_cast<int*>(full + kStages);  // [kStages]: the stage's tile was not loaded
-  int* s_flag = s_bad + kStages;                        // merger election
-  int64_t* s_range = reinterpret_cast<int64_t*>(s_flag + 4);  // start, end, units per CTA, first unit of b
-  int* s_cur = reinterpret_cast<int*>(s_range + 4);           // b, t, L, tiles of the first unit
-  SeqCursor<kT>* s_pcur = reinterpret_cast<SeqCursor<kT>*>(s_cur + 8);  // the producer's cursor
-  float* scr = reinterpret_cast<float*>(s_pcur + 1);                     // cross-phase merge area (HK < 8)
-
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int ln = lane & 15;
-  const int hw = lane >> 4;
-  const int h = warp % HK;
-  const int phase = warp / HK;
-  const int cta = blockIdx.x;
-  const int grid = gridDim.x;
-
-  int32_t* ws_err = reinterpret_cast<int32_t*>(p.ws + kWsErrOff);
-  int32_t* tickets = reinterpret_cast<int32_t*>(p.ws + kWsTicketOff);
-  float* parts = reinterpret_cast<float*>(p.ws + kWsMlOff);
-
-  // Programmatic dependent launch: nothing an earlier kernel wrote is read before this wait.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-
-  if (warp == 0) {
-    // Units (tiles) per sequence, scanned over lane-contiguous chunks of the batch.
-    const int chunk = (p.batch + 31) / 32;
-    const int b0 = lane * chunk, b1 = min(p.batch, b0 + chunk);
-    int64_t mine = 0;
-    for (int b = b0; b < b1; ++b) mine += (clamp_len(p, b) + kT - 1) / kT;
-    int64_t incl = mine;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int64_t v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    const int64_t total = __shfl_sync(0xffffffffu, incl, 31);
-    // Equal shares, but at least kMinUnitsPerCta tiles each: a small batch then runs on fewer
-    // CTAs instead of cutting every sequence into many parts that must be merged.
-    int64_t upc = total > 0 ? (total + grid - 1) / grid : 1;
-    upc = upc < kMinUnitsPerCta ? kMinUnitsPerCta : upc;
-    const int64_t start = min(total, int64_t(cta) * upc);
-    const int64_t end = min(total, start + upc);
-    if (lane == 0) {
-      s_range[0] = start;
-      s_range[1] = end;
-      s_range[2] = upc;
-    }
-    const int64_t excl = incl - mine;
-    if (start < end && excl <= start && start < incl) {
-      int64_t cum = excl;
-      for (int b = b0; b < b1; ++b) {
-        const int L = clamp_len(p, b);
-        const int tiles = (L + kT - 1) / kT;
-        if (start < cum + tiles) {
-          s_cur[0] = b;
-          s_cur[1] = int(start - cum);
-          s_cur[2] = L;
-          s_cur[3] = tiles;
-          s_range[3] = cum;
-          break;
-        }
-        cum += tiles;
-      }
-    }
-    // Padding rows (context 0): finite zeros, like an empty softmax.  CTA c takes b = c (mod grid).
-    for (int b = cta; b < p.batch; b += grid) {
-      if (clamp_len(p, b) != 0) continue;
-      uint4* o = reinterpret_cast<uint4*>(p.out + int64_t(b) * p.out_row_stride);
-      for (int i = lane; i < kHq * kHeadDim / 8; i += 32) o[i] = make_uint4(0, 0, 0, 0);
-    }
-  }
-  if (tid == 32) {
-    for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  const int n_units = int(s_range[1] - s_range[0]);
-  if (n_units <= 0) return;
-  SeqCursor<kT> cur{s_cur[0], s_cur[1], s_cur[2], s_cur[3], s_range[3]};
-
-  // Producer (thread 0): issues unit i into stage i % kStages.  A tile whose block id is out of
-  // range is not loaded: its stage is marked bad (the consumers skip it) and the barrier phase is
-  // completed by a plain arrive.  Its cursor lives in shared memory (only thread 0 touches it).
-  auto issue = [&](int i) {
-    SeqCursor<kT> pcur = *s_pcur;
-    const int st = i % kStages;
-    const int tok0 = pcur.t * kT;
-    const int64_t block = p.block_tables[int64_t(pcur.b) * p.bt_stride + tok0 / p.block_size];
-    if (block < 0 || block >= p.num_blocks) {
-      atomicOr(ws_err, 2);
-      s_bad[st] = 1;
-      mbar_arrive(&full[st]);
-    } else {
-      s_bad[st] = 0;
-      const int64_t slot = block * p.block_size + tok0 % p.block_size;
-      mbar_arrive_expect_tx(&full[st], 2 * kT * kRow);
-      bulk_g2s(smem + st * 2 * kTileBytes, p.k_cache + slot * kRow, kT * kRow, &full[st]);
-      bulk_g2s(smem + st * 2 * kTileBytes + kTileBytes, p.v_cache + slot * kRow, kT * kRow, &full[st]);
-    }
-    pcur.next(p);
-    *s_pcur = pcur;
-  };
-  if (tid == 0) {
-    *s_pcur = cur;
-    for (int i = 0; i < kStages && i < n_units; ++i) issue(i);
-  }
-
-  const float ks_h = (FP8 && p.k_scale) ? p.k_scale[h] : 1.0f;
-  const float qf = p.scale_log2 * ks_h;
-  const float vs = (FP8 && p.v_scale) ? p.v_scale[h] : 1.0f;
-  bool timed_out = false;
-
-  // One pass of the outer loop per segment (the part of one sequence in this share), so the query
-  // registers of a segment are dead once its tiles are done.
-  for (int i = 0; i < n_units;) {
-    float m[G], l[G];
-    float2 acc[G][4];
-    {
-      // This sequence's queries, pre-scaled for the base-2 softmax, and a fresh softmax state.
-      float2 qs[G][4];
-      const __nv_bfloat16* qb = p.q + int64_t(cur.b) * p.q_row_stride;
-#pragma unroll
-      for (int j = 0; j < G; ++j) {
-        const uint4 v = *reinterpret_cast<const uint4*>(qb + (h * G + j) * kHeadDim + 8 * ln);
-        qs[j][0] = make_float2(bf16lo(v.x) * qf, bf16hi(v.x) * qf);
-        qs[j][1] = make_float2(bf16lo(v.y) * qf, bf16hi(v.y) * qf);
-        qs[j][2] = make_float2(bf16lo(v.z) * qf, bf16hi(v.z) * qf);
-        qs[j][3] = make_float2(bf16lo(v.w) * qf, bf16hi(v.w) * qf);
-        m[j] = -INFINITY;
-        l[j] = 0.f;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[j][c] = make_float2(0.f, 0.f);
-      }
-      const int seg_end = min(n_units, i + (cur.tiles - cur.t));
-      for (; i < seg_end; ++i, ++cur.t) {
-        const int stage = i % kStages;
-        const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], (i / kStages) & 1));
-        if (ok && !s_bad[stage]) {
-          const uint8_t* Ks = smem + stage * 2 * kTileBytes;
-          const int tile_tok0 = cur.t * kT;
-          if (tile_tok0 + kT <= cur.L)
-            decode_tile<FP8, G, HK>(BoolTag<true>{}, Ks, tile_tok0, cur.L, phase, hw, ln, h, qs, m, l, acc);
-          else
-            decode_tile<FP8, G, HK>(BoolTag<false>{}, Ks, tile_tok0, cur.L, phase, hw, ln, h, qs, m, l, acc);
-        }
-        // Every warp is done with this stage: refill it (or leave together on a timeout).
-        if (__syncthreads_or(!ok)) {
-          timed_out = true;
-          break;
-        }
-        if (tid == 0 && i + kStages < n_units) issue(i + kStages);
-      }
-    }
-    if (timed_out) break;
-    --cur.t;  // back to the segment's last tile
-    const bool seq_end = cur.t == cur.tiles - 1;
-    {
-      // ---------------------------------------------------------------- segment epilogue
-      {  // the two half-warps hold disjoint tokens of the same D-slice
-        float m2[G], l2[G];
-        float2 a2[G][4];
-#pragma unroll
-        for (int j = 0; j < G; ++j) {
-          m2[j] = __shfl_xor_sync(0xffffffffu, m[j], 16);
-          l2[j] = __shfl_xor_sync(0xffffffffu, l[j], 16);
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            a2[j][c] = make_float2(__shfl_xor_sync(0xffffffffu, acc[j][c].x, 16),
-                                   __shfl_xor_sync(0xffffffffu, acc[j][c].y, 16));
-        }
-        merge_state<G>(m, l, acc, m2, l2, a2);
-      }
-      if constexpr (Tr::kPhases > 1) {  // warps that share a KV head
-        if (phase > 0 && hw == 0) {
-#pragma unroll
-          for (int j = 0; j < G; ++j) {
-            float* e = scr + ((warp * G + j) * 16 + ln) * 10;
-            e[0] = m[j];
-            e[1] = l[j];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              e[2 + 2 * c] = acc[j][c].x;
-              e[3 + 2 * c] = acc[j][c].y;
-            }
-          }
-        }
-        __syncthreads();
-        if (phase == 0) {
-          for (int ph = 1; ph < Tr::kPhases; ++ph) {
-            const int w2 = ph * HK + h;
-            float m2[G], l2[G];
-            float2 a2[G][4];
-#pragma unroll
-            for (int j = 0; j < G; ++j) {
-              const float* e = scr + ((w2 * G + j) * 16 + ln) * 10;
-              m2[j] = e[0];
-              l2[j] = e[1];
-#pragma unroll
-              for (int c = 0; c < 4; ++c) a2[j][c] = make_float2(e[2 + 2 * c], e[3 + 2 * c]);
-            }
-            merge_state<G>(m, l, acc, m2, l2, a2);
-          }
-        }
-      }
-      __nv_bfloat16* out_b = p.out + int64_t(cur.b) * p.out_row_stride;
-      const int64_t start = s_range[0], upc = s_range[2];
-      const int64_t pf = cur.first, pl = cur.first + cur.tiles - 1;
-      const bool whole = pf >= start && seq_end;
-      if (whole) {
-        if (phase == 0 && hw == 0) {
-#pragma unroll
-          for (int j = 0; j < G; ++j) {
-            const float inv = l[j] > 0.f ? vs / l[j] : 0.f;
-            float o[8];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              o[2 * c] = acc[j][c].x * inv;
-              o[2 * c + 1] = acc[j][c].y * inv;
-            }
-            *reinterpret_cast<uint4*>(out_b + (h * G + j) * kHeadDim + 8 * ln) = pack_bf16x8(o);
-          }
-        }
-      } else {
-        // Publish this CTA's part of the sequence (slot 0: it began before this share), then the
-        // last CTA to arrive merges the parts of CTAs first / upc .. last / upc in CTA order.
-        const int slot = pf < start ? 0 : 1;
-        float* part = parts + (int64_t(cta) * 2 + slot) * persist_part_floats(kHq);
-        if (phase == 0 && hw == 0) {
-#pragma unroll
-          for (int j = 0; j < G; ++j) {
-            const int hq = h * G + j;
-            float* o = part + 2 * kHq + hq * kHeadDim + 8 * ln;
-            reinterpret_cast<float4*>(o)[0] =
-                make_float4(acc[j][0].x * vs, acc[j][0].y * vs, acc[j][1].x * vs, acc[j][1].y * vs);
-            reinterpret_cast<float4*>(o)[1] =
-                make_float4(acc[j][2].x * vs, acc[j][2].y * vs, acc[j][3].x * vs, acc[j][3].y * vs);
-            if (ln == 0) {
-              part[hq] = m[j];
-              part[kHq + hq] = l[j];
-            }
-          }
-        }
-        __threadfence();
-        __syncthreads();
-        const int c_first = int(pf / upc), c_last = int(pl / upc);
-        if (tid == 0) *s_flag = atomicAdd(&tickets[cur.b], 1) == c_last - c_first;
-        __syncthreads();
-        if (*s_flag) {
-          __threadfence();
-          // One pass over the parts, four at a time: their loads are independent, so a part costs
-          // one L2 round trip per group of four instead of two dependent ones each.
-          for (int idx = tid; idx < kHq * (kHeadDim / 8); idx += kDecodeThreads) {
-            const int hq = idx / (kHeadDim / 8);
-            const int d0 = (idx % (kHeadDim / 8)) * 8;
-            float mx = -INFINITY, lsum = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (int c0 = c_first; c0 <= c_last; c0 += 4) {
-              float mc[4], lc[4];
-              float4 oa[4], ob[4];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                mc[k] = -INFINITY;
-                lc[k] = 0.f;
-                oa[k] = ob[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-                const int cc = c0 + k;
-                if (cc <= c_last) {
-                  const float* q = parts + (int64_t(cc) * 2 + (pf < int64_t(cc) * upc ? 0 : 1)) *
-                                               persist_part_floats(kHq);
-                  mc[k] = __ldcg(q + hq);
-                  lc[k] = __ldcg(q + kHq + hq);
-                  const float4* src = reinterpret_cast<const float4*>(q + 2 * kHq + hq * kHeadDim + d0);
-                  oa[k] = __ldcg(src);
-                  ob[k] = __ldcg(src + 1);
-                }
-              }
-              const float mn = fmaxf(fmaxf(mx, fmaxf(mc[0], mc[1])), fmaxf(mc[2], mc[3]));
-              if (mn == -INFINITY) continue;  // nothing but empty parts so far
-              const float f = exp2f(mx - mn);
-              lsum *= f;
-#pragma unroll
-              for (int d = 0; d < 8; ++d) o[d] *= f;
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float c = exp2f(mc[k] - mn);  // 0 for an empty part (m = -inf)
-                lsum += lc[k] * c;
-                o[0] += oa[k].x * c;
-                o[1] += oa[k].y * c;
-                o[2] += oa[k].z * c;
-                o[3] += oa[k].w * c;
-                o[4] += ob[k].x * c;
-                o[5] += ob[k].y * c;
-                o[6] += ob[k].z * c;
-                o[7] += ob[k].w * c;
-              }
-              mx = mn;
-            }
-            const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-#pragma unroll
-            for (int d = 0; d < 8; ++d) o[d] *= inv;
-            *reinterpret_cast<uint4*>(out_b + hq * kHeadDim + d0) = pack_bf16x8(o);
-          }
-          if (tid == 0) tickets[cur.b] = 0;  // ready for the next launch
-        }
-        __syncthreads();  // s_flag and scr are reused by the next segment
-      }
-      if constexpr (Tr::kPhases > 1) __syncthreads();
-    }
-    cur.next(p);
-  }
-  if (timed_out && tid == 0) {
-    atomicOr(ws_err, 1);
-    // Copies still in flight get a second bounded chance to land before the CTA exits.
-    for (int i = 0; i < kStages; ++i) mbar_wait(&full[i], 0), mbar_wait(&full[i], 1);
-  }
-}
-
-template <bool FP8, int G, int HK>
-constexpr size_t persist_smem_bytes() {
-  return size_t(kStages) * 2 * Traits<FP8, HK>::kTileB + kStages * sizeof(uint64_t) + (kStages + 4) * sizeof(int) +
-         4 * sizeof(int64_t) + 8 * sizeof(int) + sizeof(SeqCursor<Traits<FP8, HK>::kT>) +
-         (Traits<FP8, HK>::kPhases > 1 ? size_t(8) * G * 16 * 10 * 4 : 0);
-}
-
-template <bool FP8, int G, int HK>
-int launch_decode_persistent(const DecodeParams& p, cudaStream_t stream) {
-  constexpr size_t smem = persist_smem_bytes<FP8, G, HK>();
-  constexpr int kPerSm = ctas_per_sm<FP8, G>();
-  // Per device: the shared-memory opt-in and the grid (SMs x CTAs per SM).  The first call on a
-  // device happens before any graph capture (the engine's eager warm-up).
-  static std::atomic<int> grid_of[kMaxDecodeDevices];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= kMaxDecodeDevices) {
-    set_error("hl_paged_decode: no usable current device");
-    return HL_ERR_CUDA;
-  }
-  int grid = grid_of[dev].load(std::memory_order_acquire);
-  if (grid == 0) {
-    int sms = 0;
-    e = cudaFuncSetAttribute(paged_decode_persistent_kernel<FP8, G, HK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(smem));
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) {
-      set_error("hl_paged_decode: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
-      return HL_ERR_CUDA;
-    }
-    constexpr int kMaxGrid = kPersistHeadSlots / (HK * G);
-    grid = sms * kPerSm < kMaxGrid ? sms * kPerSm : kMaxGrid;
-    grid_of[dev].store(grid, std::memory_order_release);
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kDecodeThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, paged_decode_persistent_kernel<FP8, G, HK>, p);
-  if (e != cudaSuccess) {
-    set_error("hl_paged_decode: launch failed: %s", cudaGetErrorString(e));
-    return HL_ERR_CUDA;
-  }
-  return HL_OK;
-}
-
 template <bool FP8, int G, int HK>
 int launch_decode(const DecodeParams& p, cudaStream_t stream) {
   constexpr size_t smem = size_t(kStages) * 2 * Traits<FP8, HK>::kTileB + kStages * sizeof(uint64_t) + 16;
@@ -995,24 +571,24 @@ int launch_decode(const DecodeParams& p, cudaStream_t stream) {
 }
 
 template <bool FP8, int G>
-int dispatch_hk(int hk, bool split, const DecodeParams& p, cudaStream_t s) {
+int dispatch_hk(int hk, const DecodeParams& p, cudaStream_t s) {
   switch (hk) {
-    case 1: return split ? launch_decode<FP8, G, 1>(p, s) : launch_decode_persistent<FP8, G, 1>(p, s);
-    case 2: return split ? launch_decode<FP8, G, 2>(p, s) : launch_decode_persistent<FP8, G, 2>(p, s);
-    case 4: return split ? launch_decode<FP8, G, 4>(p, s) : launch_decode_persistent<FP8, G, 4>(p, s);
-    case 8: return split ? launch_decode<FP8, G, 8>(p, s) : launch_decode_persistent<FP8, G, 8>(p, s);
+    case 1: return launch_decode<FP8, G, 1>(p, s);
+    case 2: return launch_decode<FP8, G, 2>(p, s);
+    case 4: return launch_decode<FP8, G, 4>(p, s);
+    case 8: return launch_decode<FP8, G, 8>(p, s);
   }
   set_error("hl_paged_decode: num_kv_heads=%d not in {1,2,4,8}", hk);
   return HL_ERR_UNSUPPORTED;
 }
 
 template <bool FP8>
-int dispatch_g(int g, int hk, bool split, const DecodeParams& p, cudaStream_t s) {
+int dispatch_g(int g, int hk, const DecodeParams& p, cudaStream_t s) {
   switch (g) {
-    case 1: return dispatch_hk<FP8, 1>(hk, split, p, s);
-    case 2: return dispatch_hk<FP8, 2>(hk, split, p, s);
-    case 4: return dispatch_hk<FP8, 4>(hk, split, p, s);
-    case 8: return dispatch_hk<FP8, 8>(hk, split, p, s);
+    case 1: return dispatch_hk<FP8, 1>(hk, p, s);
+    case 2: return dispatch_hk<FP8, 2>(hk, p, s);
+    case 4: return dispatch_hk<FP8, 4>(hk, p, s);
+    case 8: return dispatch_hk<FP8, 8>(hk, p, s);
   }
   set_error("hl_paged_decode: Hq/Hk=%d not in {1,2,4,8}", g);
   return HL_ERR_UNSUPPORTED;
@@ -1044,14 +620,12 @@ extern "C" int64_t hl_paged_decode_workspace_size(int batch, int num_q_heads, in
   const int64_t S = max_splits_for(max_blocks_per_seq, block_size);
   const int64_t rows = int64_t(batch) * S * num_q_heads;
   const int64_t simt = kWsMlOff + align256(rows * int64_t(sizeof(float2))) + rows * head_dim * int64_t(sizeof(float));
-  const int64_t persist = kWsMlOff + int64_t(2) * kPersistHeadSlots * (kHeadDim + 2) * 4;
   const int64_t tc = decode_tc_workspace_bytes(batch, num_q_heads);
-  const int64_t cc = simt > persist ? simt : persist;
-  return cc > tc ? cc : tc;
+  return simt > tc ? simt : tc;
 }
 
 namespace {
-int paged_decode_impl(int mode, const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+int paged_decode_impl(bool allow_tc, const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
                       int kv_dtype, const float* k_scale, const float* v_scale, const int32_t* block_tables,
                       int64_t bt_stride, int max_blocks_per_seq, const int32_t* context_lens, int batch,
                       int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
@@ -1065,7 +639,7 @@ extern "C" int hl_paged_decode(const void* q, int64_t q_row_stride, const void* 
                                int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
                                float softmax_scale, void* out, int64_t out_row_stride, void* workspace,
                                int64_t workspace_bytes, void* stream) {
-  return paged_decode_impl(0, q, q_row_stride, k_cache, v_cache, kv_dtype, k_scale, v_scale, block_tables,
+  return paged_decode_impl(false, q, q_row_stride, k_cache, v_cache, kv_dtype, k_scale, v_scale, block_tables,
                            bt_stride, max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, head_dim,
                            block_size, num_blocks, softmax_scale, out, out_row_stride, workspace, workspace_bytes,
                            stream);
@@ -1077,20 +651,7 @@ extern "C" int hl_paged_decode_tc(const void* q, int64_t q_row_stride, const voi
                                     const int32_t* context_lens, int batch, int num_q_heads, int num_kv_heads,
                                     int head_dim, int block_size, int64_t num_blocks, float softmax_scale, void* out,
                                     int64_t out_row_stride, void* workspace, int64_t workspace_bytes, void* stream) {
-  return paged_decode_impl(1, q, q_row_stride, k_cache, v_cache, kv_dtype, k_scale, v_scale, block_tables,
-                           bt_stride, max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, head_dim,
-                           block_size, num_blocks, softmax_scale, out, out_row_stride, workspace, workspace_bytes,
-                           stream);
-}
-
-extern "C" int hl_paged_decode_persistent(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
-                                      int kv_dtype, const float* k_scale, const float* v_scale,
-                                      const int32_t* block_tables, int64_t bt_stride, int max_blocks_per_seq,
-                                      const int32_t* context_lens, int batch, int num_q_heads, int num_kv_heads,
-                                      int head_dim, int block_size, int64_t num_blocks, float softmax_scale,
-                                      void* out, int64_t out_row_stride, void* workspace, int64_t workspace_bytes,
-                                      void* stream) {
-  return paged_decode_impl(2, q, q_row_stride, k_cache, v_cache, kv_dtype, k_scale, v_scale, block_tables,
+  return paged_decode_impl(true, q, q_row_stride, k_cache, v_cache, kv_dtype, k_scale, v_scale, block_tables,
                            bt_stride, max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, head_dim,
                            block_size, num_blocks, softmax_scale, out, out_row_stride, workspace, workspace_bytes,
                            stream);
@@ -1098,7 +659,7 @@ extern "C" int hl_paged_decode_persistent(const void* q, int64_t q_row_stride, c
 
 namespace {
 
-int paged_decode_impl(int mode, const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+int paged_decode_impl(bool allow_tc, const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
                       int kv_dtype, const float* k_scale, const float* v_scale, const int32_t* block_tables,
                       int64_t bt_stride, int max_blocks_per_seq, const int32_t* context_lens, int batch,
                       int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
@@ -1160,8 +721,7 @@ int paged_decode_impl(int mode, const void* q, int64_t q_row_stride, const void*
   // every measured length.
   const bool tc_fits = decode_tc_supported(batch, num_q_heads, num_kv_heads, block_size, fp8) &&
                        num_blocks * block_size < (int64_t(1) << 31);
-  const bool allow_tc = mode == 1;
-  if (allow_tc || (mode == 0 && g >= (fp8 ? kTcMinGroupFp8 : kTcMinGroupBf16) && tc_fits)) {
+  if (allow_tc || (g >= (fp8 ? kTcMinGroupFp8 : kTcMinGroupBf16) && tc_fits)) {
     if (!decode_tc_supported(batch, num_q_heads, num_kv_heads, block_size, fp8)) {
       set_error("hl_paged_decode_tc: needs batch <= 2048, Hq/Hk in {1,2,4,8,16} (BF16) or {1,2,4,8} (FP8), "
                 "block_size %% 128 == 0");
@@ -1172,9 +732,8 @@ int paged_decode_impl(int mode, const void* q, int64_t q_row_stride, const void*
                             max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, block_size,
                             num_blocks, p.scale_log2, out, out_row_stride, workspace, s);
   }
-  const bool split = mode != 2;  // mode 2: the persistent kernel (comparison entry point)
-  if (fp8) return dispatch_g<true>(g, num_kv_heads, split, p, s);
-  return dispatch_g<false>(g, num_kv_heads, split, p, s);
+  if (fp8) return dispatch_g<true>(g, num_kv_heads, p, s);
+  return dispatch_g<false>(g, num_kv_heads, p, s);
 }
 
 }  // namespace

@@ -803,8 +803,8 @@ class ModelRunner:
         """Replays the recorded decode packets back to back on the device (each: a device-to-
         device packet copy + one graph replay, tokens fed back through next_tokens).  Returns
         the elapsed seconds measured with CUDA events on the launching stream, and, when
-        probe_every > 0, (algorithmic bytes, seconds, seconds of the split-K grid kernel) samples
-        of the layer-0 decode kernel timed on its own between steps."""
+        probe_every > 0, (algorithmic bytes, seconds) samples of the layer-0 decode kernel timed
+        on its own between steps."""
         graph = self.graphs[self._decode_graph_batch_size(bs)]
         stream = torch.cuda.current_stream()
         samples = []
@@ -841,29 +841,23 @@ class ModelRunner:
         v_cache = layer.decode_v_cache if self.use_fp8_kv_cache else layer.v_cache
         elem = 1 if self.use_fp8_kv_cache else 2
 
-        def timed(persistent: bool) -> float:
-            def launch():
-                kernels.paged_decode(q, k_cache, v_cache, bt, ctx, layer.scale, out=out,
-                                     workspace=self.decode_workspace, k_scale=layer.k_scale, v_scale=layer.v_scale,
-                                     persistent=persistent)
+        def launch():
+            kernels.paged_decode(q, k_cache, v_cache, bt, ctx, layer.scale, out=out, workspace=self.decode_workspace,
+                                 k_scale=layer.k_scale, v_scale=layer.v_scale)
 
-            for _ in range(3):
-                launch()
-            stream = torch.cuda.current_stream()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            reps = 20
-            # Nothing in flight before the start event: the decode kernel is a programmatic
-            # dependent launch and would otherwise begin under the last warm-up launch's tail.
-            torch.cuda.synchronize()
-            e0.record(stream)
-            for _ in range(reps):
-                launch()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            return e0.elapsed_time(e1) / 1e3 / reps
-
-        t = timed(False)
-        t_split = timed(True)  # the persistent kernel on the same live cache, for comparison
+        for _ in range(3):
+            launch()
+        stream = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        # Nothing in flight before the start event: the decode kernel is a programmatic dependent
+        # launch and would otherwise begin under the last warm-up launch's tail.
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            launch()
+        e1.record(stream)
+        torch.cuda.synchronize()
         lens = ctx.tolist()
         nbytes = sum(lens) * hk * d * elem * 2 + bs * hq * d * 2 * 2
-        return nbytes, t, t_split
+        return nbytes, e0.elapsed_time(e1) / 1e3 / reps

@@ -145,8 +145,7 @@ def make_decode_workspace(batch: int, num_q_heads: int, head_dim: int, max_block
 def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                  context_lens: torch.Tensor, softmax_scale: float, out: torch.Tensor | None = None,
                  workspace: torch.Tensor | None = None, k_scale: torch.Tensor | None = None,
-                 v_scale: torch.Tensor | None = None, tensor_cores: bool = False,
-                 persistent: bool = False) -> torch.Tensor:
+                 v_scale: torch.Tensor | None = None, tensor_cores: bool = False) -> torch.Tensor:
     """Decode attention for one new token per sequence over the paged cache.
 
     q [B, Hq, D] (or [B, 1, Hq, D]) bf16; k_cache/v_cache [NB, BS, Hk, D] bf16 or e4m3;
@@ -154,8 +153,7 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
     The semantics are flash_attn_with_kvcache's for a single causal query token
     (mini_vllm/layers/attention.py:162-170).  The library picks the kernel (the tcgen05 one for
     GQA ratios >= 4); tensor_cores=True forces the tcgen05 variant (hl_paged_decode_tc) for any
-    ratio it supports; persistent=True runs the persistent CUDA-core kernel
-    (hl_paged_decode_persistent) in place of the split-K grid kernel."""
+    ratio it supports."""
     if q.dim() == 4:
         assert q.shape[1] == 1
         q = q.squeeze(1)
@@ -181,7 +179,7 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
     if workspace is None:
         workspace = make_decode_workspace(b, hq, hd, max_blocks, bsz, q.device)
     lib = _lib.load()
-    fn = lib.hl_paged_decode_tc if tensor_cores else (lib.hl_paged_decode_persistent if persistent else lib.hl_paged_decode)
+    fn = lib.hl_paged_decode_tc if tensor_cores else lib.hl_paged_decode
     check(fn(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), kv_dtype,
              _p(k_scale), _p(v_scale), block_tables.data_ptr(), block_tables.stride(0),
              max_blocks, context_lens.data_ptr(), b, hq, hk, hd, bsz, nb, float(softmax_scale),

@@ -136,20 +136,6 @@ int hl_paged_decode_tc(const void* q, int64_t q_row_stride,
                     void* out, int64_t out_row_stride,
                     void* workspace, int64_t workspace_bytes, void* stream);
 
-/* hl_paged_decode on a persistent CUDA-core kernel (SMs x CTAs-per-SM CTAs walking equal shares
- * of the batch's tiles, sequences cut by a share boundary merged by their last CTA) instead of the
- * split-K grid kernel it runs by default for Hq/Hk <= 2; same arguments, semantics and workspace.
- * Kept for comparison. */
-int hl_paged_decode_persistent(const void* q, int64_t q_row_stride,
-                               const void* k_cache, const void* v_cache, int kv_dtype,
-                           const float* k_scale, const float* v_scale,
-                           const int32_t* block_tables, int64_t bt_stride, int max_blocks_per_seq,
-                           const int32_t* context_lens, int batch,
-                           int num_q_heads, int num_kv_heads, int head_dim,
-                           int block_size, int64_t num_blocks, float softmax_scale,
-                           void* out, int64_t out_row_stride,
-                           void* workspace, int64_t workspace_bytes, void* stream);
-
 /* Allocation-free variant of hl_paged_decode (no counterpart in the reference).  For callers
  * that cannot allocate device memory themselves — a host binding this library through an FFI
  * with no device allocator, or a serving loop whose memory is all reserved up front and must not

@@ -156,30 +156,6 @@ def test_decode_gqa_layouts_and_edge_lengths(hq, hk):
     assert_close(out, want, **BF16_TOL, what=f"hq={hq} hk={hk}")
 
 
-@pytest.mark.parametrize("hq,hk,fp8", [(16, 8, False), (8, 1, False), (16, 8, True), (8, 8, False)])
-def test_decode_persistent_kernel_against_oracle(hq, hk, fp8):
-    """The persistent CUDA-core kernel (hl_paged_decode_persistent, kept for comparison with the
-    default split-K grid kernel) against the oracle, on edge lengths, twice in a row on one
-    workspace."""
-    g = torch.Generator().manual_seed(50 + hq + hk)
-    k, v, bt, ln = make_paged(g, len(EDGE_LENS), hk, 128, sum(-(-n // 256) for n in EDGE_LENS) + 2, 256, EDGE_LENS)
-    q = torch.randn(len(EDGE_LENS), hq, 128, generator=g).bfloat16()
-    ks = vs = None
-    if fp8:
-        ks, vs = torch.rand(hk, generator=g) + 0.5, torch.rand(hk, generator=g) + 0.5
-        k, v = kv_store.quantize_e4m3(k, ks), kv_store.quantize_e4m3(v, vs)
-    kd = k.to(DEV).view(torch.float8_e4m3fn) if fp8 else k.to(DEV)
-    vd = v.to(DEV).view(torch.float8_e4m3fn) if fp8 else v.to(DEV)
-    ws = kernels.make_decode_workspace(len(EDGE_LENS), hq, 128, bt.shape[1], 256, DEV)
-    want = oattn.paged_decode(q, k, v, bt, ln, 128 ** -0.5, ks, vs, fp8=fp8)
-    for _ in range(2):
-        out = kernels.paged_decode(q.to(DEV), kd, vd, bt.to(DEV), ln.to(DEV), 128 ** -0.5, workspace=ws,
-                                   k_scale=None if ks is None else ks.to(DEV),
-                                   v_scale=None if vs is None else vs.to(DEV), persistent=True)
-        assert_close(out, want, **(dict(rtol=2e-2, atol=6e-2) if fp8 else BF16_TOL), what="persistent kernel")
-    assert kernels.decode_errors(ws) == 0
-
-
 def test_decode_workspace_reuse_and_padding_rows():
     """Two launches sharing one workspace (tickets must be reset), with padding rows
     (context 0, block table -1) as the CUDA graph buckets produce."""
