@@ -546,9 +546,9 @@ def small_kernels(args, g):
 
 
 def allreduce_profile(args):
-    """Under torchrun with --gpus N: the fused NVLink all-reduce + add + RMSNorm against NCCL
-    all_reduce followed by the add + RMSNorm kernel, at decode batches of the 0.6B (hidden 1024)
-    and 8B (hidden 4096) models.  Each variant is captured in a CUDA graph of 56 calls (one
+    """Under torchrun with --gpus N: the fused NVLink all-reduce + add + RMSNorm (one-shot and
+    two-shot kernels) against NCCL all_reduce followed by the add + RMSNorm kernel, at decode
+    batches of the 0.6B (hidden 1024) and 8B (hidden 4096) models.  Each variant is captured in a CUDA graph of 56 calls (one
     decode step's worth) and replayed; CUDA events, max over ranks."""
     import torch
     import torch.distributed as dist
@@ -574,6 +574,13 @@ def allreduce_profile(args):
             out = torch.empty_like(res)
 
             def fused():
+                ar.two_shot = False
+                for i in range(calls):
+                    ar.output(i % 2, rows).copy_(part)
+                    ar.add_rmsnorm(i % 2, rows, res, w, 1e-6, out)
+
+            def fused_2shot():
+                ar.two_shot = True
                 for i in range(calls):
                     ar.output(i % 2, rows).copy_(part)
                     ar.add_rmsnorm(i % 2, rows, res, w, 1e-6, out)
@@ -589,7 +596,8 @@ def allreduce_profile(args):
                     ar.output(i % 2, rows).copy_(part)
                     part.clone()
 
-            for name, fn in (("fused_nvlink", fused), ("nccl_plus_rmsnorm", nccl), ("copies_only", copies)):
+            for name, fn in (("fused_nvlink", fused), ("fused_nvlink_2shot", fused_2shot),
+                             ("nccl_plus_rmsnorm", nccl), ("copies_only", copies)):
                 fn()
                 torch.cuda.synchronize()
                 graph = torch.cuda.CUDAGraph()

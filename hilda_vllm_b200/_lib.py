@@ -115,6 +115,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hl_allreduce_signal_bytes": (c_i64, []),
     "hl_allreduce_add_rmsnorm": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_i64, c_f32,
                                          c_vp, c_vp, c_i64, c_vp]),
+    "hl_allreduce_add_rmsnorm_2shot": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_i64,
+                                               c_f32, c_vp, c_vp, c_i64, c_vp]),
     "hl_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_vp]),
     "hl_sample": (c_int, [c_vp, c_i64, c_int, c_int, c_i64, c_vp, ctypes.c_uint64, c_vp, c_vp, c_vp, c_vp]),
     "hl_sample_filtered": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_vp, ctypes.c_uint64, c_vp, c_vp,

@@ -33,7 +33,8 @@ constexpr int kArThreads = 128;
 
 struct ArParams {
   const __nv_bfloat16* data[kArMaxRanks];  // rank p's partial sums [rows, hidden]
-  int* signal[kArMaxRanks];                // rank p's flags [kArMaxBlocks][kArMaxRanks]
+  __nv_bfloat16* result[kArMaxRanks];      // two-shot: rank p's reduced rows [rows, hidden]
+  int* signal[kArMaxRanks];                // rank p's flags [2][kArMaxBlocks][kArMaxRanks]
   int world;
   int rank;
   int rows;
@@ -60,6 +61,13 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // copies older than the flag.
 __device__ __forceinline__ void store_flag_sys(int* p, int v) {
   asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Publishes this thread's earlier stores, and those it has observed (the CTA's, through the
+// __syncthreads before it), at system scope before the flag: the two-shot barrier announces rows
+// that this kernel itself pushed into the peers' memory.
+__device__ __forceinline__ void store_flag_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ int load_acquire_sys(const int* p) {
@@ -186,6 +194,173 @@ __global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(const __grid
   }
 }
 
+
+// Barrier of this CTA with the same CTA of every peer on flag bank `bank`: thread t < world
+// (t != rank) writes the epoch into peer t's slot for this rank and polls its own slot for peer t.
+// Returns false (and records HL_AR_TIMEOUT) if a peer did not arrive in time.
+template <bool kRelease>
+__device__ __forceinline__ bool cta_barrier(const ArParams& p, int bank, int epoch, int* s_ok) {
+  const int blk = blockIdx.x;
+  const int tid = threadIdx.x;
+  if (tid < p.world && tid != p.rank) {
+    int* slot = p.signal[tid] + (bank * kArMaxBlocks + blk) * kArMaxRanks + p.rank;
+    if constexpr (kRelease)
+      store_flag_release_sys(slot, epoch);
+    else
+      store_flag_sys(slot, epoch);
+    const int* mine = p.signal[p.rank] + (bank * kArMaxBlocks + blk) * kArMaxRanks + tid;
+    const unsigned long long t0 = global_ns();
+    bool arrived = false;
+    for (uint32_t it = 0;; ++it) {
+      if (load_acquire_sys(mine) >= epoch) {
+        arrived = true;
+        break;
+      }
+      if ((it & 255u) == 255u && global_ns() - t0 > p.timeout_ns) break;
+    }
+    if (!arrived) {
+      *s_ok = 0;
+      atomicOr(p.error_word, HL_AR_TIMEOUT);
+    }
+  }
+  __syncthreads();
+  return *s_ok != 0;
+}
+
+// Two-shot variant for more than two ranks: each rank reduces only the rows it owns (row r is
+// owned by rank r % world), reading them from every rank, and pushes the bf16 sum into every
+// rank's result buffer; after a second barrier (released at system scope, because it announces
+// this kernel's own remote stores) every rank reads all rows' sums from its local result buffer
+// and applies the add + RMSNorm.  Per call and rank the NVLink traffic is 2 (world - 1) / world
+// of the rows instead of the one-shot's (world - 1) x the rows, for one more barrier.  The sums
+// are taken in rank order, as in the one-shot kernel, so both give bit-identical results.
+// A CTA works on the same rows in both phases (warp w: rows blk * 4 + w + k * grid * 4), so the
+// second barrier is again between equal CTA indices.
+template <int NV>
+__global__ void __launch_bounds__(kArThreads) ar2_add_rmsnorm_kernel(const __grid_constant__ ArParams p) {
+  __shared__ int s_epoch;
+  __shared__ int s_ok;
+  const int blk = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  if (tid == 0) {
+    s_epoch = p.epochs[blk] + 1;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const int epoch = s_epoch;
+  // The partial sums were written by an earlier kernel of this stream: relaxed flags suffice.
+  bool ok = cta_barrier<false>(p, 0, epoch, &s_ok);
+  if (tid == 0) p.epochs[blk] = epoch;
+
+  constexpr int kRowsPerCta = kArThreads / 32;
+  constexpr int RG = NV <= 4 ? 4 : (NV <= 8 ? 2 : 1);
+  // ---------------------------------------------------------------- phase 1: owned rows
+  if (ok) {
+    for (int row = blk * kRowsPerCta + warp; row < p.rows; row += gridDim.x * kRowsPerCta) {
+      if (row % p.world != p.rank) continue;
+      const int64_t base = int64_t(row) * p.hidden + 8 * lane;
+      float buf[NV][8];
+#pragma unroll
+      for (int c = 0; c < NV; ++c)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) buf[c][t] = 0.f;
+      for (int r0 = 0; r0 < p.world; r0 += RG) {
+        uint4 a[RG][NV];
+#pragma unroll
+        for (int g = 0; g < RG; ++g)
+          if (r0 + g < p.world)
+#pragma unroll
+            for (int c = 0; c < NV; ++c)
+              a[g][c] = __ldcv(reinterpret_cast<const uint4*>(p.data[r0 + g] + base + 256 * c));
+#pragma unroll
+        for (int g = 0; g < RG; ++g)
+          if (r0 + g < p.world)
+#pragma unroll
+            for (int c = 0; c < NV; ++c) {
+              const uint32_t w[4] = {a[g][c].x, a[g][c].y, a[g][c].z, a[g][c].w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                buf[c][2 * t] = __fadd_rn(buf[c][2 * t], bf16lo(w[t]));
+                buf[c][2 * t + 1] = __fadd_rn(buf[c][2 * t + 1], bf16hi(w[t]));
+              }
+            }
+      }
+      uint4 sum[NV];
+#pragma unroll
+      for (int c = 0; c < NV; ++c) {
+        uint32_t o[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(buf[c][2 * t], buf[c][2 * t + 1]);
+          o[t] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        sum[c] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      for (int r = 0; r < p.world; ++r)
+#pragma unroll
+        for (int c = 0; c < NV; ++c) *reinterpret_cast<uint4*>(p.result[r] + base + 256 * c) = sum[c];
+    }
+  }
+  __syncthreads();
+  ok = ok && cta_barrier<true>(p, 1, epoch, &s_ok);
+
+  // ---------------------------------------------------------------- phase 2: add + RMSNorm
+  const __nv_bfloat16* mine = p.result[p.rank];
+  for (int row = blk * kRowsPerCta + warp; row < p.rows; row += gridDim.x * kRowsPerCta) {
+    const int64_t base = int64_t(row) * p.hidden + 8 * lane;
+    float buf[NV][8];
+    uint4 rv[NV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      rv[c] = *reinterpret_cast<const uint4*>(p.residual + base + 256 * c);
+      // Pushed by the row's owner in this call: not cached in L1 from an earlier call.
+      const uint4 sv = ok ? __ldcv(reinterpret_cast<const uint4*>(mine + base + 256 * c)) : make_uint4(0, 0, 0, 0);
+      const uint32_t w[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        buf[c][2 * t] = bf16lo(w[t]);
+        buf[c][2 * t + 1] = bf16hi(w[t]);
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      const uint32_t rw[4] = {rv[c].x, rv[c].y, rv[c].z, rv[c].w};
+      uint32_t ro[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        buf[c][2 * t] = __fadd_rn(buf[c][2 * t], bf16lo(rw[t]));
+        buf[c][2 * t + 1] = __fadd_rn(buf[c][2 * t + 1], bf16hi(rw[t]));
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(buf[c][2 * t], buf[c][2 * t + 1]);
+        ro[t] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      *reinterpret_cast<uint4*>(p.residual + base + 256 * c) = make_uint4(ro[0], ro[1], ro[2], ro[3]);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) ss = fmaf(buf[c][t], buf[c][t], ss);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / float(p.hidden) + p.eps);
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      const int col = 8 * (lane + 32 * c);
+      const uint4 wv = *reinterpret_cast<const uint4*>(p.weight + col);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float a = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t], inv)), bf16lo(ww[t]));
+        const float b = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t + 1], inv)), bf16hi(ww[t]));
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
+        o[t] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      *reinterpret_cast<uint4*>(p.out + int64_t(row) * p.out_stride + col) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 }  // namespace
 }  // namespace hl
 
@@ -249,13 +424,39 @@ extern "C" int hl_ipc_close_handle(void* dev_ptr) {
   return HL_OK;
 }
 
-extern "C" int64_t hl_allreduce_signal_bytes(void) { return int64_t(kArMaxBlocks) * kArMaxRanks * sizeof(int); }
+// Two flag banks (the two-shot kernel's second barrier uses bank 1).
+extern "C" int64_t hl_allreduce_signal_bytes(void) { return int64_t(2) * kArMaxBlocks * kArMaxRanks * sizeof(int); }
+
+namespace {
+int allreduce_launch(void* const* peer_data, void* const* peer_result, void* const* peer_signal, int world, int rank,
+                     int rows, int hidden, void* residual, const void* weight, void* out, int64_t out_stride,
+                     float eps, int* epochs, int* error_word, int64_t timeout_ns, void* stream);
+}
 
 extern "C" int hl_allreduce_add_rmsnorm(void* const* peer_data, void* const* peer_signal, int world, int rank,
                                         int rows, int hidden, void* residual, const void* weight, void* out,
                                         int64_t out_stride, float eps, int* epochs, int* error_word,
                                         int64_t timeout_ns, void* stream) {
   clear_error();
+  return allreduce_launch(peer_data, nullptr, peer_signal, world, rank, rows, hidden, residual, weight, out,
+                          out_stride, eps, epochs, error_word, timeout_ns, stream);
+}
+
+extern "C" int hl_allreduce_add_rmsnorm_2shot(void* const* peer_data, void* const* peer_result,
+                                              void* const* peer_signal, int world, int rank, int rows, int hidden,
+                                              void* residual, const void* weight, void* out, int64_t out_stride,
+                                              float eps, int* epochs, int* error_word, int64_t timeout_ns,
+                                              void* stream) {
+  clear_error();
+  HL_CHECK_ARG(peer_result, "hl_allreduce_add_rmsnorm_2shot: result buffers missing");
+  return allreduce_launch(peer_data, peer_result, peer_signal, world, rank, rows, hidden, residual, weight, out,
+                          out_stride, eps, epochs, error_word, timeout_ns, stream);
+}
+
+namespace {
+int allreduce_launch(void* const* peer_data, void* const* peer_result, void* const* peer_signal, int world, int rank,
+                     int rows, int hidden, void* residual, const void* weight, void* out, int64_t out_stride,
+                     float eps, int* epochs, int* error_word, int64_t timeout_ns, void* stream) {
   if (rows == 0) return HL_OK;
   HL_CHECK_ARG(peer_data && peer_signal && residual && weight && out && epochs && error_word && rows > 0,
                "hl_allreduce_add_rmsnorm: bad arguments");
@@ -265,6 +466,10 @@ extern "C" int hl_allreduce_add_rmsnorm(void* const* peer_data, void* const* pee
   HL_CHECK_ARG(aligned16(residual) && aligned16(weight) && aligned16(out) && out_stride % 8 == 0,
                "hl_allreduce_add_rmsnorm: 16-byte alignment required");
   HL_CHECK_ARG(timeout_ns > 0, "hl_allreduce_add_rmsnorm: timeout must be positive");
+  // Two-shot: a CTA must see the same rows in every call (row r -> CTA r / 4), which holds while
+  // one pass of the grid covers all rows.
+  HL_CHECK_ARG(!peer_result || rows <= kArMaxBlocks * (kArThreads / 32),
+               "hl_allreduce_add_rmsnorm_2shot: at most %d rows", kArMaxBlocks * (kArThreads / 32));
   ArParams prm;
   memset(&prm, 0, sizeof(prm));
   for (int r = 0; r < world; ++r) {
@@ -272,6 +477,10 @@ extern "C" int hl_allreduce_add_rmsnorm(void* const* peer_data, void* const* pee
                  "hl_allreduce_add_rmsnorm: null or misaligned peer pointer");
     prm.data[r] = static_cast<const __nv_bfloat16*>(peer_data[r]);
     prm.signal[r] = static_cast<int*>(peer_signal[r]);
+    if (peer_result) {
+      HL_CHECK_ARG(peer_result[r] && aligned16(peer_result[r]), "hl_allreduce_add_rmsnorm_2shot: bad result pointer");
+      prm.result[r] = static_cast<__nv_bfloat16*>(peer_result[r]);
+    }
   }
   prm.world = world;
   prm.rank = rank;
@@ -288,9 +497,12 @@ extern "C" int hl_allreduce_add_rmsnorm(void* const* peer_data, void* const* pee
   const int groups = (rows + kArThreads / 32 - 1) / (kArThreads / 32);
   const int blocks = groups < kArMaxBlocks ? groups : kArMaxBlocks;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define HL_AR_CASE(NV) \
-  case NV:             \
-    ar_add_rmsnorm_kernel<NV><<<blocks, kArThreads, 0, s>>>(prm); \
+#define HL_AR_CASE(NV)                                                 \
+  case NV:                                                             \
+    if (peer_result)                                                   \
+      ar2_add_rmsnorm_kernel<NV><<<blocks, kArThreads, 0, s>>>(prm);   \
+    else                                                               \
+      ar_add_rmsnorm_kernel<NV><<<blocks, kArThreads, 0, s>>>(prm);    \
     break;
   switch (hidden / 256) {
     HL_AR_CASE(1) HL_AR_CASE(2) HL_AR_CASE(3) HL_AR_CASE(4) HL_AR_CASE(5) HL_AR_CASE(6) HL_AR_CASE(8)
@@ -304,3 +516,4 @@ extern "C" int hl_allreduce_add_rmsnorm(void* const* peer_data, void* const* pee
   HL_CHECK_LAUNCH("hl_allreduce_add_rmsnorm");
   return HL_OK;
 }
+}  // namespace

@@ -58,7 +58,8 @@ class NvlinkAllReduce:
         sig_bytes = int(self.lib.hl_allreduce_signal_bytes())
         self._owned: list[int] = []
         self._opened: list[int] = []
-        own = [self._alloc(nbytes), self._alloc(nbytes), self._alloc(sig_bytes)]
+        # [partials slot 0, partials slot 1, flags, reduced rows (two-shot)]
+        own = [self._alloc(nbytes), self._alloc(nbytes), self._alloc(sig_bytes), self._alloc(nbytes)]
         self._epochs = self._alloc(MAX_BLOCKS * 4)
         self._error = self._alloc(256)
         handles = b""
@@ -71,9 +72,9 @@ class NvlinkAllReduce:
             dist.all_gather_object(gathered, handles, group=group)
         else:
             gathered[0] = handles
-        ptrs = [[0] * world for _ in range(3)]  # [data0, data1, signal][rank]
+        ptrs = [[0] * world for _ in range(4)]  # [data0, data1, signal, result][rank]
         for p in range(world):
-            for i in range(3):
+            for i in range(4):
                 if p == rank:
                     ptrs[i][p] = own[i]
                     continue
@@ -85,6 +86,10 @@ class NvlinkAllReduce:
         arr = ctypes.c_void_p * world
         self._peer_data = [arr(*ptrs[0]), arr(*ptrs[1])]
         self._peer_signal = arr(*ptrs[2])
+        self._peer_result = arr(*ptrs[3])
+        # More than two ranks: the two-shot kernel (each rank reduces 1/world of the rows and pushes
+        # them to all), whose NVLink traffic does not grow with the rank count.
+        self.two_shot = world > 2
         self._buf_ptrs = own[:2]
         self.buffers = [torch.as_tensor(_DeviceArray(p, (max_rows, hidden), "<i2"), device=device).view(torch.bfloat16)
                         for p in own[:2]]
@@ -99,14 +104,13 @@ class NvlinkAllReduce:
 
     # ------------------------------------------------------------------ use
     def fits(self, rows: int) -> bool:
-        """Whether this batch takes the fused one-shot path.  Every rank reads the rows of all
-        the others, so the traffic grows with (world - 1) x hidden: measured on B200 (56 calls in
-        a graph, 256 rows), it beats NCCL + RMSNorm at 2 ranks up to hidden 4096 (7.8 vs 18.3 us
-        at hidden 1024, 14.9 vs 27.8 at 4096) and at 8 ranks for hidden 1024 (18.7 vs 34.2 us),
-        but not at 8 ranks for hidden 4096 (72.7 vs 40.8 us), where NCCL moves less data."""
-        if not 0 < rows <= self.max_rows:
-            return False
-        return self.world == 2 or self.hidden <= 2048
+        """Whether this batch takes the fused path (decode batches up to the buffers' rows).  At
+        two ranks the one-shot kernel (each rank reads the other's rows) beat NCCL + RMSNorm on
+        B200 (56 calls in a graph, 256 rows: 7.8 vs 18.3 us at hidden 1024, 14.9 vs 27.8 at 4096);
+        from three ranks on the two-shot kernel runs, whose traffic per rank stays below twice the
+        rows (the one-shot kernel's grows with world - 1: 72.7 vs NCCL's 40.8 us at 8 ranks and
+        hidden 4096)."""
+        return 0 < rows <= min(self.max_rows, 512)
 
     def output(self, slot: int, rows: int) -> torch.Tensor:
         """Where the row-parallel GEMM of `slot` writes its partial sums for `rows` rows."""
@@ -130,6 +134,13 @@ class NvlinkAllReduce:
             out = torch.empty_like(residual)
         stream = torch.cuda.current_stream(residual.device).cuda_stream
         self.stats["calls"] += 1
+        if self.two_shot:
+            check(self.lib.hl_allreduce_add_rmsnorm_2shot(
+                ctypes.addressof(self._peer_data[slot]), ctypes.addressof(self._peer_result),
+                ctypes.addressof(self._peer_signal), self.world, self.rank, rows, self.hidden, residual.data_ptr(),
+                weight.data_ptr(), out.data_ptr(), out.stride(0), float(eps), ctypes.c_void_p(self._epochs),
+                ctypes.c_void_p(self._error), self.timeout_ns, stream), "hl_allreduce_add_rmsnorm_2shot")
+            return out, residual
         check(self.lib.hl_allreduce_add_rmsnorm(
             ctypes.addressof(self._peer_data[slot]), ctypes.addressof(self._peer_signal), self.world, self.rank, rows,
             self.hidden, residual.data_ptr(), weight.data_ptr(), out.data_ptr(), out.stride(0), float(eps),

@@ -360,6 +360,19 @@ int hl_allreduce_add_rmsnorm(void* const* peer_data, void* const* peer_signal, i
                              int64_t out_stride, float eps, int* epochs, int* error_word,
                              int64_t timeout_ns, void* stream);
 
+/* Two-shot form of hl_allreduce_add_rmsnorm for more than two ranks, same result bit for bit:
+ * rank p sums only rows r with r % world == p (reading them from every rank) and stores the bf16
+ * sum into every rank's result buffer (peer_result: world device pointers to [rows, hidden] bf16
+ * buffers, mapped like peer_data); after a second barrier every rank applies the add + RMSNorm
+ * to all rows from its own result buffer.  Per call each rank moves 2 (world - 1) / world of the
+ * rows over NVLink instead of (world - 1) x the rows.  rows <= 512; signal areas as above (the
+ * second barrier uses their second half).  Replaces the same calls as hl_allreduce_add_rmsnorm
+ * (mini_vllm/layers/linear.py:176-178 with layers/layernorm.py:30-42). */
+int hl_allreduce_add_rmsnorm_2shot(void* const* peer_data, void* const* peer_result, void* const* peer_signal,
+                                   int world, int rank, int rows, int hidden, void* residual,
+                                   const void* weight, void* out, int64_t out_stride, float eps, int* epochs,
+                                   int* error_word, int64_t timeout_ns, void* stream);
+
 /* Token per row of bf16 logits: rows with temperatures[row] > 0 are sampled by the Gumbel-max
  * trick, argmax_i (logit_i / T + Gumbel noise) — the distribution of the reference's
  * exponential-race Sampler with top_k = -1, top_p = 1 (mini_vllm/layers/sampler.py:12-25) — the

@@ -3,8 +3,9 @@
 * one rank: the kernel reduces to add + RMSNorm and must equal hl_rmsnorm bit for bit;
 * a peer that never arrives (its flag is never set): the bounded wait expires, the error word
   says HL_AR_TIMEOUT, the context stays usable;
-* two GPUs (skipped with fewer): two processes, several alternating calls, outputs bit-identical
-  on both ranks and equal to bf16(sum of partials) + add + RMSNorm.
+* two or more GPUs (skipped with fewer): one process per GPU, several alternating calls, outputs
+  bit-identical on every rank and equal to bf16(sum of partials) + add + RMSNorm, for the one-shot
+  and the two-shot kernel.
 """
 import ctypes
 import os
@@ -30,10 +31,12 @@ def _reference(partials, residual, weight, eps):
     return y, res
 
 
+@pytest.mark.parametrize("two_shot", [False, True])
 @pytest.mark.parametrize("rows,hidden", [(1, 1024), (256, 1024), (300, 4096)])
-def test_single_rank_equals_add_rmsnorm(rows, hidden):
+def test_single_rank_equals_add_rmsnorm(rows, hidden, two_shot):
     g = torch.Generator().manual_seed(rows + hidden)
     ar = NvlinkAllReduce(0, 1, 512, hidden, torch.device(DEV))
+    ar.two_shot = two_shot
     try:
         w = (torch.rand(hidden, generator=g) + 0.5).bfloat16().to(DEV)
         for slot in (0, 1, 0):
@@ -89,14 +92,14 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, two_shot, hidden, rows):
     import torch.distributed as dist
     try:
         torch.cuda.set_device(rank)
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 device_id=torch.device("cuda", rank))
-        hidden, rows = 1024, 256
         ar = NvlinkAllReduce(rank, world, 512, hidden, torch.device("cuda", rank), timeout_s=10.0)
+        ar.two_shot = two_shot
         w = (torch.arange(hidden, device="cuda") % 7 + 1).bfloat16() / 4
         results = []
         for call in range(6):
@@ -125,18 +128,22 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_ranks_bit_exact_and_identical():
+@pytest.mark.parametrize("two_shot,hidden,rows", [(False, 1024, 256), (True, 1024, 256), (True, 4096, 300)])
+def test_ranks_bit_exact_and_identical(two_shot, hidden, rows):
+    """All GPUs of the box (up to 8) as ranks, one-shot and two-shot kernels: every rank's output
+    and residual equal bf16(sum of partials in rank order) + add + RMSNorm bit for bit."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
+    world = min(torch.cuda.device_count(), 8)
     env_backup = os.environ.get("NCCL_NVLS_ENABLE")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     try:
-        procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+        procs = [ctx.Process(target=_worker, args=(r, world, port, q, two_shot, hidden, rows)) for r in range(world)]
         for p in procs:
             p.start()
-        out = [q.get(timeout=300) for _ in range(2)]
+        out = [q.get(timeout=300) for _ in range(world)]
         for p in procs:
             p.join(timeout=60)
     finally:
@@ -148,4 +155,5 @@ def test_two_ranks_bit_exact_and_identical():
     for rank, results, err in out:
         assert err == 0, (rank, results)
         assert all(ok_y and ok_r for ok_y, ok_r, _ in results), (rank, results)
-    assert [c for *_, c in out[0][1]] == [c for *_, c in out[1][1]]  # identical on both ranks
+    for other in out[1:]:
+        assert [c for *_, c in out[0][1]] == [c for *_, c in other[1]]  # identical on every rank
