@@ -9,17 +9,19 @@ decode step's critical path.  Here the ranks poll a sequence number instead:
 
   header (little-endian uint64 words)
     [0] seq      messages published so far
-    [1] length   payload bytes of message `seq`
-    [2] crc      crc32 of that payload
     [3] writer   process id of rank 0 (readers give up if it disappears)
-    [8 + r]      ack of rank r: the last seq it has finished reading
-  payload at PAYLOAD_OFF
+    [8 + r]      ack of rank r: the number of messages it has finished reading
+    [72 + k]     payload bytes of the message in slot k (k < SLOTS)
+    [72 + SLOTS + k]  crc32 of that payload
+  payload: SLOTS slots of equal size after the header; message i lives in slot i % SLOTS
 
-Writer: waits until every reader acked the previous message (the payload area is then free),
-writes payload, length and crc, then seq + 1.  Reader: waits until seq moves, copies the payload,
-checks the crc (on a weakly ordered CPU it may see the new seq before the payload; it then reads
-again), unpickles, acks.  Waits poll for a while, then back off with short sleeps, so an idle rank
-does not hold a core at 100 %.
+Writer: message i may reuse its slot once every reader has acked message i - SLOTS, so rank 0 can
+run up to SLOTS calls ahead of the slowest rank (a decode step then never waits for the other
+ranks to wake up and read the previous one); it writes payload, length and crc, then seq = i + 1.
+Reader: waits until seq moves past what it has read, copies the slot, checks the crc (on a weakly
+ordered CPU it may see the new seq before the payload; it then reads again), unpickles, acks.
+Waits spin for a while (a rank waiting for its next step should wake at once), then yield, then
+back off with short sleeps, so an idle rank does not hold a core at 100 %.
 """
 from __future__ import annotations
 
@@ -32,9 +34,12 @@ from multiprocessing.shared_memory import SharedMemory
 
 import numpy as np
 
-HEADER_WORDS = 8 + 64  # fixed words + one ack slot per rank (up to 64 ranks)
+SLOTS = 8
+HEADER_WORDS = 8 + 64 + 2 * SLOTS  # fixed words, one ack per rank (up to 64 ranks), slot lengths and crcs
+LEN_OFF = 8 + 64
+CRC_OFF = LEN_OFF + SLOTS
 PAYLOAD_OFF = HEADER_WORDS * 8
-DEFAULT_BYTES = 4 << 20  # the largest call (prefill metadata of 16384 tokens) is ~0.35 MB
+DEFAULT_BYTES = 8 << 20  # SLOTS x 1 MB; the largest call (prefill metadata of 16384 tokens) is ~0.35 MB
 
 
 class ControlPlaneError(RuntimeError):
@@ -60,7 +65,8 @@ class ShmChannel:
         self.buf, self.rank, self.world, self.owner = buf, rank, world, owner
         self._name, self._closer = name, closer
         self.hdr = np.ndarray((HEADER_WORDS,), dtype=np.uint64, buffer=buf)
-        self.capacity = size - PAYLOAD_OFF
+        self.slot_bytes = ((size - PAYLOAD_OFF) // SLOTS) & ~63
+        self.capacity = self.slot_bytes
         # A reader starts from 0, so one that attaches after the first message still reads it
         # (the writer cannot move past a message until every reader has acked it).
         self.seen = 0
@@ -108,9 +114,9 @@ class ShmChannel:
     # -------------------------------------------------------------- waiting
     @staticmethod
     def _pause(spins: int) -> None:
-        if spins < 2000:
+        if spins < 200_000:
             return
-        time.sleep(0 if spins < 20000 else 0.0002)
+        time.sleep(0 if spins < 400_000 else 0.0002)
 
     # -------------------------------------------------------------- writer
     def send(self, method: str, *args, timeout_s: float = 120.0) -> None:
@@ -121,16 +127,19 @@ class ShmChannel:
                                     "segment")
         seq = int(self.hdr[0])
         acks = self.hdr[8 + 1:8 + self.world]
+        need = seq - SLOTS + 1  # every reader must have read message seq - SLOTS (this slot's last)
         t0, spins = time.monotonic(), 0
-        while self.world > 1 and int(acks.min()) < seq:
+        while self.world > 1 and int(acks.min()) < need:
             spins += 1
             self._pause(spins)
             if spins % 4096 == 0 and time.monotonic() - t0 > timeout_s:
-                late = [r + 1 for r, a in enumerate(acks.tolist()) if a < seq]
-                raise ControlPlaneError(f"ranks {late} did not read control message {seq} within {timeout_s} s")
-        self.buf[PAYLOAD_OFF:PAYLOAD_OFF + len(data)] = data
-        self.hdr[1] = len(data)
-        self.hdr[2] = zlib.crc32(data)
+                late = [r + 1 for r, a in enumerate(acks.tolist()) if a < need]
+                raise ControlPlaneError(f"ranks {late} did not read control message {need - 1} within {timeout_s} s")
+        k = seq % SLOTS
+        off = PAYLOAD_OFF + k * self.slot_bytes
+        self.buf[off:off + len(data)] = data
+        self.hdr[LEN_OFF + k] = len(data)
+        self.hdr[CRC_OFF + k] = zlib.crc32(data)
         self.hdr[0] = seq + 1
 
     # -------------------------------------------------------------- readers
@@ -138,22 +147,25 @@ class ShmChannel:
         assert not self.owner
         writer = int(self.hdr[3])
         spins = 0
+        k = self.seen % SLOTS
+        off = PAYLOAD_OFF + k * self.slot_bytes
         while True:
-            seq = int(self.hdr[0])
-            if seq > self.seen:
-                n = int(self.hdr[1])
-                crc = int(self.hdr[2])
-                data = bytes(self.buf[PAYLOAD_OFF:PAYLOAD_OFF + n])
-                if zlib.crc32(data) == crc and int(self.hdr[0]) == seq:
+            if int(self.hdr[0]) > self.seen:
+                n = int(self.hdr[LEN_OFF + k])
+                crc = int(self.hdr[CRC_OFF + k])
+                data = bytes(self.buf[off:off + n])
+                # The writer cannot reuse this slot before this reader acks it, so a crc match is
+                # this message (a mismatch: published fields not all visible yet, read again).
+                if n <= self.slot_bytes and zlib.crc32(data) == crc:
                     break
-                continue  # published fields not all visible yet: read again
+                continue
             spins += 1
             self._pause(spins)
             if spins % 8192 == 0 and not _pid_alive(writer):
                 raise ControlPlaneError(f"rank 0 (pid {writer}) is gone")
-        self.seen = seq
+        self.seen += 1
         method, *args = pickle.loads(data)
-        self.hdr[8 + self.rank] = seq
+        self.hdr[8 + self.rank] = self.seen
         return method, args
 
     def close(self) -> None:

@@ -8,7 +8,7 @@ import time
 import numpy as np
 import pytest
 
-from hilda_vllm_b200.engine.control_plane import ControlPlaneError, ShmChannel
+from hilda_vllm_b200.engine.control_plane import SLOTS, ControlPlaneError, ShmChannel
 
 
 def _reader(name, rank, world, n, out, delay):
@@ -66,10 +66,11 @@ def test_writer_gives_up_when_a_reader_stops_reading():
     p = ctx.Process(target=_silent_reader, args=(ch.name, ready))
     p.start()
     assert ready.wait(60)
-    ch.send("first", 1)  # the buffer is free
+    for i in range(SLOTS):  # the writer may run SLOTS messages ahead of a reader
+        ch.send("early", i, timeout_s=0.5)
     t0 = time.monotonic()
     with pytest.raises(ControlPlaneError, match=r"ranks \[1\] did not read"):
-        ch.send("second", 2, timeout_s=0.5)
+        ch.send("one too many", 2, timeout_s=0.5)
     assert time.monotonic() - t0 < 20
     p.terminate()
     p.join(timeout=30)
