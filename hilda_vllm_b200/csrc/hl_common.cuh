@@ -141,23 +141,4 @@ __device__ __forceinline__ uint2 quant8_e4m3(uint4 v, float scale) {
   return make_uint2(out[0], out[1]);
 }
 
-// e4m3 byte of a value that e4m3 holds exactly, or of its truncation to the subnormal grid
-// (multiples of 2^-9) below 2^-6; |x| < 2^8.  Branch-free.
-__device__ __forceinline__ uint32_t e4m3_byte(float x) {
-  const uint32_t u = __float_as_uint(x);
-  const uint32_t sign = (u >> 24) & 0x80u;
-  const int e = int((u >> 23) & 0xffu) - 120;  // e4m3 biased exponent
-  const uint32_t m = (u >> 20) & 7u;
-  const int sh = 1 - e;                        // subnormal: (1.m) >> (1 - e), zero below 2^-9
-  const uint32_t sub = sh <= 4 ? (8u | m) >> sh : 0u;
-  return sign | (e >= 1 ? (uint32_t(e) << 3) | m : sub);
-}
-
-// The larger e4m3 term of x: x truncated to 4 significant bits, or to the subnormal grid.
-__device__ __forceinline__ float e4m3_head(float x) {
-  const float a = fabsf(x);
-  const float t = a >= 0.015625f ? __uint_as_float(__float_as_uint(a) & 0xfff00000u) : floorf(a * 512.f) * 0.001953125f;
-  return copysignf(t, x);
-}
-
 }  // namespace hl

@@ -173,44 +173,6 @@ __device__ __forceinline__ void merge_state(float (&m)[G], float (&l)[G], float2
   }
 }
 
-// Last CTA of sequence b: combines the n_splits partials (m, l, O) in split order.  Each thread
-// produces 8 consecutive output elements of one query head.
-template <int kHq>
-__device__ __forceinline__ void merge_splits(const DecodeParams& p, int b, int n_splits, const float2* ws_ml,
-                                             const float* ws_o, __nv_bfloat16* out_b, int tid) {
-  for (int idx = tid; idx < kHq * (kHeadDim / 8); idx += kDecodeThreads) {
-    const int hq = idx / (kHeadDim / 8);
-    const int d0 = (idx % (kHeadDim / 8)) * 8;
-    const int64_t row0 = int64_t(b) * p.max_splits * kHq + hq;
-    float mx = -INFINITY;
-    for (int s = 0; s < n_splits; ++s) mx = fmaxf(mx, __ldcg(&ws_ml[row0 + int64_t(s) * kHq]).x);
-    float lsum = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (mx != -INFINITY) {
-      for (int s = 0; s < n_splits; ++s) {
-        const int64_t row = row0 + int64_t(s) * kHq;
-        const float2 ml = __ldcg(&ws_ml[row]);
-        if (ml.x == -INFINITY) continue;
-        const float c = exp2f(ml.x - mx);
-        lsum += ml.y * c;
-        const float4* src = reinterpret_cast<const float4*>(ws_o + row * kHeadDim + d0);
-        const float4 a = __ldcg(src), bq = __ldcg(src + 1);
-        o[0] += a.x * c;
-        o[1] += a.y * c;
-        o[2] += a.z * c;
-        o[3] += a.w * c;
-        o[4] += bq.x * c;
-        o[5] += bq.y * c;
-        o[6] += bq.z * c;
-        o[7] += bq.w * c;
-      }
-    }
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-#pragma unroll
-    for (int d = 0; d < 8; ++d) o[d] *= inv;
-    *reinterpret_cast<uint4*>(out_b + hq * kHeadDim + d0) = pack_bf16x8(o);
-  }
-}
-
 template <bool B>
 struct BoolTag {
   static constexpr bool value = B;
@@ -532,396 +494,40 @@ paged_decode_kernel(const DecodeParams p) {
   if (!*flag_smem) return;
   __threadfence();
 
-  merge_splits<kHq>(p, b, n_splits, ws_ml, ws_o, out_b, tid);
+  // Last CTA of sequence b: combine the n_splits partials.  Each thread produces 8
+  // consecutive output elements of one query head.
+  for (int idx = tid; idx < kHq * (kHeadDim / 8); idx += kDecodeThreads) {
+    const int hq = idx / (kHeadDim / 8);
+    const int d0 = (idx % (kHeadDim / 8)) * 8;
+    const int64_t row0 = int64_t(b) * p.max_splits * kHq + hq;
+    float mx = -INFINITY;
+    for (int s = 0; s < n_splits; ++s) mx = fmaxf(mx, __ldcg(&ws_ml[row0 + int64_t(s) * kHq]).x);
+    float lsum = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (mx != -INFINITY) {
+      for (int s = 0; s < n_splits; ++s) {
+        const int64_t row = row0 + int64_t(s) * kHq;
+        const float2 ml = __ldcg(&ws_ml[row]);
+        if (ml.x == -INFINITY) continue;
+        const float c = exp2f(ml.x - mx);
+        lsum += ml.y * c;
+        const float4* src = reinterpret_cast<const float4*>(ws_o + row * kHeadDim + d0);
+        const float4 a = __ldcg(src), bq = __ldcg(src + 1);
+        o[0] += a.x * c;
+        o[1] += a.y * c;
+        o[2] += a.z * c;
+        o[3] += a.w * c;
+        o[4] += bq.x * c;
+        o[5] += bq.y * c;
+        o[6] += bq.z * c;
+        o[7] += bq.w * c;
+      }
+    }
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) o[d] *= inv;
+    *reinterpret_cast<uint4*>(out_b + hq * kHeadDim + d0) = pack_bf16x8(o);
+  }
   if (tid == 0) tickets[b] = 0;  // ready for the next launch
-}
-
-// ------------------------------------------------------------------------------------------
-// e4m3 caches, Hq/Hk <= 4, Hk in {4, 8}: the same split-K grid and pipeline, but the scores come
-// from warp-level e4m3 tensor-core MMAs.  The CUDA-core kernel above is instruction-bound on e4m3
-// bytes (each K byte is unpacked to fp32 and multiplied once per query head, then reduced across
-// a half-warp); an MMA consumes the staged e4m3 K rows as they are.
-//
-// Per tile, warp w takes 16 tokens of KV head w % Hk: S[16 x 8] = K[16 x 128] . B[128 x 8] with
-// four m16n8k32 MMAs, the A operand loaded from the staged rows by ldmatrix (rows padded by 16
-// bytes in shared memory, so the 8 rows of a matrix fall on different banks) and the B columns
-// = the G query heads as two e4m3 terms each: after an exact power-of-two shift that puts the
-// head's largest |q| in [2^7, 2^8), q1 = q truncated to 4 significant bits and q2 = q - q1 (column
-// 2j + term; the other columns are zero).  q1 + q2 reproduces every bf16 component within 2^8 of
-// the head's largest exactly, smaller ones to 2^-9 after the shift.  The MMA's fp32 accumulator
-// adds the two columns of a head; 2^-shift, k_scale and the softmax scale go into one multiplier.
-// The softmax state (m, l) is kept per warp (replicated in every lane); the probabilities go
-// through shared memory to the P.V update, which stays on CUDA cores: half-warp hw takes tokens
-// 8 hw .. 8 hw + 7, each lane 8 dims of the V row (e4m3 -> fp32, v_scale folded into the output).
-// ------------------------------------------------------------------------------------------
-template <int HK>
-struct MmaTraits {
-  static constexpr int kRow = HK * kHeadDim;        // bytes per token (e4m3), all local KV heads
-  static constexpr int kRowP = kRow + 16;           // padded shared-memory row
-  static constexpr int kPhases = 8 / HK;            // warps sharing a KV head
-  static constexpr int kT = 16 * kPhases;           // tokens per stage: 16 per warp
-  static constexpr int kStageB = kT * kRowP;        // bytes per K (or V) stage
-  static_assert(kSplit % kT == 0, "split must be a whole number of tiles");
-};
-
-template <int G, int HK>
-constexpr size_t mma_smem_bytes() {
-  return size_t(kStages) * 2 * MmaTraits<HK>::kStageB + kStages * sizeof(uint64_t) + 8 * 16 * 4 * sizeof(float) + 16;
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void mma_e4m3(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-template <int G, int HK>
-__global__ void __launch_bounds__(kDecodeThreads, 3) paged_decode_mma_kernel(const DecodeParams p) {
-  using Tr = MmaTraits<HK>;
-  constexpr int kRow = Tr::kRow;
-  constexpr int kRowP = Tr::kRowP;
-  constexpr int kT = Tr::kT;
-  constexpr int kStageB = Tr::kStageB;
-  constexpr int kHq = HK * G;
-  static_assert(G <= 4, "2G MMA columns must fit in 8");
-
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * 2 * kStageB);
-  float* pbuf = reinterpret_cast<float*>(full + kStages);  // [warp][16 tokens][4 heads]
-  int* flag_smem = reinterpret_cast<int*>(pbuf + 8 * 16 * 4);
-
-  const int split = blockIdx.x;
-  const int b = blockIdx.y;
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int g = lane >> 2;   // MMA group: token row g (and g + 8), B column g
-  const int t = lane & 3;    // thread in group: C columns 2t, 2t + 1 = head t's two terms
-  const int ln = lane & 15;  // P.V: dims [8 ln, 8 ln + 8)
-  const int hw = lane >> 4;  // P.V: tokens [8 hw, 8 hw + 8) of the warp's 16
-  const int h = warp % HK;
-  const int phase = warp / HK;
-
-  int32_t* ws_err = reinterpret_cast<int32_t*>(p.ws + kWsErrOff);
-  int32_t* tickets = reinterpret_cast<int32_t*>(p.ws + kWsTicketOff);
-  float2* ws_ml = reinterpret_cast<float2*>(p.ws + kWsMlOff);
-  float* ws_o = reinterpret_cast<float*>(
-      p.ws + kWsMlOff + align256(int64_t(p.batch) * p.max_splits * kHq * sizeof(float2)));
-
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  int L = p.context_lens[b];
-  const int Lmax = p.max_blocks * p.block_size;
-  L = L < 0 ? 0 : (L > Lmax ? Lmax : L);
-  const int n_splits = (L + kSplit - 1) / kSplit;
-  __nv_bfloat16* out_b = p.out + int64_t(b) * p.out_row_stride;
-  if (split >= n_splits) {
-    if (split == 0) {
-      for (int i = tid; i < kHq * kHeadDim / 8; i += kDecodeThreads)
-        reinterpret_cast<uint4*>(out_b)[i] = make_uint4(0, 0, 0, 0);
-    }
-    return;
-  }
-  const int tok0 = split * kSplit;
-  const int tok1 = min(L, tok0 + kSplit);
-  const int64_t block = p.block_tables[int64_t(b) * p.bt_stride + tok0 / p.block_size];
-  const bool bad_block = block < 0 || block >= p.num_blocks;
-  const int ntiles = (tok1 - tok0 + kT - 1) / kT;
-  const int64_t base_slot = block * p.block_size + (tok0 % p.block_size);
-  const uint8_t* kbase = p.k_cache + base_slot * kRow;
-  const uint8_t* vbase = p.v_cache + base_slot * kRow;
-
-  if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  // One bulk copy per token row (the destination rows are padded).
-  auto issue = [&](int i) {
-    const int st = i % kStages;
-    mbar_arrive_expect_tx(&full[st], 2 * kT * kRow);
-    for (int r = 0; r < kT; ++r) {
-      const int64_t src = (int64_t(i) * kT + r) * kRow;
-      bulk_g2s(smem + st * 2 * kStageB + r * kRowP, kbase + src, kRow, &full[st]);
-      bulk_g2s(smem + st * 2 * kStageB + kStageB + r * kRowP, vbase + src, kRow, &full[st]);
-    }
-  };
-  if (bad_block) {
-    if (tid == 0) atomicOr(ws_err, 2);
-  } else if (tid == 0) {
-    for (int i = 0; i < kStages && i < ntiles; ++i) issue(i);
-  }
-
-  // ---------------------------------------------------------------- Q as two e4m3 terms (B operand)
-  uint32_t bq[4][2];
-  float fh;  // the score multiplier of head t (2^-shift x k_scale x softmax scale x log2 e)
-  {
-    const int j = g >> 1;
-    const bool col = j < G;
-    const __nv_bfloat16* qh = p.q + int64_t(b) * p.q_row_stride + (h * G + (col ? j : 0)) * kHeadDim;
-    float qv[4][8];
-    float amax = 0.f;
-#pragma unroll
-    for (int bb = 0; bb < 4; ++bb)
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const uint2 v = *reinterpret_cast<const uint2*>(qh + 32 * bb + 16 * half + 4 * t);
-        qv[bb][4 * half + 0] = bf16lo(v.x);
-        qv[bb][4 * half + 1] = bf16hi(v.x);
-        qv[bb][4 * half + 2] = bf16lo(v.y);
-        qv[bb][4 * half + 3] = bf16hi(v.y);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) amax = fmaxf(amax, fabsf(qv[bb][4 * half + k]));
-      }
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));  // the 4 lanes of a group: 128 dims
-    const int e = int((__float_as_uint(amax) >> 23) & 0xffu) - 127;
-    int shift = amax > 0.f ? 7 - e : 0;  // largest |q| * 2^shift in [2^7, 2^8)
-    shift = shift > 126 ? 126 : shift;
-    const float up = __uint_as_float(uint32_t(shift + 127) << 23);
-    const float down = __uint_as_float(uint32_t(127 - shift) << 23);
-    const bool second = (g & 1) != 0;
-#pragma unroll
-    for (int bb = 0; bb < 4; ++bb)
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t w = 0;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float x = qv[bb][4 * half + k] * up;
-          const float hd = e4m3_head(x);
-          w |= e4m3_byte(second ? x - hd : hd) << (8 * k);
-        }
-        bq[bb][half] = col ? w : 0u;
-      }
-    const float ks = p.k_scale ? p.k_scale[h] : 1.f;
-    const float f = p.scale_log2 * ks * down;  // for head j (columns 2j, 2j + 1)
-    fh = __shfl_sync(0xffffffffu, f, 8 * (t < G ? t : 0));  // lane 8t holds column 2t: head t
-  }
-
-  float m[G], l[G];
-  float2 acc[G][4];
-#pragma unroll
-  for (int j = 0; j < G; ++j) {
-    m[j] = -INFINITY;
-    l[j] = 0.f;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) acc[j][c] = make_float2(0.f, 0.f);
-  }
-  float* pw = pbuf + warp * 16 * 4;
-  const uint32_t a_off = uint32_t(((lane & 7) + ((lane >> 3) & 1) * 8 + phase * 16) * kRowP + h * kHeadDim +
-                                  (lane >> 4) * 16);
-
-  bool timed_out = false;
-  if (!bad_block) {
-    for (int i = 0; i < ntiles; ++i) {
-      const int stage = i % kStages;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], (i / kStages) & 1));
-      if (ok) {
-        const uint8_t* Ks = smem + stage * 2 * kStageB;
-        const uint8_t* Vs = Ks + kStageB + (phase * 16) * kRowP + h * kHeadDim;
-        const int wtok = tok0 + i * kT + phase * 16;  // this warp's first token
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t abase = smem_u32(Ks) + a_off;
-#pragma unroll
-        for (int bb = 0; bb < 4; ++bb) {
-          uint32_t a[4];
-          ldsm_x4(abase + 32 * bb, a);
-          mma_e4m3(c, a, bq[bb][0], bq[bb][1]);
-        }
-        const bool v_lo = wtok + g < tok1, v_hi = wtok + g + 8 < tok1;
-        const float s_lo = v_lo ? (c[0] + c[1]) * fh : -INFINITY;
-        const float s_hi = v_hi ? (c[2] + c[3]) * fh : -INFINITY;
-        float mt = fmaxf(s_lo, s_hi);
-#pragma unroll
-        for (int o = 4; o <= 16; o <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
-        // Lane j (group 0) holds head j's tile maximum: update every lane's copy of (m, l, acc).
-        float mine = 0.f;
-#pragma unroll
-        for (int j = 0; j < G; ++j) {
-          const float mtj = __shfl_sync(0xffffffffu, mt, j);
-          if (mtj > m[j] + kLazyLog2) {  // also the first tile with a token (m = -inf)
-            const float corr = exp2f(m[j] - mtj);
-            l[j] *= corr;
-            const float2 c2 = make_float2(corr, corr);
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) acc[j][cc] = __fmul2_rn(acc[j][cc], c2);
-            m[j] = mtj;
-          }
-          if (t == j) mine = m[j];
-        }
-        float p_lo = 0.f, p_hi = 0.f;
-        if (t < G && mine != -INFINITY) {
-          p_lo = v_lo ? exp2f(s_lo - mine) : 0.f;
-          p_hi = v_hi ? exp2f(s_hi - mine) : 0.f;
-          pw[g * 4 + t] = p_lo;
-          pw[(g + 8) * 4 + t] = p_hi;
-        }
-        float ps = p_lo + p_hi;
-#pragma unroll
-        for (int o = 4; o <= 16; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-#pragma unroll
-        for (int j = 0; j < G; ++j) l[j] += __shfl_sync(0xffffffffu, ps, j);
-        __syncwarp();
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int tt = hw * 8 + k;
-          if (wtok + tt >= tok1) continue;  // never touch V rows past the context (may hold NaN bits)
-          const float4 pv = *reinterpret_cast<const float4*>(pw + tt * 4);
-          const float pj[4] = {pv.x, pv.y, pv.z, pv.w};
-          float2 vx[4];
-          load8x2<true>(Vs + tt * kRowP + 8 * ln, vx);
-#pragma unroll
-          for (int j = 0; j < G; ++j) {
-            const float2 p2 = make_float2(pj[j], pj[j]);
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) acc[j][cc] = __ffma2_rn(p2, vx[cc], acc[j][cc]);
-          }
-        }
-        __syncwarp();  // pbuf is rewritten by the next tile
-      }
-      if (__syncthreads_or(!ok)) {
-        timed_out = true;
-        break;
-      }
-      if (tid == 0 && i + kStages < ntiles) issue(i + kStages);
-    }
-  }
-  if (timed_out) {
-    if (tid == 0) {
-      atomicOr(ws_err, 1);
-      for (int i = 0; i < kStages; ++i) mbar_wait(&full[i], 0), mbar_wait(&full[i], 1);
-    }
-    return;
-  }
-
-  // The half-warps share (m, l): their accumulators add.
-#pragma unroll
-  for (int j = 0; j < G; ++j)
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-      acc[j][c] = make_float2(acc[j][c].x + __shfl_xor_sync(0xffffffffu, acc[j][c].x, 16),
-                              acc[j][c].y + __shfl_xor_sync(0xffffffffu, acc[j][c].y, 16));
-
-  // Warps that share a KV head (Hk = 4) merge through the now idle stage buffers.
-  if constexpr (Tr::kPhases > 1) {
-    __syncthreads();
-    float* scr = reinterpret_cast<float*>(smem);  // [warp][j][lane 0..15][10]
-    if (phase > 0 && hw == 0) {
-#pragma unroll
-      for (int j = 0; j < G; ++j) {
-        float* e = scr + ((warp * G + j) * 16 + ln) * 10;
-        e[0] = m[j];
-        e[1] = l[j];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          e[2 + 2 * c] = acc[j][c].x;
-          e[3 + 2 * c] = acc[j][c].y;
-        }
-      }
-    }
-    __syncthreads();
-    if (phase == 0) {
-      for (int ph = 1; ph < Tr::kPhases; ++ph) {
-        const int w2 = ph * HK + h;
-        float m2[G], l2[G];
-        float2 a2[G][4];
-#pragma unroll
-        for (int j = 0; j < G; ++j) {
-          const float* e = scr + ((w2 * G + j) * 16 + ln) * 10;
-          m2[j] = e[0];
-          l2[j] = e[1];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) a2[j][c] = make_float2(e[2 + 2 * c], e[3 + 2 * c]);
-        }
-        merge_state<G>(m, l, acc, m2, l2, a2);
-      }
-    }
-  }
-
-  const float vs = p.v_scale ? p.v_scale[h] : 1.0f;
-  if (n_splits == 1) {
-    if (phase == 0 && hw == 0) {
-#pragma unroll
-      for (int j = 0; j < G; ++j) {
-        const float inv = l[j] > 0.f ? vs / l[j] : 0.f;
-        float o[8];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          o[2 * c] = acc[j][c].x * inv;
-          o[2 * c + 1] = acc[j][c].y * inv;
-        }
-        *reinterpret_cast<uint4*>(out_b + (h * G + j) * kHeadDim + 8 * ln) = pack_bf16x8(o);
-      }
-    }
-    return;
-  }
-  if (phase == 0 && hw == 0) {
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const int hq = h * G + j;
-      const int64_t row = (int64_t(b) * p.max_splits + split) * kHq + hq;
-      float* o = ws_o + row * kHeadDim + 8 * ln;
-      reinterpret_cast<float4*>(o)[0] =
-          make_float4(acc[j][0].x * vs, acc[j][0].y * vs, acc[j][1].x * vs, acc[j][1].y * vs);
-      reinterpret_cast<float4*>(o)[1] =
-          make_float4(acc[j][2].x * vs, acc[j][2].y * vs, acc[j][3].x * vs, acc[j][3].y * vs);
-      if (ln == 0) ws_ml[row] = make_float2(m[j], l[j]);
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int prev = atomicAdd(&tickets[b], 1);
-    *flag_smem = (prev == n_splits - 1);
-  }
-  __syncthreads();
-  if (!*flag_smem) return;
-  __threadfence();
-  merge_splits<kHq>(p, b, n_splits, ws_ml, ws_o, out_b, tid);
-  if (tid == 0) tickets[b] = 0;
-}
-
-template <int G, int HK>
-int launch_decode_mma(const DecodeParams& p, cudaStream_t stream) {
-  constexpr size_t smem = mma_smem_bytes<G, HK>();
-  static std::atomic<bool> configured[kMaxDecodeDevices];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= kMaxDecodeDevices) {
-    set_error("hl_paged_decode: no usable current device");
-    return HL_ERR_CUDA;
-  }
-  if (!configured[dev].load(std::memory_order_acquire)) {
-    e = cudaFuncSetAttribute(paged_decode_mma_kernel<G, HK>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) {
-      set_error("hl_paged_decode: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
-      return HL_ERR_CUDA;
-    }
-    configured[dev].store(true, std::memory_order_release);
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.max_splits, p.batch);
-  cfg.blockDim = dim3(kDecodeThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, paged_decode_mma_kernel<G, HK>, p);
-  if (e != cudaSuccess) {
-    set_error("hl_paged_decode: launch failed: %s", cudaGetErrorString(e));
-    return HL_ERR_CUDA;
-  }
-  return HL_OK;
 }
 
 template <bool FP8, int G, int HK>
@@ -1125,11 +731,6 @@ int paged_decode_impl(bool allow_tc, const void* q, int64_t q_row_stride, const 
     return decode_tc_launch(q, q_row_stride, k_cache, v_cache, fp8, k_scale, v_scale, block_tables, bt_stride,
                             max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, block_size,
                             num_blocks, p.scale_log2, out, out_row_stride, workspace, s);
-  }
-  if (fp8 && (g == 1 || g == 2) && (num_kv_heads == 4 || num_kv_heads == 8)) {
-    // e4m3 scores on warp-level tensor-core MMAs (the CUDA-core unpacking is instruction-bound).
-    if (g == 1) return num_kv_heads == 8 ? launch_decode_mma<1, 8>(p, s) : launch_decode_mma<1, 4>(p, s);
-    return num_kv_heads == 8 ? launch_decode_mma<2, 8>(p, s) : launch_decode_mma<2, 4>(p, s);
   }
   if (fp8) return dispatch_g<true>(g, num_kv_heads, p, s);
   return dispatch_g<false>(g, num_kv_heads, p, s);
