@@ -320,6 +320,7 @@ def run_ours(args):
     if not args.no_e2e:
         fresh()
         runner.io_bytes = {"h2d": 0, "d2h": 0}
+        runner.gpu_wait_s = 0.0
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         outs = llm.generate(prompts, sp, use_tqdm=False)
@@ -332,7 +333,9 @@ def run_ours(args):
                "d2h_bytes_per_step": int(runner.io_bytes["d2h"] / n_steps),
                "wall_s": round(wall, 3), "output_tokens": n_out,
                "prefill_s": round(stats["prefill_time_s"], 4), "decode_s": round(stats["decode_time_s"], 3),
-               "decode_tok_s": round(stats["decode_throughput_toks"], 1)}
+               "decode_tok_s": round(stats["decode_throughput_toks"], 1),
+               "rank0_gpu_wait_s": round(runner.gpu_wait_s, 3),
+               "rank0_host_s": round(wall - runner.gpu_wait_s, 3)}
         # The same job sampled at temperature 0.6 (the reference's own benchmark setting,
         # benchmarks/bench.py:186-192): sampled on the device by the Gumbel-max kernel.
         fresh()

@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import os
 import pickle
+import time
 from multiprocessing.shared_memory import SharedMemory
 
 import numpy as np
@@ -158,6 +159,9 @@ class ModelRunner:
 
         self.external = getattr(config, "distributed_executor", "spawn") == "external"
         self.io_bytes = {"h2d": 0, "d2h": 0}
+        # Seconds the host spent blocked on the GPU for a step's tokens (rank 0); the rest of a
+        # job's wall time is host work (scheduling, packets, control plane) or idle GPU.
+        self.gpu_wait_s = 0.0
         self.recording: list[torch.Tensor] | None = None
         if self.world_size > 1 and not dist.is_initialized():
             port = int(os.getenv("MINI_VLLM_DIST_PORT", "2333"))
@@ -612,7 +616,9 @@ class ModelRunner:
 
     def collect_decode(self, handle) -> list[int]:
         par, bs = handle
+        t0 = time.perf_counter()
         self.done_events[par].synchronize()
+        self.gpu_wait_s += time.perf_counter() - t0
         if self.allreduce is not None:
             self.allreduce.check_errors()
         self._check_error_words(par)
@@ -737,7 +743,9 @@ class ModelRunner:
             self.allreduce.copy_error_word()
         self._queue_error_words(0)
         self.copy_done.record()
+        t0 = time.perf_counter()
         self.copy_done.synchronize()
+        self.gpu_wait_s += time.perf_counter() - t0
         if self.allreduce is not None:
             self.allreduce.check_errors()
         self._check_error_words(0)
