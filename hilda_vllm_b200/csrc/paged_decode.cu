@@ -76,16 +76,16 @@ struct DecodeParams {
 template <bool FP8, int G>
 constexpr int ctas_per_sm() { return G <= 2 ? 3 : (G <= 4 ? 2 : 1); }
 
-template <bool FP8, int HK>
+template <bool FP8, int HK, int SPLIT = kSplit>
 struct Traits {
   static constexpr int kElem = FP8 ? 1 : 2;
   static constexpr int kTileB = kTileBytes;  // bytes per K (and per V) stage
   static constexpr int kRowBytes = HK * kHeadDim * kElem;  // one token, all local KV heads
-  static constexpr int kT = kTileB / kRowBytes < kSplit ? kTileB / kRowBytes : kSplit;  // tokens per tile
+  static constexpr int kT = kTileB / kRowBytes < SPLIT ? kTileB / kRowBytes : SPLIT;  // tokens per tile
   static constexpr int kPhases = 8 / HK;                    // warps sharing one KV head
   static constexpr int kTPW = kT / kPhases;                 // tokens per warp per tile
   static constexpr int kTPH = kTPW / 2;                     // tokens per half-warp per tile
-  static_assert(kSplit % kT == 0, "split must be a whole number of tiles");
+  static_assert(SPLIT % kT == 0, "split must be a whole number of tiles");
   static_assert(kTPH >= 1, "tile too small");
 };
 
@@ -185,12 +185,12 @@ constexpr float kLazyLog2 = 8.f;
 
 // One staged tile of kT tokens for this warp's KV head: the half-warp's kTPH tokens, all G query
 // heads.  kFull: every token of the tile is inside the context (no per-token checks).
-template <bool FP8, int G, int HK, class FullTag>
+template <bool FP8, int G, int HK, int SPLIT, class FullTag>
 __device__ __forceinline__ void decode_tile(FullTag, const uint8_t* Ks, int tile_tok0, int tok1, int phase, int hw,
                                             int ln, int h, const float2 (&qs)[G][4], float (&m)[G], float (&l)[G],
                                             float2 (&acc)[G][4]) {
   constexpr bool kFull = FullTag::value;
-  using Tr = Traits<FP8, HK>;
+  using Tr = Traits<FP8, HK, SPLIT>;
   constexpr int kTPW = Tr::kTPW;
   constexpr int kTPH = Tr::kTPH;
   constexpr int kRow = Tr::kRowBytes;
@@ -258,10 +258,10 @@ __device__ __forceinline__ void decode_tile(FullTag, const uint8_t* Ks, int tile
   }
 }
 
-template <bool FP8, int G, int HK>
+template <bool FP8, int G, int HK, int SPLIT>
 __global__ void __launch_bounds__(kDecodeThreads, ctas_per_sm<FP8, G>())
 paged_decode_kernel(const DecodeParams p) {
-  using Tr = Traits<FP8, HK>;
+  using Tr = Traits<FP8, HK, SPLIT>;
   constexpr int kTileBytes = Tr::kTileB;
   constexpr int kT = Tr::kT;
   constexpr int kRow = Tr::kRowBytes;
@@ -294,7 +294,7 @@ paged_decode_kernel(const DecodeParams p) {
   int L = p.context_lens[b];
   const int Lmax = p.max_blocks * p.block_size;
   L = L < 0 ? 0 : (L > Lmax ? Lmax : L);
-  const int n_splits = (L + kSplit - 1) / kSplit;
+  const int n_splits = (L + SPLIT - 1) / SPLIT;
   __nv_bfloat16* out_b = p.out + int64_t(b) * p.out_row_stride;
 
   if (split >= n_splits) {
@@ -305,8 +305,8 @@ paged_decode_kernel(const DecodeParams p) {
     return;
   }
 
-  const int tok0 = split * kSplit;
-  const int tok1 = min(L, tok0 + kSplit);
+  const int tok0 = split * SPLIT;
+  const int tok1 = min(L, tok0 + SPLIT);
   const int page = tok0 / p.block_size;
   const int64_t block = p.block_tables[int64_t(b) * p.bt_stride + page];
   const bool bad_block = block < 0 || block >= p.num_blocks;
@@ -371,9 +371,9 @@ paged_decode_kernel(const DecodeParams p) {
         const uint8_t* Ks = smem + stage * 2 * kTileBytes;
         const int tile_tok0 = tok0 + t * kT;
         if (tile_tok0 + kT <= tok1)
-          decode_tile<FP8, G, HK>(BoolTag<true>{}, Ks, tile_tok0, tok1, phase, hw, ln, h, qs, m, l, acc);
+          decode_tile<FP8, G, HK, SPLIT>(BoolTag<true>{}, Ks, tile_tok0, tok1, phase, hw, ln, h, qs, m, l, acc);
         else
-          decode_tile<FP8, G, HK>(BoolTag<false>{}, Ks, tile_tok0, tok1, phase, hw, ln, h, qs, m, l, acc);
+          decode_tile<FP8, G, HK, SPLIT>(BoolTag<false>{}, Ks, tile_tok0, tok1, phase, hw, ln, h, qs, m, l, acc);
       }  // ok
       // Every warp is done with this stage: refill it (or leave together on a timeout).
       if (__syncthreads_or(!ok)) {
@@ -530,7 +530,7 @@ paged_decode_kernel(const DecodeParams p) {
   if (tid == 0) tickets[b] = 0;  // ready for the next launch
 }
 
-template <bool FP8, int G, int HK>
+template <bool FP8, int G, int HK, int SPLIT>
 int launch_decode(const DecodeParams& p, cudaStream_t stream) {
   constexpr size_t smem = size_t(kStages) * 2 * Traits<FP8, HK>::kTileB + kStages * sizeof(uint64_t) + 16;
   // The shared-memory opt-in is per device; the first call on a device happens before any graph
@@ -543,7 +543,8 @@ int launch_decode(const DecodeParams& p, cudaStream_t stream) {
     return HL_ERR_CUDA;
   }
   if (!configured[dev].load(std::memory_order_acquire)) {
-    e = cudaFuncSetAttribute(paged_decode_kernel<FP8, G, HK>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    e = cudaFuncSetAttribute(paged_decode_kernel<FP8, G, HK, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(smem));
     if (e != cudaSuccess) {
       set_error("hl_paged_decode: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
       return HL_ERR_CUDA;
@@ -562,7 +563,7 @@ int launch_decode(const DecodeParams& p, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, paged_decode_kernel<FP8, G, HK>, p);
+  e = cudaLaunchKernelEx(&cfg, paged_decode_kernel<FP8, G, HK, SPLIT>, p);
   if (e != cudaSuccess) {
     set_error("hl_paged_decode: launch failed: %s", cudaGetErrorString(e));
     return HL_ERR_CUDA;
@@ -570,33 +571,41 @@ int launch_decode(const DecodeParams& p, cudaStream_t stream) {
   return HL_OK;
 }
 
-template <bool FP8, int G>
+template <bool FP8, int G, int SPLIT>
 int dispatch_hk(int hk, const DecodeParams& p, cudaStream_t s) {
   switch (hk) {
-    case 1: return launch_decode<FP8, G, 1>(p, s);
-    case 2: return launch_decode<FP8, G, 2>(p, s);
-    case 4: return launch_decode<FP8, G, 4>(p, s);
-    case 8: return launch_decode<FP8, G, 8>(p, s);
+    case 1: return launch_decode<FP8, G, 1, SPLIT>(p, s);
+    case 2: return launch_decode<FP8, G, 2, SPLIT>(p, s);
+    case 4: return launch_decode<FP8, G, 4, SPLIT>(p, s);
+    case 8: return launch_decode<FP8, G, 8, SPLIT>(p, s);
   }
   set_error("hl_paged_decode: num_kv_heads=%d not in {1,2,4,8}", hk);
   return HL_ERR_UNSUPPORTED;
 }
 
-template <bool FP8>
+template <bool FP8, int SPLIT>
 int dispatch_g(int g, int hk, const DecodeParams& p, cudaStream_t s) {
   switch (g) {
-    case 1: return dispatch_hk<FP8, 1>(hk, p, s);
-    case 2: return dispatch_hk<FP8, 2>(hk, p, s);
-    case 4: return dispatch_hk<FP8, 4>(hk, p, s);
-    case 8: return dispatch_hk<FP8, 8>(hk, p, s);
+    case 1: return dispatch_hk<FP8, 1, SPLIT>(hk, p, s);
+    case 2: return dispatch_hk<FP8, 2, SPLIT>(hk, p, s);
+    case 4: return dispatch_hk<FP8, 4, SPLIT>(hk, p, s);
+    case 8: return dispatch_hk<FP8, 8, SPLIT>(hk, p, s);
   }
   set_error("hl_paged_decode: Hq/Hk=%d not in {1,2,4,8}", g);
   return HL_ERR_UNSUPPORTED;
 }
 
-int64_t max_splits_for(int max_blocks, int block_size) {
-  return (int64_t(max_blocks) * block_size + kSplit - 1) / kSplit;
+int64_t max_splits_for(int max_blocks, int block_size, int split = kSplit) {
+  return (int64_t(max_blocks) * block_size + split - 1) / split;
 }
+
+// Small launches (a few sequences) run with 32-token splits: the grid of 128-token splits would
+// leave most SMs idle (config 1: 8 sequences of up to 1024 tokens = 64 CTAs on 148 SMs), and a
+// split streams its tokens at the rate one CTA's pipeline allows.  The choice depends only on the
+// batch size and the block-table width, so a CUDA graph replays the same grid.
+constexpr int kSmallSplit = 32;
+constexpr int kSmallGridCtas = 296;  // 2 x the SMs of a B200
+
 
 }  // namespace
 }  // namespace hl
@@ -617,8 +626,14 @@ using namespace hl;
 extern "C" int64_t hl_paged_decode_workspace_size(int batch, int num_q_heads, int head_dim, int max_blocks_per_seq,
                                                   int block_size) {
   if (batch <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_blocks_per_seq <= 0 || block_size <= 0) return -1;
-  const int64_t S = max_splits_for(max_blocks_per_seq, block_size);
-  const int64_t rows = int64_t(batch) * S * num_q_heads;
+  // (sequence, split) partial slots: the 128-token grid's, or the small grid's, which runs only
+  // while batch x 128-token splits < kSmallGridCtas (bounded so the size grows with the batch).
+  const int64_t units = int64_t(batch) * max_splits_for(max_blocks_per_seq, block_size);
+  const int64_t units_small = int64_t(batch) * max_splits_for(max_blocks_per_seq, block_size, kSmallSplit);
+  const int64_t cap_small = int64_t(kSmallGridCtas) * (kSplit / kSmallSplit);
+  const int64_t u = units > (units_small < cap_small ? units_small : cap_small)
+                        ? units : (units_small < cap_small ? units_small : cap_small);
+  const int64_t rows = u * num_q_heads;
   const int64_t simt = kWsMlOff + align256(rows * int64_t(sizeof(float2))) + rows * head_dim * int64_t(sizeof(float));
   const int64_t tc = decode_tc_workspace_bytes(batch, num_q_heads);
   return simt > tc ? simt : tc;
@@ -687,7 +702,8 @@ int paged_decode_impl(bool allow_tc, const void* q, int64_t q_row_stride, const 
               (long long)workspace_bytes);
     return HL_ERR_WORKSPACE;
   }
-  const int64_t S = max_splits_for(max_blocks_per_seq, block_size);
+  const bool small = int64_t(batch) * max_splits_for(max_blocks_per_seq, block_size) < kSmallGridCtas;
+  const int64_t S = max_splits_for(max_blocks_per_seq, block_size, small ? kSmallSplit : kSplit);
   HL_CHECK_ARG(S <= 65535, "hl_paged_decode: too many splits");
 
   DecodeParams p;
@@ -732,8 +748,9 @@ int paged_decode_impl(bool allow_tc, const void* q, int64_t q_row_stride, const 
                             max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads, block_size,
                             num_blocks, p.scale_log2, out, out_row_stride, workspace, s);
   }
-  if (fp8) return dispatch_g<true>(g, num_kv_heads, p, s);
-  return dispatch_g<false>(g, num_kv_heads, p, s);
+  if (small) return fp8 ? dispatch_g<true, kSmallSplit>(g, num_kv_heads, p, s)
+                        : dispatch_g<false, kSmallSplit>(g, num_kv_heads, p, s);
+  return fp8 ? dispatch_g<true, kSplit>(g, num_kv_heads, p, s) : dispatch_g<false, kSplit>(g, num_kv_heads, p, s);
 }
 
 }  // namespace
