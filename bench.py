@@ -61,6 +61,8 @@ def parse():
                          "decode of configs[0]; c3: FP8 KV with a capped pool; c4: mixed chunked prefill + "
                          "decode with shared prefixes; c5: Qwen3-8B (TP over --gpus)")
     ap.add_argument("--kv", default="auto", choices=["auto", "fp8"], help="KV cache dtype for c5")
+    ap.add_argument("--tp-shard", type=int, default=1,
+                    help="decode-kernel profiles: the per-GPU head counts under tensor parallelism of this degree")
     ap.add_argument("--profile", default="",
                     choices=["", "decode-kernel", "decode-kernel-tc", "decode-steps", "prefill-kernel", "small-kernels",
                              "allreduce", "reference-kernels"],
@@ -886,6 +888,8 @@ def run_profile(args):
         if args.workload == "c5":
             hq = 32
             lens = torch.randint(256 + 256, 1024 + 256 + 1, (b,), generator=g)
+        if args.tp_shard > 1:  # one GPU's heads under tensor parallelism
+            hq, hk = hq // args.tp_shard, hk // args.tp_shard
         fp8 = args.kv == "fp8"
         nblk = [-(-int(n) // bs) for n in lens]
         perm = torch.randperm(sum(nblk), generator=g).tolist()
