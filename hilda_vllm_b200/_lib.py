@@ -97,6 +97,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "hl_varlen_prefill_read_errors": (c_int, [c_vp]),
     "hl_varlen_prefill_copy_errors_async": (c_int, [c_vp, c_vp]),
+    "hl_varlen_prefill_clear_errors": (c_int, [c_vp]),
     "hl_pack_decode_batch": (
         c_int,
         [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_vp],

@@ -1003,3 +1003,16 @@ extern "C" int hl_varlen_prefill_copy_errors_async(int32_t* dst, void* stream) {
   }
   return HL_OK;
 }
+
+extern "C" int hl_varlen_prefill_clear_errors(void* stream) {
+  clear_error();
+  const int32_t zero = 0;
+  cudaError_t e = cudaMemcpyToSymbolAsync(g_prefill_errors, &zero, sizeof(int32_t), 0, cudaMemcpyHostToDevice,
+                                          static_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("hl_varlen_prefill_clear_errors: %s", cudaGetErrorString(e));
+    return HL_ERR_CUDA;
+  }
+  return HL_OK;
+}

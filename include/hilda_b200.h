@@ -210,6 +210,9 @@ int hl_varlen_prefill_read_errors(int32_t* errors_out);
  * so a caller can fetch them together with a step's other results without an extra sync. */
 int hl_varlen_prefill_copy_errors_async(int32_t* dst, void* stream);
 
+/* Clears the prefill error word (after a caller has handled it); synchronises `stream`. */
+int hl_varlen_prefill_clear_errors(void* stream);
+
 /* ------------------------------------------------------------------------------------
  * Decode-batch packing on the GPU.
  * Replaces the host loop of ModelRunner.prepare_decode and its block-table row sync,

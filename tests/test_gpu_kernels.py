@@ -585,6 +585,29 @@ def test_prefill_tensor_core_large_scores_rescale(precise, one_head):
         assert int(over.sum()) <= max(1, err.numel() // 100000) and float(err.max()) < 4e-2
 
 
+def test_prefill_block_outside_the_pool_sets_error_bit():
+    """A key tile whose block id lies outside the pool reads zeros (TMA fill, no fault) and sets
+    bit 1 of the prefill error word; clearing the word restores zero."""
+    from hilda_vllm_b200 import _lib
+    g = torch.Generator().manual_seed(77)
+    hq, hk, bs, nb = 16, 8, 256, 8
+    k, v, bt, _ = make_paged(g, 1, hk, 128, nb, bs, [600])
+    bad = bt.clone()
+    bad[0, 1] = nb + 3
+    cuq = torch.tensor([0, 88], dtype=torch.int32)
+    cuk = torch.tensor([0, 600], dtype=torch.int32)
+    q = torch.randn(88, hq, 128, generator=g).bfloat16()
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.hl_varlen_prefill_clear_errors(stream) == 0
+    kernels.varlen_prefill(q.to(DEV), k.to(DEV), v.to(DEV), cuq.to(DEV), cuk.to(DEV), 88, 600, 128 ** -0.5,
+                           block_table=bad.to(DEV))
+    torch.cuda.synchronize()
+    assert kernels.prefill_errors() & 2
+    assert lib.hl_varlen_prefill_clear_errors(stream) == 0
+    assert kernels.prefill_errors() == 0
+
+
 @pytest.mark.parametrize("one_head", [False, True])
 def test_prefill_tensor_core_paged_with_prefix_chunks(one_head):
     g = torch.Generator().manual_seed(41)
