@@ -143,7 +143,7 @@ def test_decode_config1_shapes():
 EDGE_LENS = [0, 1, 2, 127, 128, 129, 255, 256, 257, 511, 512, 1000, 1024, 1025, 2047, 3000, 4096]
 
 
-@pytest.mark.parametrize("hq,hk", [(16, 8), (32, 8), (8, 8), (16, 4), (8, 2), (8, 1), (64, 8), (4, 4)])
+@pytest.mark.parametrize("hq,hk", [(16, 8), (32, 8), (8, 8), (16, 4), (8, 2), (8, 1), (64, 8), (4, 4), (2, 1)])
 def test_decode_gqa_layouts_and_edge_lengths(hq, hk):
     g = torch.Generator().manual_seed(hq * 10 + hk)
     lens = EDGE_LENS
