@@ -440,15 +440,21 @@ __global__ void __launch_bounds__(kThreads, 1) varlen_prefill_tc_kernel(const __
 // columns, P_lo in the next 64 with SPLIT_P) and the PV product reads them straight from TMEM
 // as the A operand (tcgen05.mma with [a-tmem]), so P never touches shared memory.
 //   warp 0     TMA producer (both Q tiles once, then K+V tiles into a 2-stage ring)
-//   warp 1     TMEM allocator + MMA issuer, in ping-pong order per key tile j:
-//                PV_a(j), QK_a(j+1), PV_b(j), QK_b(j+1)
-//              so the tensor core works on one head while the other head's softmax runs.
-//   warps 2-3  idle
+//   warp 1     TMEM allocator; its lane 0 alone is the MMA issuer, in ping-pong order per key
+//              tile j:  PV_a(j), QK_a(j+1), PV_b(j), QK_b(j+1)
+//              so the tensor core works on one head while the other head's softmax runs.  The
+//              tensor pipe takes an M128 x N128 x K16 instruction every 64 cycles, so the issuer
+//              does as little as possible between MMAs: descriptors are built once and a K step
+//              adds a constant to the start-address field.
+//   warps 2-3  zero the V rows past the sequence in the last key tile
 //   warps 4-7  softmax of head a (thread = query row = TMEM lane; warp w reads TMEM lanes
 //              32 * (w % 4) ..), warps 8-11 softmax of head b.
+// Waiting roles sleep in mbarrier.try_wait with a suspend-time hint instead of spinning, which
+// leaves the issue slots (and the power budget: the kernel runs at the 1 kW cap when timed for
+// more than a few ms) to the warps that work.
 // Registers: the kernel launches with 168 per thread (384 x 168 = 64512 of the SM's 65536);
-// warpgroup 0 (warps 0-3) gives back down to 56 with setmaxnreg.dec and the two softmax
-// warpgroups take them with setmaxnreg.inc to 224 (128 x 56 + 256 x 224 = 64512), so a whole
+// warpgroup 0 (warps 0-3) gives back down to 120 with setmaxnreg.dec and the two softmax
+// warpgroups take them with setmaxnreg.inc to 192 (128 x 120 + 256 x 192 = 64512), so a whole
 // 128-key S row stays in registers.
 // O is rescaled lazily: the running reference max only moves when a tile's max exceeds it by
 // more than kRescaleLog2 (probabilities then stay <= 2^kRescaleLog2, exact in bf16 range),
@@ -518,20 +524,40 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Bounded mbarrier wait that also gives up as soon as another role has raised the abort flag.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr uint32_t kSuspendHintNs = 100000;        // longest sleep of one try_wait
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // a wait gives up after 2 s
+
+// Bounded mbarrier wait: the thread sleeps inside try_wait until the phase completes (or the
+// hint elapses), so waiting warps take no issue slots.  Gives up as soon as another role has
+// raised the abort flag, or after kWaitLimitNs of global time (error bit 0).
 __device__ __forceinline__ bool wait2(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < kMaxWaitPolls; ++i) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(addr), "r"(parity)
+        : "r"(addr), "r"(parity), "r"(kSuspendHintNs)
         : "memory");
     if (done) return true;
-    if ((i & 63u) == 63u && *abort_flag) return false;
+    if ((i & 15u) == 15u) {
+      if (*abort_flag) return false;
+      const uint64_t now = global_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        break;
+      }
+    }
   }
   *abort_flag = 1;
   atomicOr(&g_prefill_errors, 1);
@@ -550,6 +576,8 @@ __global__ void __launch_bounds__(kThreads2, 1) varlen_prefill_pair_kernel(const
   uint64_t* s_full = bars + 5;    // [2] heads
   uint64_t* p_full = bars + 7;    // [2] heads
   uint64_t* o_done = bars + 9;
+  uint64_t* v_land = bars + 10;   // the last key tile's TMA landed (MMA issuer -> warps 2-3)
+  uint64_t* v_zero = bars + 11;   // its V rows past the sequence are zeroed (warps 2-3 -> issuer)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13);
 
@@ -582,6 +610,8 @@ __global__ void __launch_bounds__(kThreads2, 1) varlen_prefill_pair_kernel(const
       mbar_init(&p_full[i], 128);   // every softmax thread of head i wrote its P row
     }
     mbar_init(o_done, 1);
+    mbar_init(v_land, 1);
+    mbar_init(v_zero, 64);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -595,7 +625,7 @@ __global__ void __launch_bounds__(kThreads2, 1) varlen_prefill_pair_kernel(const
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 120;");
   }
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -634,89 +664,101 @@ __global__ void __launch_bounds__(kThreads2, 1) varlen_prefill_pair_kernel(const
       for (int t = issued >= 2 ? issued - 2 : 0; t < issued; ++t) mbar_wait(&kv_full[t & 1], (t >> 1) & 1);
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (n_tiles > 0) {
+    // ---------------------------------------------------------------- MMA issuer (lane 0)
+    if (n_tiles > 0 && lane == 0) {
+      // A 16-wide K step only moves a descriptor's start-address field (bits 0-13 = address
+      // >> 4; every address here is below 256 KiB, so the field never carries), so each MMA
+      // adds a compile-time constant to one of these.
+      const uint64_t dq0 = smem_desc(sbase + kOff2Qa, 16, 1024), dq1 = smem_desc(sbase + kOff2Qb, 16, 1024);
+      const uint64_t dk0 = smem_desc(sbase + kOff2K, 16, 1024), dk1 = smem_desc(sbase + kOff2K + 2 * kTile, 16, 1024);
+      const uint64_t dv0 = smem_desc(sbase + kOff2K + kTile, kHalf, 1024);
+      const uint64_t dv1 = smem_desc(sbase + kOff2K + 3 * kTile, kHalf, 1024);
       auto qk = [&](int j, int h) {
-        const uint32_t qbase = sbase + (h ? kOff2Qb : kOff2Qa);
-        const uint32_t kbase = sbase + kOff2K + (j & 1) * 2 * kTile;
+        const uint64_t a0 = h ? dq1 : dq0;
+        const uint64_t b0 = (j & 1) ? dk1 : dk0;
+        const uint32_t d = tmem + h * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t a = smem_desc(qbase + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-          const uint64_t b = smem_desc(kbase + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-          umma_bf16(tmem + h * 128, a, b, kIdescS, kk > 0 ? 1u : 0u);
+          const uint64_t off = uint64_t(((kk >> 2) * kHalf + (kk & 3) * 32) >> 4);
+          umma_bf16(d, a0 + off, b0 + off, kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(smem_u32(&s_full[h]));
       };
       auto pv = [&](int j, int h) {
-        const uint32_t vbase = sbase + kOff2K + (j & 1) * 2 * kTile + kTile;
+        const uint64_t b0 = (j & 1) ? dv1 : dv0;
         const uint32_t pcol = tmem + h * 128;
         const uint32_t ocol = tmem + kColO + h * 128;
+        const uint32_t first = j > 0 ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t b = smem_desc(vbase + kk * 16 * 128, kHalf, 1024);
-          umma_bf16_ts(ocol, pcol + kk * 8, b, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16_ts(ocol, pcol + kk * 8, b0 + uint64_t((kk * 16 * 128) >> 4), kIdescPV, kk > 0 ? 1u : first);
         if constexpr (SPLIT_P) {
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t b = smem_desc(vbase + kk * 16 * 128, kHalf, 1024);
-            umma_bf16_ts(ocol, pcol + 64 + kk * 8, b, kIdescPV, 1u);
-          }
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16_ts(ocol, pcol + 64 + kk * 8, b0 + uint64_t((kk * 16 * 128) >> 4), kIdescPV, 1u);
         }
       };
-      bool ok = __all_sync(0xffffffffu, wait2(q_full, 0, abort_flag) && wait2(&kv_full[0], 0, abort_flag));
-      if (ok && lane == 0) {
+      // The last key tile reaches past the sequence: warps 2-3 zero its V rows past Lk once its
+      // TMA has landed (signalled here), and PV waits for that.
+      const bool tail_partial = (n_tiles - 1) * kBN + kBN > Lk;
+      auto landed = [&](int t) {
+        if (tail_partial && t == n_tiles - 1) mbar_arrive(v_land);
+      };
+      bool ok = wait2(q_full, 0, abort_flag) && wait2(&kv_full[0], 0, abort_flag);
+      if (ok) {
+        landed(0);
         tc_fence_after();
         qk(0, 0);
         qk(0, 1);
       }
-      __syncwarp();
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int st = j & 1;
-        ok = __all_sync(0xffffffffu, wait2(&p_full[0], j & 1, abort_flag));
+        ok = wait2(&p_full[0], j & 1, abort_flag);
         if (!ok) break;
-        const int j0 = j * kBN;
-        if (j0 + kBN > Lk) {
-          // Last, partial tile: zero the V rows past the sequence so that P = 0 never meets a
-          // non-finite cache value inside the MMA (the tile's TMA landed before its QK).
-          uint8_t* vs = smem + kOff2K + st * 2 * kTile + kTile;
-          for (int rr = max(Lk - j0, 0) + lane; rr < kBN; rr += 32) {
-            uint4* v0 = reinterpret_cast<uint4*>(vs + rr * 128);
-            uint4* v1 = reinterpret_cast<uint4*>(vs + kHalf + rr * 128);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-        }
-        if (lane == 0) {
-          tc_fence_after();
-          pv(j, 0);
-        }
-        if (j + 1 < n_tiles) {
-          ok = __all_sync(0xffffffffu, wait2(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag));
+        if (tail_partial && j == n_tiles - 1) {
+          ok = wait2(v_zero, 0, abort_flag);
           if (!ok) break;
-          if (lane == 0) qk(j + 1, 0);
         }
-        ok = __all_sync(0xffffffffu, wait2(&p_full[1], j & 1, abort_flag));
+        tc_fence_after();
+        pv(j, 0);
+        if (j + 1 < n_tiles) {
+          ok = wait2(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag);
+          if (!ok) break;
+          landed(j + 1);
+          qk(j + 1, 0);
+        }
+        ok = wait2(&p_full[1], j & 1, abort_flag);
         if (!ok) break;
-        if (lane == 0) {
-          tc_fence_after();
-          pv(j, 1);
-          umma_commit(smem_u32(&kv_empty[st]));
-          if (j + 1 < n_tiles) qk(j + 1, 1);
+        tc_fence_after();
+        pv(j, 1);
+        umma_commit(smem_u32(&kv_empty[st]));
+        if (j + 1 < n_tiles) qk(j + 1, 1);
+      }
+      umma_commit(smem_u32(o_done));
+      if (!ok) mbar_wait(o_done, 0);  // let issued MMAs finish before TMEM is freed
+    }
+    __syncwarp();
+  } else if (warp == 2 || warp == 3) {
+    // ---------------------------------------------------------------- tail V rows
+    // Zero the V rows past the sequence in the last, partial key tile so that P = 0 never
+    // meets a non-finite cache value inside the MMA (rows of a cache block nobody wrote).
+    const int jl = n_tiles - 1;
+    if (n_tiles > 0 && jl * kBN + kBN > Lk) {
+      if (wait2(v_land, 0, abort_flag)) {
+        uint8_t* vs = smem + kOff2K + (jl & 1) * 2 * kTile + kTile;
+        for (int rr = max(Lk - jl * kBN, 0) + (threadIdx.x - 64); rr < kBN; rr += 64) {
+          uint4* v0 = reinterpret_cast<uint4*>(vs + rr * 128);
+          uint4* v1 = reinterpret_cast<uint4*>(vs + kHalf + rr * 128);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
         }
-        __syncwarp();
+        fence_proxy_async_smem();
       }
-      if (lane == 0) {
-        umma_commit(smem_u32(o_done));
-        if (!ok) mbar_wait(o_done, 0);  // let issued MMAs finish before TMEM is freed
-      }
-      __syncwarp();
+      mbar_arrive(v_zero);
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- softmax + epilogue
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 192;");
     const int h = (warp - 4) >> 2;   // 0: head a, 1: head b
     const int quarter = warp & 3;    // TMEM lanes [32 * quarter, +32) belong to this warp
     const int r = quarter * 32 + lane;
