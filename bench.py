@@ -313,7 +313,10 @@ def run_ours(args):
                 "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one config-2 mid-job launch "
                                    "(bench.py --profile decode-kernel), 1.028x algorithmic, scaled to this run's "
                                    "average launch") if ncu_ratio else None,
-                "kernel": f"paged_decode_kernel<bf16,G={g_ratio},Hk={hk}>",
+                # hl_paged_decode runs the tensor-core kernel from GQA 4 on, and for one KV head per
+                # GPU at GQA 2 (tensor parallelism over all KV heads).
+                "kernel": (f"paged_decode_tc_kernel<G={g_ratio},bf16>" if g_ratio >= 4 or (hk == 1 and g_ratio == 2)
+                           else f"paged_decode_kernel<bf16,G={g_ratio},Hk={hk}>"),
                 "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "of fallback (6650 GB/s)",
                 "samples": len(samples), "avg_launch_us": round(1e6 * ktime / max(1, len(samples)), 2),
                 "bytes_per_launch_avg": int(kbytes / max(1, len(samples)))}
@@ -583,13 +586,13 @@ def allreduce_profile(args):
             out = torch.empty_like(res)
 
             def fused():
-                ar.two_shot = False
+                ar.force_two_shot = False
                 for i in range(calls):
                     ar.output(i % 2, rows).copy_(part)
                     ar.add_rmsnorm(i % 2, rows, res, w, 1e-6, out)
 
             def fused_2shot():
-                ar.two_shot = True
+                ar.force_two_shot = True
                 for i in range(calls):
                     ar.output(i % 2, rows).copy_(part)
                     ar.add_rmsnorm(i % 2, rows, res, w, 1e-6, out)

@@ -855,17 +855,25 @@ class ModelRunner:
 
         for _ in range(3):
             launch()
+        reps = 20
+        # The launches replay from a CUDA graph, as in a decode step: issued from Python one by
+        # one, a launch of a few tens of microseconds (one GPU's heads under tensor parallelism)
+        # would be timed at the host's issue rate instead.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                launch()
+        graph.replay()
         stream = torch.cuda.current_stream()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = 20
         # Nothing in flight before the start event: the decode kernel is a programmatic dependent
-        # launch and would otherwise begin under the last warm-up launch's tail.
+        # launch and would otherwise begin under the previous launch's tail.
         torch.cuda.synchronize()
         e0.record(stream)
-        for _ in range(reps):
-            launch()
+        graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
+        del graph
         lens = ctx.tolist()
         nbytes = sum(lens) * hk * d * elem * 2 + bs * hq * d * 2 * 2
         return nbytes, e0.elapsed_time(e1) / 1e3 / reps

@@ -87,10 +87,8 @@ class NvlinkAllReduce:
         self._peer_data = [arr(*ptrs[0]), arr(*ptrs[1])]
         self._peer_signal = arr(*ptrs[2])
         self._peer_result = arr(*ptrs[3])
-        # More than two ranks: the two-shot kernel (each rank reduces 1/world of the rows and pushes
-        # them to all), whose NVLink traffic does not grow with the rank count.
-        self.two_shot = world > 2
         self._buf_ptrs = own[:2]
+        self.force_two_shot: bool | None = None
         self.buffers = [torch.as_tensor(_DeviceArray(p, (max_rows, hidden), "<i2"), device=device).view(torch.bfloat16)
                         for p in own[:2]]
         self.error_host = torch.zeros(1, dtype=torch.int32, pin_memory=True, device="cpu")
@@ -104,13 +102,26 @@ class NvlinkAllReduce:
 
     # ------------------------------------------------------------------ use
     def fits(self, rows: int) -> bool:
-        """Whether this batch takes the fused path (decode batches up to the buffers' rows).  At
-        two ranks the one-shot kernel (each rank reads the other's rows) beat NCCL + RMSNorm on
-        B200 (56 calls in a graph, 256 rows: 7.8 vs 18.3 us at hidden 1024, 14.9 vs 27.8 at 4096);
-        from three ranks on the two-shot kernel runs, whose traffic per rank stays below twice the
-        rows (the one-shot kernel's grows with world - 1: 72.7 vs NCCL's 40.8 us at 8 ranks and
-        hidden 4096)."""
+        """Whether this batch takes the fused path (decode batches up to the buffers' rows).  On
+        B200 (56 calls in a graph) the faster fused kernel beats NCCL + RMSNorm at every measured
+        shape: two ranks, 256 rows: 7.8 vs 18.3 us (hidden 1024), 14.9 vs 27.8 (hidden 4096);
+        four and eight ranks: see two_shot()."""
         return 0 < rows <= min(self.max_rows, 512)
+
+    def two_shot(self, rows: int) -> bool:
+        """The two-shot kernel (each rank reduces 1/world of the rows and pushes them to all) once
+        the one-shot kernel would pull more than 6 MiB from its peers, counting at least 128 rows
+        (below that the one-shot kernel has few CTAs and is latency-bound): the one-shot kernel's
+        traffic grows with world - 1, the two-shot kernel's does not, but it waits on a second
+        barrier.  B200, us per call (one-shot / two-shot / NCCL + RMSNorm):
+          4 ranks  hidden 1024 rows 256:  9.3 / 14.0 / 22.7   hidden 4096 rows  64: 22.1 / 22.5 / 25.2
+                                                                hidden 4096 rows 256: 29.7 / 25.1 / 32.9
+          8 ranks  hidden 1024 rows  64: 10.8 / 15.9 / 32.2   hidden 4096 rows  64: 40.7 / 31.0 / 36.4
+                   hidden 1024 rows 256: 15.7 / 16.7 / 34.3   hidden 4096 rows 256: 68.8 / 35.2 / 40.8
+        `force_two_shot` (None, True or False) overrides the choice, for tests and profiles."""
+        if self.force_two_shot is not None:
+            return self.force_two_shot
+        return self.world > 2 and (self.world - 1) * max(rows, 128) * self.hidden * 2 > (6 << 20)
 
     def output(self, slot: int, rows: int) -> torch.Tensor:
         """Where the row-parallel GEMM of `slot` writes its partial sums for `rows` rows."""
@@ -134,7 +145,7 @@ class NvlinkAllReduce:
             out = torch.empty_like(residual)
         stream = torch.cuda.current_stream(residual.device).cuda_stream
         self.stats["calls"] += 1
-        if self.two_shot:
+        if self.two_shot(rows):
             check(self.lib.hl_allreduce_add_rmsnorm_2shot(
                 ctypes.addressof(self._peer_data[slot]), ctypes.addressof(self._peer_result),
                 ctypes.addressof(self._peer_signal), self.world, self.rank, rows, self.hidden, residual.data_ptr(),

@@ -36,7 +36,7 @@ def _reference(partials, residual, weight, eps):
 def test_single_rank_equals_add_rmsnorm(rows, hidden, two_shot):
     g = torch.Generator().manual_seed(rows + hidden)
     ar = NvlinkAllReduce(0, 1, 512, hidden, torch.device(DEV))
-    ar.two_shot = two_shot
+    ar.force_two_shot = two_shot
     try:
         w = (torch.rand(hidden, generator=g) + 0.5).bfloat16().to(DEV)
         for slot in (0, 1, 0):
@@ -99,7 +99,7 @@ def _worker(rank, world, port, q, two_shot, hidden, rows):
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 device_id=torch.device("cuda", rank))
         ar = NvlinkAllReduce(rank, world, 512, hidden, torch.device("cuda", rank), timeout_s=10.0)
-        ar.two_shot = two_shot
+        ar.force_two_shot = two_shot
         w = (torch.arange(hidden, device="cuda") % 7 + 1).bfloat16() / 4
         results = []
         for call in range(6):
