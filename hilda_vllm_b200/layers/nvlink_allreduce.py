@@ -7,7 +7,9 @@ output straight into a buffer every peer has mapped (CUDA IPC), and the next RMS
 hl_allreduce_add_rmsnorm: one kernel that meets the peers at a flag barrier, reads the rows of
 all ranks over NVLink, sums them in rank order and applies the add + RMSNorm.  Two buffers
 alternate (o_proj -> slot 0, down_proj -> slot 1), which is what lets the kernel use a single
-barrier per call.  Batches larger than the buffers (prefill) keep NCCL.
+barrier per call.  From three ranks on, wide rows take hl_allreduce_add_rmsnorm_2shot instead
+(each rank reduces 1/world of the rows, pushes them to every rank, second barrier).  Batches
+larger than the buffers (prefill) keep NCCL.
 
 All ranks must make the same calls in the same order; the decision to use the buffers depends
 only on the row count, which is identical on every rank.
@@ -34,6 +36,12 @@ def active() -> "NvlinkAllReduce | None":
 def set_active(ar: "NvlinkAllReduce | None") -> None:
     global _ACTIVE
     _ACTIVE = ar
+
+
+def prefer_two_shot(world: int, rows: int, hidden: int) -> bool:
+    """True when the one-shot kernel would pull more than 5 MiB of bf16 partial sums from its
+    peers, counting at least 128 rows (see NvlinkAllReduce.two_shot for the measurements)."""
+    return world > 2 and (world - 1) * max(rows, 128) * hidden * 2 > (5 << 20)
 
 
 class _DeviceArray:
@@ -110,7 +118,7 @@ class NvlinkAllReduce:
 
     def two_shot(self, rows: int) -> bool:
         """The two-shot kernel (each rank reduces 1/world of the rows and pushes them to all) once
-        the one-shot kernel would pull more than 6 MiB from its peers, counting at least 128 rows
+        the one-shot kernel would pull more than 5 MiB from its peers, counting at least 128 rows
         (below that the one-shot kernel has few CTAs and is latency-bound): the one-shot kernel's
         traffic grows with world - 1, the two-shot kernel's does not, but it waits on a second
         barrier.  B200, us per call (one-shot / two-shot / NCCL + RMSNorm):
@@ -121,7 +129,7 @@ class NvlinkAllReduce:
         `force_two_shot` (None, True or False) overrides the choice, for tests and profiles."""
         if self.force_two_shot is not None:
             return self.force_two_shot
-        return self.world > 2 and (self.world - 1) * max(rows, 128) * self.hidden * 2 > (6 << 20)
+        return prefer_two_shot(self.world, rows, self.hidden)
 
     def output(self, slot: int, rows: int) -> torch.Tensor:
         """Where the row-parallel GEMM of `slot` writes its partial sums for `rows` rows."""

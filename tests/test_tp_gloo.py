@@ -150,3 +150,20 @@ def test_merge_shard_argmax_ties_pick_lowest_global_index():
         idxs.append(i + 2 * s)
     merged = merge_shard_argmax(torch.stack(vals), torch.stack(idxs))
     assert merged.tolist() == logits.argmax(-1).tolist() == [1, 0, 2]
+
+
+def test_all_reduce_kernel_choice_follows_measured_costs():
+    """One-shot vs two-shot fused all-reduce, against the B200 measurements (us per call,
+    one-shot / two-shot): the two-shot kernel is chosen exactly where it was the faster one, or
+    within 2 %."""
+    from hilda_vllm_b200.layers.nvlink_allreduce import prefer_two_shot
+
+    measured = {  # (world, rows, hidden): (one-shot us, two-shot us)
+        (4, 256, 1024): (9.3, 14.0), (4, 64, 4096): (22.1, 22.5), (4, 256, 4096): (29.7, 25.1),
+        (8, 64, 1024): (10.8, 15.9), (8, 256, 1024): (15.7, 16.7), (8, 64, 4096): (40.7, 31.0),
+        (8, 256, 4096): (68.8, 35.2),
+    }
+    for (world, rows, hidden), (one, two) in measured.items():
+        chosen = two if prefer_two_shot(world, rows, hidden) else one
+        assert chosen <= 1.02 * min(one, two), (world, rows, hidden)
+    assert not prefer_two_shot(1, 512, 8192) and not prefer_two_shot(2, 512, 8192)
