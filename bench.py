@@ -60,7 +60,8 @@ def parse():
                     help="c2 (default, the headline): BASELINE configs[1]; c1: the single-op KV store + paged "
                          "decode of configs[0]; c3: FP8 KV with a capped pool; c4: mixed chunked prefill + "
                          "decode with shared prefixes; c5: Qwen3-8B (TP over --gpus)")
-    ap.add_argument("--kv", default="auto", choices=["auto", "fp8"], help="KV cache dtype for c5")
+    ap.add_argument("--kv", default="auto", choices=["auto", "bf16", "fp8"],
+                    help="KV cache dtype for c5 (auto = bf16, the model dtype)")
     ap.add_argument("--tp-shard", type=int, default=1,
                     help="decode-kernel profiles: the per-GPU head counts under tensor parallelism of this degree")
     ap.add_argument("--profile", default="",
@@ -1109,9 +1110,9 @@ def run_workload(args):
                    for _ in range(256)]
         params = [SamplingParams(greedy=True, max_tokens=512, ignore_eos=True)] * 256
         kw = dict(max_num_seqs=256, max_model_len=1024 + 512 + 256, max_num_batched_tokens=16384,
-                  kv_cache_dtype=args.kv, gpu_memory_utilization=0.85)
+                  kv_cache_dtype="fp8" if args.kv == "fp8" else "auto", gpu_memory_utilization=0.85)
         cfg = ROOT / "hilda_vllm_b200" / "model_configs" / "qwen3-8b"
-        desc = f"qwen3-8b, 256 seqs, prompt U[256,1024], 512 greedy, {args.kv} KV, tp{args.gpus}"
+        desc = f"qwen3-8b, 256 seqs, prompt U[256,1024], 512 greedy, {'fp8' if args.kv == 'fp8' else 'bf16'} KV, tp{args.gpus}"
     fields, llm = _engine_e2e(args, cfg, prompts, params, **kw)
     if fields is None:
         return
