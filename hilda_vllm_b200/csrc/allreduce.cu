@@ -78,123 +78,6 @@ __device__ __forceinline__ int load_acquire_sys(const int* p) {
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// One warp per row, NV = hidden / 256 16-byte vectors per lane (lane + 32 c), the same layout
-// and summation order as the add + RMSNorm kernel, so one rank reproduces it bit for bit.
-template <int NV>
-__global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(const __grid_constant__ ArParams p) {
-  __shared__ int s_epoch;
-  __shared__ int s_ok;
-  const int blk = blockIdx.x;
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-
-  // ---------------------------------------------------------------- barrier with the peers
-  if (tid == 0) {
-    s_epoch = p.epochs[blk] + 1;
-    s_ok = 1;
-  }
-  __syncthreads();
-  const int epoch = s_epoch;
-  if (tid < p.world && tid != p.rank) {
-    store_flag_sys(p.signal[tid] + blk * kArMaxRanks + p.rank, epoch);
-    const int* mine = p.signal[p.rank] + blk * kArMaxRanks + tid;
-    const unsigned long long t0 = global_ns();
-    bool arrived = false;
-    for (uint32_t it = 0;; ++it) {
-      if (load_acquire_sys(mine) >= epoch) {
-        arrived = true;
-        break;
-      }
-      if ((it & 255u) == 255u && global_ns() - t0 > p.timeout_ns) break;
-    }
-    if (!arrived) {
-      s_ok = 0;
-      atomicOr(p.error_word, HL_AR_TIMEOUT);
-    }
-  }
-  __syncthreads();
-  const bool ok = s_ok != 0;
-  if (tid == 0) p.epochs[blk] = epoch;
-
-  // ---------------------------------------------------------------- rows of this CTA
-  constexpr int kRowsPerCta = kArThreads / 32;
-  // Ranks whose rows are loaded together: every load of a group is issued before any is used,
-  // so a group costs one NVLink round trip.
-  constexpr int RG = NV <= 4 ? 4 : (NV <= 8 ? 2 : 1);
-  for (int row = blk * kRowsPerCta + warp; row < p.rows; row += gridDim.x * kRowsPerCta) {
-    const int64_t base = int64_t(row) * p.hidden + 8 * lane;
-    uint4 rv[NV];
-#pragma unroll
-    for (int c = 0; c < NV; ++c) rv[c] = *reinterpret_cast<const uint4*>(p.residual + base + 256 * c);
-    float buf[NV][8];
-#pragma unroll
-    for (int c = 0; c < NV; ++c)
-#pragma unroll
-      for (int t = 0; t < 8; ++t) buf[c][t] = 0.f;
-    if (ok) {
-      for (int r0 = 0; r0 < p.world; r0 += RG) {
-        uint4 a[RG][NV];
-#pragma unroll
-        for (int g = 0; g < RG; ++g)
-          if (r0 + g < p.world)
-#pragma unroll
-            for (int c = 0; c < NV; ++c)
-              // Peer partials change between calls at the same addresses: no L1 caching.
-              a[g][c] = __ldcv(reinterpret_cast<const uint4*>(p.data[r0 + g] + base + 256 * c));
-#pragma unroll
-        for (int g = 0; g < RG; ++g)
-          if (r0 + g < p.world)
-#pragma unroll
-            for (int c = 0; c < NV; ++c) {
-              const uint32_t w[4] = {a[g][c].x, a[g][c].y, a[g][c].z, a[g][c].w};
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                buf[c][2 * t] = __fadd_rn(buf[c][2 * t], bf16lo(w[t]));
-                buf[c][2 * t + 1] = __fadd_rn(buf[c][2 * t + 1], bf16hi(w[t]));
-              }
-            }
-      }
-    }
-    // x = bf16(all-reduce) + residual (fp32), residual := bf16(x)  (add_rms_forward order)
-    float ss = 0.f;
-#pragma unroll
-    for (int c = 0; c < NV; ++c) {
-      const uint32_t rw[4] = {rv[c].x, rv[c].y, rv[c].z, rv[c].w};
-      uint32_t ro[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        buf[c][2 * t] = __fadd_rn(bf16_round(buf[c][2 * t]), bf16lo(rw[t]));
-        buf[c][2 * t + 1] = __fadd_rn(bf16_round(buf[c][2 * t + 1]), bf16hi(rw[t]));
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(buf[c][2 * t], buf[c][2 * t + 1]);
-        ro[t] = *reinterpret_cast<uint32_t*>(&h2);
-      }
-      *reinterpret_cast<uint4*>(p.residual + base + 256 * c) = make_uint4(ro[0], ro[1], ro[2], ro[3]);
-#pragma unroll
-      for (int t = 0; t < 8; ++t) ss = fmaf(buf[c][t], buf[c][t], ss);
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(ss / float(p.hidden) + p.eps);
-#pragma unroll
-    for (int c = 0; c < NV; ++c) {
-      const int col = 8 * (lane + 32 * c);
-      const uint4 wv = *reinterpret_cast<const uint4*>(p.weight + col);
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float a = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t], inv)), bf16lo(ww[t]));
-        const float b = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t + 1], inv)), bf16hi(ww[t]));
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
-        o[t] = *reinterpret_cast<uint32_t*>(&h2);
-      }
-      *reinterpret_cast<uint4*>(p.out + int64_t(row) * p.out_stride + col) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-  }
-}
-
-
 // Barrier of this CTA with the same CTA of every peer on flag bank `bank`: thread t < world
 // (t != rank) writes the epoch into peer t's slot for this rank and polls its own slot for peer t.
 // Returns false (and records HL_AR_TIMEOUT) if a peer did not arrive in time.
@@ -227,15 +110,160 @@ __device__ __forceinline__ bool cta_barrier(const ArParams& p, int bank, int epo
   return *s_ok != 0;
 }
 
+// Work split.  The peer reads are done in units of 1024 elements of one row (32 lanes x 4
+// 16-byte vectors); a warp issues the loads of a unit from every rank at once, so a unit costs one
+// NVLink round trip whatever the rank count.  A CTA takes a group of rows_per_cta() rows and its
+// four warps share the group's units; the add + RMSNorm then runs one warp per row, with the
+// row in registers in the add + RMSNorm kernel's layout and order (lane owns the vectors
+// lane + 32 c), so one rank reproduces that kernel bit for bit.
+constexpr int kUnitElems = 1024;
+
+__host__ __device__ constexpr int rows_per_cta(int hidden) { return hidden <= 1024 ? 4 : (hidden <= 2048 ? 2 : 1); }
+
+// bf16(sum over ranks, in rank order, in fp32) of the ncv 8-element vectors this lane owns in one
+// unit; `off` = row * hidden + unit * 1024 + 8 * lane.  Peer partials change between calls at the
+// same addresses: no L1 caching.
+__device__ __forceinline__ void reduce_unit(const ArParams& p, int64_t off, int ncv, uint4 (&sum)[4]) {
+  uint4 a[kArMaxRanks][4];
+#pragma unroll
+  for (int r = 0; r < kArMaxRanks; ++r)
+    if (r < p.world)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c < ncv) a[r][c] = __ldcv(reinterpret_cast<const uint4*>(p.data[r] + off + 256 * c));
+  float buf[4][8];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int t = 0; t < 8; ++t) buf[c][t] = 0.f;
+#pragma unroll
+  for (int r = 0; r < kArMaxRanks; ++r)
+    if (r < p.world)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c < ncv) {
+          const uint32_t w[4] = {a[r][c].x, a[r][c].y, a[r][c].z, a[r][c].w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            buf[c][2 * t] = __fadd_rn(buf[c][2 * t], bf16lo(w[t]));
+            buf[c][2 * t + 1] = __fadd_rn(buf[c][2 * t + 1], bf16hi(w[t]));
+          }
+        }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(buf[c][2 * t], buf[c][2 * t + 1]);
+      o[t] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+    sum[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// residual[row] := bf16(sums + residual[row]) (fp32 add); out[row] = bf16(bf16(x * rsqrt(mean(x^2)
+// + eps)) * weight), x the fp32 sum: the add_rms_forward order.  `sums` points at the row's
+// all-reduced bf16 values (shared memory, or the two-shot result buffer, read past L1); `zero`
+// treats them as zeros (a peer wait timed out).
+template <int NV>
+__device__ __forceinline__ void add_rmsnorm_row(const ArParams& p, int row, const __nv_bfloat16* sums,
+                                                bool from_global, bool zero) {
+  const int lane = threadIdx.x & 31;
+  const int64_t base = int64_t(row) * p.hidden + 8 * lane;
+  float buf[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NV; ++c) {
+    const uint4 rv = *reinterpret_cast<const uint4*>(p.residual + base + 256 * c);
+    const uint4* sp = reinterpret_cast<const uint4*>(sums + 8 * lane + 256 * c);
+    const uint4 sv = zero ? make_uint4(0, 0, 0, 0) : (from_global ? __ldcv(sp) : *sp);
+    const uint32_t w[4] = {sv.x, sv.y, sv.z, sv.w};
+    const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+    uint32_t ro[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      buf[c][2 * t] = __fadd_rn(bf16lo(w[t]), bf16lo(rw[t]));
+      buf[c][2 * t + 1] = __fadd_rn(bf16hi(w[t]), bf16hi(rw[t]));
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(buf[c][2 * t], buf[c][2 * t + 1]);
+      ro[t] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+    *reinterpret_cast<uint4*>(p.residual + base + 256 * c) = make_uint4(ro[0], ro[1], ro[2], ro[3]);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) ss = fmaf(buf[c][t], buf[c][t], ss);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = rsqrtf(ss / float(p.hidden) + p.eps);
+#pragma unroll
+  for (int c = 0; c < NV; ++c) {
+    const int col = 8 * (lane + 32 * c);
+    const uint4 wv = *reinterpret_cast<const uint4*>(p.weight + col);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float a = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t], inv)), bf16lo(ww[t]));
+      const float b = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t + 1], inv)), bf16hi(ww[t]));
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
+      o[t] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+    *reinterpret_cast<uint4*>(p.out + int64_t(row) * p.out_stride + col) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// One-shot: every rank reads every rank's partial sums of all rows.  The units of a row group
+// are reduced into shared memory (bf16 sums, [rows_per_cta][hidden]), then one warp per row
+// applies the add + RMSNorm.
+template <int NV>
+__global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(const __grid_constant__ ArParams p) {
+  extern __shared__ __align__(16) __nv_bfloat16 s_sums[];
+  __shared__ int s_epoch;
+  __shared__ int s_ok;
+  const int blk = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  if (tid == 0) {
+    s_epoch = p.epochs[blk] + 1;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const int epoch = s_epoch;
+  const bool ok = cta_barrier<false>(p, 0, epoch, &s_ok);
+  if (tid == 0) p.epochs[blk] = epoch;
+
+  const int rpc = rows_per_cta(p.hidden);
+  const int units = (p.hidden + kUnitElems - 1) / kUnitElems;
+  for (int row0 = blk * rpc; row0 < p.rows; row0 += gridDim.x * rpc) {
+    const int nr = min(rpc, p.rows - row0);
+    if (ok) {
+      for (int w = warp; w < nr * units; w += kArThreads / 32) {
+        const int rl = w / units;
+        const int u = w - rl * units;
+        const int ncv = min(4, (p.hidden - u * kUnitElems) / 256);
+        uint4 sum[4];
+        reduce_unit(p, int64_t(row0 + rl) * p.hidden + u * kUnitElems + 8 * lane, ncv, sum);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (c < ncv)
+            *reinterpret_cast<uint4*>(s_sums + rl * p.hidden + u * kUnitElems + 8 * lane + 256 * c) = sum[c];
+      }
+    }
+    __syncthreads();
+    if (warp < nr) add_rmsnorm_row<NV>(p, row0 + warp, s_sums + warp * p.hidden, false, !ok);
+    __syncthreads();  // the next group reuses s_sums
+  }
+}
+
 // Two-shot variant for more than two ranks: each rank reduces only the rows it owns (row r is
 // owned by rank r % world), reading them from every rank, and pushes the bf16 sum into every
 // rank's result buffer; after a second barrier (released at system scope, because it announces
 // this kernel's own remote stores) every rank reads all rows' sums from its local result buffer
 // and applies the add + RMSNorm.  Per call and rank the NVLink traffic is 2 (world - 1) / world
 // of the rows instead of the one-shot's (world - 1) x the rows, for one more barrier.  The sums
-// are taken in rank order, as in the one-shot kernel, so both give bit-identical results.
-// A CTA works on the same rows in both phases (warp w: rows blk * 4 + w + k * grid * 4), so the
-// second barrier is again between equal CTA indices.
+// are taken in rank order, as in the one-shot kernel, so both give bit-identical results.  A CTA
+// works on the same row groups in both phases, so the second barrier is again between equal CTA
+// indices.
 template <int NV>
 __global__ void __launch_bounds__(kArThreads) ar2_add_rmsnorm_kernel(const __grid_constant__ ArParams p) {
   __shared__ int s_epoch;
@@ -254,109 +282,38 @@ __global__ void __launch_bounds__(kArThreads) ar2_add_rmsnorm_kernel(const __gri
   bool ok = cta_barrier<false>(p, 0, epoch, &s_ok);
   if (tid == 0) p.epochs[blk] = epoch;
 
-  constexpr int kRowsPerCta = kArThreads / 32;
-  constexpr int RG = NV <= 4 ? 4 : (NV <= 8 ? 2 : 1);
+  const int rpc = rows_per_cta(p.hidden);
+  const int units = (p.hidden + kUnitElems - 1) / kUnitElems;
   // ---------------------------------------------------------------- phase 1: owned rows
   if (ok) {
-    for (int row = blk * kRowsPerCta + warp; row < p.rows; row += gridDim.x * kRowsPerCta) {
-      if (row % p.world != p.rank) continue;
-      const int64_t base = int64_t(row) * p.hidden + 8 * lane;
-      float buf[NV][8];
+    for (int row0 = blk * rpc; row0 < p.rows; row0 += gridDim.x * rpc) {
+      const int nr = min(rpc, p.rows - row0);
+      for (int w = warp; w < nr * units; w += kArThreads / 32) {
+        const int rl = w / units;
+        const int u = w - rl * units;
+        const int row = row0 + rl;
+        if (row % p.world != p.rank) continue;
+        const int ncv = min(4, (p.hidden - u * kUnitElems) / 256);
+        const int64_t off = int64_t(row) * p.hidden + u * kUnitElems + 8 * lane;
+        uint4 sum[4];
+        reduce_unit(p, off, ncv, sum);
+        for (int r = 0; r < p.world; ++r)
 #pragma unroll
-      for (int c = 0; c < NV; ++c)
-#pragma unroll
-        for (int t = 0; t < 8; ++t) buf[c][t] = 0.f;
-      for (int r0 = 0; r0 < p.world; r0 += RG) {
-        uint4 a[RG][NV];
-#pragma unroll
-        for (int g = 0; g < RG; ++g)
-          if (r0 + g < p.world)
-#pragma unroll
-            for (int c = 0; c < NV; ++c)
-              a[g][c] = __ldcv(reinterpret_cast<const uint4*>(p.data[r0 + g] + base + 256 * c));
-#pragma unroll
-        for (int g = 0; g < RG; ++g)
-          if (r0 + g < p.world)
-#pragma unroll
-            for (int c = 0; c < NV; ++c) {
-              const uint32_t w[4] = {a[g][c].x, a[g][c].y, a[g][c].z, a[g][c].w};
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                buf[c][2 * t] = __fadd_rn(buf[c][2 * t], bf16lo(w[t]));
-                buf[c][2 * t + 1] = __fadd_rn(buf[c][2 * t + 1], bf16hi(w[t]));
-              }
-            }
+          for (int c = 0; c < 4; ++c)
+            if (c < ncv) *reinterpret_cast<uint4*>(p.result[r] + off + 256 * c) = sum[c];
       }
-      uint4 sum[NV];
-#pragma unroll
-      for (int c = 0; c < NV; ++c) {
-        uint32_t o[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(buf[c][2 * t], buf[c][2 * t + 1]);
-          o[t] = *reinterpret_cast<uint32_t*>(&h2);
-        }
-        sum[c] = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-      for (int r = 0; r < p.world; ++r)
-#pragma unroll
-        for (int c = 0; c < NV; ++c) *reinterpret_cast<uint4*>(p.result[r] + base + 256 * c) = sum[c];
     }
   }
   __syncthreads();
   ok = ok && cta_barrier<true>(p, 1, epoch, &s_ok);
 
   // ---------------------------------------------------------------- phase 2: add + RMSNorm
-  const __nv_bfloat16* mine = p.result[p.rank];
-  for (int row = blk * kRowsPerCta + warp; row < p.rows; row += gridDim.x * kRowsPerCta) {
-    const int64_t base = int64_t(row) * p.hidden + 8 * lane;
-    float buf[NV][8];
-    uint4 rv[NV];
-#pragma unroll
-    for (int c = 0; c < NV; ++c) {
-      rv[c] = *reinterpret_cast<const uint4*>(p.residual + base + 256 * c);
-      // Pushed by the row's owner in this call: not cached in L1 from an earlier call.
-      const uint4 sv = ok ? __ldcv(reinterpret_cast<const uint4*>(mine + base + 256 * c)) : make_uint4(0, 0, 0, 0);
-      const uint32_t w[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        buf[c][2 * t] = bf16lo(w[t]);
-        buf[c][2 * t + 1] = bf16hi(w[t]);
-      }
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int c = 0; c < NV; ++c) {
-      const uint32_t rw[4] = {rv[c].x, rv[c].y, rv[c].z, rv[c].w};
-      uint32_t ro[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        buf[c][2 * t] = __fadd_rn(buf[c][2 * t], bf16lo(rw[t]));
-        buf[c][2 * t + 1] = __fadd_rn(buf[c][2 * t + 1], bf16hi(rw[t]));
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(buf[c][2 * t], buf[c][2 * t + 1]);
-        ro[t] = *reinterpret_cast<uint32_t*>(&h2);
-      }
-      *reinterpret_cast<uint4*>(p.residual + base + 256 * c) = make_uint4(ro[0], ro[1], ro[2], ro[3]);
-#pragma unroll
-      for (int t = 0; t < 8; ++t) ss = fmaf(buf[c][t], buf[c][t], ss);
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(ss / float(p.hidden) + p.eps);
-#pragma unroll
-    for (int c = 0; c < NV; ++c) {
-      const int col = 8 * (lane + 32 * c);
-      const uint4 wv = *reinterpret_cast<const uint4*>(p.weight + col);
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float a = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t], inv)), bf16lo(ww[t]));
-        const float b = __fmul_rn(bf16_round(__fmul_rn(buf[c][2 * t + 1], inv)), bf16hi(ww[t]));
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
-        o[t] = *reinterpret_cast<uint32_t*>(&h2);
-      }
-      *reinterpret_cast<uint4*>(p.out + int64_t(row) * p.out_stride + col) = make_uint4(o[0], o[1], o[2], o[3]);
+  // Sums pushed by the rows' owners in this call: read past L1.
+  for (int row0 = blk * rpc; row0 < p.rows; row0 += gridDim.x * rpc) {
+    const int nr = min(rpc, p.rows - row0);
+    if (warp < nr) {
+      const int row = row0 + warp;
+      add_rmsnorm_row<NV>(p, row, p.result[p.rank] + int64_t(row) * p.hidden, true, !ok);
     }
   }
 }
@@ -466,10 +423,8 @@ int allreduce_launch(void* const* peer_data, void* const* peer_result, void* con
   HL_CHECK_ARG(aligned16(residual) && aligned16(weight) && aligned16(out) && out_stride % 8 == 0,
                "hl_allreduce_add_rmsnorm: 16-byte alignment required");
   HL_CHECK_ARG(timeout_ns > 0, "hl_allreduce_add_rmsnorm: timeout must be positive");
-  // Two-shot: a CTA must see the same rows in every call (row r -> CTA r / 4), which holds while
-  // one pass of the grid covers all rows.
-  HL_CHECK_ARG(!peer_result || rows <= kArMaxBlocks * (kArThreads / 32),
-               "hl_allreduce_add_rmsnorm_2shot: at most %d rows", kArMaxBlocks * (kArThreads / 32));
+  // Decode batches: the flag barrier and the row groups are per CTA, at most kArMaxBlocks CTAs.
+  HL_CHECK_ARG(!peer_result || rows <= 512, "hl_allreduce_add_rmsnorm_2shot: at most 512 rows");
   ArParams prm;
   memset(&prm, 0, sizeof(prm));
   for (int r = 0; r < world; ++r) {
@@ -494,15 +449,17 @@ int allreduce_launch(void* const* peer_data, void* const* peer_result, void* con
   prm.epochs = epochs;
   prm.error_word = error_word;
   prm.timeout_ns = static_cast<unsigned long long>(timeout_ns);
-  const int groups = (rows + kArThreads / 32 - 1) / (kArThreads / 32);
+  const int rpc = rows_per_cta(hidden);
+  const int groups = (rows + rpc - 1) / rpc;
   const int blocks = groups < kArMaxBlocks ? groups : kArMaxBlocks;
+  const size_t sums_bytes = size_t(rpc) * hidden * sizeof(__nv_bfloat16);  // <= 16 KiB
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define HL_AR_CASE(NV)                                                 \
-  case NV:                                                             \
-    if (peer_result)                                                   \
-      ar2_add_rmsnorm_kernel<NV><<<blocks, kArThreads, 0, s>>>(prm);   \
-    else                                                               \
-      ar_add_rmsnorm_kernel<NV><<<blocks, kArThreads, 0, s>>>(prm);    \
+#define HL_AR_CASE(NV)                                                          \
+  case NV:                                                                      \
+    if (peer_result)                                                            \
+      ar2_add_rmsnorm_kernel<NV><<<blocks, kArThreads, 0, s>>>(prm);            \
+    else                                                                        \
+      ar_add_rmsnorm_kernel<NV><<<blocks, kArThreads, sums_bytes, s>>>(prm);    \
     break;
   switch (hidden / 256) {
     HL_AR_CASE(1) HL_AR_CASE(2) HL_AR_CASE(3) HL_AR_CASE(4) HL_AR_CASE(5) HL_AR_CASE(6) HL_AR_CASE(8)

@@ -32,7 +32,7 @@ def _reference(partials, residual, weight, eps):
 
 
 @pytest.mark.parametrize("two_shot", [False, True])
-@pytest.mark.parametrize("rows,hidden", [(1, 1024), (256, 1024), (300, 4096)])
+@pytest.mark.parametrize("rows,hidden", [(1, 1024), (256, 1024), (300, 4096), (37, 2560), (512, 8192)])
 def test_single_rank_equals_add_rmsnorm(rows, hidden, two_shot):
     g = torch.Generator().manual_seed(rows + hidden)
     ar = NvlinkAllReduce(0, 1, 512, hidden, torch.device(DEV))
@@ -128,7 +128,8 @@ def _worker(rank, world, port, q, two_shot, hidden, rows):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("two_shot,hidden,rows", [(False, 1024, 256), (True, 1024, 256), (True, 4096, 300)])
+@pytest.mark.parametrize("two_shot,hidden,rows", [(False, 1024, 256), (True, 1024, 256), (True, 4096, 300),
+                                                   (False, 4096, 256), (False, 2560, 37), (True, 2560, 37)])
 def test_ranks_bit_exact_and_identical(two_shot, hidden, rows):
     """All GPUs of the box (up to 8) as ranks, one-shot and two-shot kernels: every rank's output
     and residual equal bf16(sum of partials in rank order) + add + RMSNorm bit for bit."""
