@@ -84,6 +84,61 @@ def test_missing_peer_times_out_with_error_word():
     assert float((torch.ones(3, device=DEV) * 2).sum()) == 6.0
 
 
+@pytest.mark.parametrize("two_shot", [False, True])
+@pytest.mark.parametrize("world,rank,hidden,rows", [(4, 1, 1024, 256), (8, 3, 1024, 256), (8, 5, 4096, 256),
+                                                    (8, 0, 2560, 37), (4, 2, 4096, 300)])
+def test_emulated_ranks_on_one_gpu(two_shot, world, rank, hidden, rows):
+    """`world` ranks emulated in one process on one GPU: every peer's partial sums, flags and
+    result buffer are local buffers, and this rank's own flag area is set in advance so that no
+    wait blocks (nothing waits on another kernel).  The kernel's multi-rank arithmetic (the sum in
+    rank order over all ranks, the two-shot kernel's owned rows and pushes) must give
+    bf16(sum of partials) + add + RMSNorm bit for bit; the two-shot kernel reads the rows other
+    ranks own from this rank's result buffer, which the test fills with the expected sums."""
+    lib = _lib.load()
+    g = torch.Generator().manual_seed(world * 1000 + hidden + rows)
+    partials = [torch.randn(rows, hidden, generator=g).bfloat16().to(DEV) for _ in range(world)]
+    res = torch.randn(rows, hidden, generator=g).bfloat16().to(DEV)
+    w = (torch.rand(hidden, generator=g) + 0.5).bfloat16().to(DEV)
+    want_y, want_r = _reference(partials, res, w, 1e-6)
+    sums = torch.zeros(rows, hidden, dtype=torch.float32, device=DEV)
+    for p in partials:
+        sums += p.float()
+    sums = sums.bfloat16()
+    owned = torch.tensor([r % world == rank for r in range(rows)], device=DEV)
+    sig_bytes = int(lib.hl_allreduce_signal_bytes())
+    sig = [torch.zeros(sig_bytes // 4, dtype=torch.int32, device=DEV) for _ in range(world)]
+    sig[rank].fill_(1 << 30)  # every peer "arrived" long ago, on both flag banks
+    results = [torch.zeros(rows, hidden, dtype=torch.bfloat16, device=DEV) for _ in range(world)]
+    results[rank][~owned] = sums[~owned]
+    epochs = torch.zeros(128, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = torch.empty_like(res)
+    arr = ctypes.c_void_p * world
+    peer_data = arr(*[p.data_ptr() for p in partials])
+    peer_sig = arr(*[x.data_ptr() for x in sig])
+    peer_res = arr(*[x.data_ptr() for x in results])
+    stream = torch.cuda.current_stream().cuda_stream
+    if two_shot:
+        rc = lib.hl_allreduce_add_rmsnorm_2shot(ctypes.addressof(peer_data), ctypes.addressof(peer_res),
+                                                ctypes.addressof(peer_sig), world, rank, rows, hidden, res.data_ptr(),
+                                                w.data_ptr(), out.data_ptr(), out.stride(0), 1e-6, epochs.data_ptr(),
+                                                err.data_ptr(), 2_000_000_000, stream)
+    else:
+        rc = lib.hl_allreduce_add_rmsnorm(ctypes.addressof(peer_data), ctypes.addressof(peer_sig), world, rank, rows,
+                                          hidden, res.data_ptr(), w.data_ptr(), out.data_ptr(), out.stride(0), 1e-6,
+                                          epochs.data_ptr(), err.data_ptr(), 2_000_000_000, stream)
+    kernels.check(rc, "hl_allreduce_add_rmsnorm")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(out.view(torch.int16), want_y.view(torch.int16))
+    assert torch.equal(res.view(torch.int16), want_r.view(torch.int16))
+    if two_shot:  # this rank pushed exactly its own rows' sums to every rank
+        for r in range(world):
+            assert torch.equal(results[r][owned].view(torch.int16), sums[owned].view(torch.int16))
+            if r != rank:
+                assert not (results[r][~owned].float() != 0).any()
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
