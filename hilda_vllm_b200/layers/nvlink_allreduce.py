@@ -39,9 +39,9 @@ def set_active(ar: "NvlinkAllReduce | None") -> None:
 
 
 def prefer_two_shot(world: int, rows: int, hidden: int) -> bool:
-    """True when the one-shot kernel would pull more than 5 MiB of bf16 partial sums from its
+    """True when the one-shot kernel would pull more than 10 MiB of bf16 partial sums from its
     peers, counting at least 128 rows (see NvlinkAllReduce.two_shot for the measurements)."""
-    return world > 2 and (world - 1) * max(rows, 128) * hidden * 2 > (5 << 20)
+    return world > 2 and (world - 1) * max(rows, 128) * hidden * 2 > (10 << 20)
 
 
 class _DeviceArray:
@@ -113,19 +113,17 @@ class NvlinkAllReduce:
         """Whether this batch takes the fused path (decode batches up to the buffers' rows).  On
         B200 (56 calls in a graph) the faster fused kernel beats NCCL + RMSNorm at every measured
         shape: two ranks, 256 rows: 7.8 vs 18.3 us (hidden 1024), 14.9 vs 27.8 (hidden 4096);
-        four and eight ranks: see two_shot()."""
+        eight ranks: see two_shot()."""
         return 0 < rows <= min(self.max_rows, 512)
 
     def two_shot(self, rows: int) -> bool:
         """The two-shot kernel (each rank reduces 1/world of the rows and pushes them to all) once
-        the one-shot kernel would pull more than 5 MiB from its peers, counting at least 128 rows
-        (below that the one-shot kernel has few CTAs and is latency-bound): the one-shot kernel's
-        traffic grows with world - 1, the two-shot kernel's does not, but it waits on a second
-        barrier.  B200, us per call (one-shot / two-shot / NCCL + RMSNorm):
-          4 ranks  hidden 1024 rows 256:  9.3 / 14.0 / 22.7   hidden 4096 rows  64: 22.1 / 22.5 / 25.2
-                                                                hidden 4096 rows 256: 29.7 / 25.1 / 32.9
-          8 ranks  hidden 1024 rows  64: 10.8 / 15.9 / 32.2   hidden 4096 rows  64: 40.7 / 31.0 / 36.4
-                   hidden 1024 rows 256: 15.7 / 16.7 / 34.3   hidden 4096 rows 256: 68.8 / 35.2 / 40.8
+        the one-shot kernel would pull more than 10 MiB from its peers, counting at least 128 rows:
+        the one-shot kernel's traffic grows with world - 1, the two-shot kernel's does not, but it
+        waits on a second barrier.  B200, 8 ranks, us per call in a graph of 56 calls (one-shot /
+        two-shot / NCCL all-reduce + RMSNorm):
+          hidden 1024  rows  64: 10.1 / 16.2 / 32.0     hidden 4096  rows  64: 17.9 / 22.6 / 36.1
+          hidden 1024  rows 256: 14.6 / 16.7 / 34.0     hidden 4096  rows 256: 37.2 / 35.1 / 40.7
         `force_two_shot` (None, True or False) overrides the choice, for tests and profiles."""
         if self.force_two_shot is not None:
             return self.force_two_shot
