@@ -110,8 +110,9 @@ def _reference_outputs():
     return w, q, m, logits
 
 
-def test_tensor_parallel_layers_two_gloo_ranks():
-    world = 2
+def _run_ranks(world):
+    """Runs _worker on `world` spawned gloo ranks; returns {rank: result} or raises with the first
+    failing rank's message."""
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _port()
@@ -119,13 +120,30 @@ def test_tensor_parallel_layers_two_gloo_ranks():
     for p in procs:
         p.start()
     results = {}
-    for _ in range(world):
-        item = queue.get(timeout=240)
-        assert len(item) > 2, f"rank {item[0]} failed: {item[1]}"
-        results[item[0]] = item
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
+    try:
+        for _ in range(world):
+            item = queue.get(timeout=240)
+            if len(item) <= 2:
+                raise RuntimeError(f"rank {item[0]} failed: {item[1]}")
+            results[item[0]] = item
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    if any(p.exitcode != 0 for p in procs):
+        raise RuntimeError(f"rank exit codes {[p.exitcode for p in procs]}")
+    return results
+
+
+def test_tensor_parallel_layers_two_gloo_ranks():
+    world = 2
+    # The rendezvous port is picked free and then bound by the ranks a moment later, so another
+    # process on the host can take it in between: one retry on a fresh port.
+    try:
+        results = _run_ranks(world)
+    except RuntimeError:
+        results = _run_ranks(world)
     w, q, m, logits = _reference_outputs()
     # o_proj over the concatenated per-rank head outputs == full o_proj (sum of the two shards)
     o_full = q @ w["model.layers.0.self_attn.o_proj.weight"].t()
