@@ -313,6 +313,83 @@ def golden_tiny_model(ref):
         json.dump({"prompts": prompts, "seed": 7, "steps": steps, "config": tiny_config_dict()}, f)
 
 
+def golden_qwen3_0_6b(ref, decode_steps=32):
+    """The Qwen3-0.6B configuration of this repository (28 layers, hidden 1024, 16 Q / 8 KV heads,
+    vocab 151,936, tied embeddings) with the seeded random init, run through the reference
+    modules: prefill of four 64-token prompts, then `decode_steps` free-running greedy decode
+    steps; records each step's greedy tokens, the top-1 logit and the top-1 minus top-2 gap."""
+    import torch.distributed as dist
+    from transformers import AutoConfig
+
+    from hilda_vllm_b200.utils.loader import random_init
+    from oracle import attention as oattn
+
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29534", world_size=1, rank=0)
+    import mini_vllm.layers.attention as ref_attn
+    from mini_vllm.models.qwen3 import Qwen3ForCausalLM
+    from mini_vllm.utils.context import reset_context, set_context
+
+    def fa_varlen(q, k, v, max_seqlen_q, cu_seqlens_q, max_seqlen_k, cu_seqlens_k, softmax_scale, causal,
+                  block_table=None):
+        return oattn.varlen_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, softmax_scale, block_table).to(q.dtype)
+
+    def fa_kvcache(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal):
+        return oattn.paged_decode(q.squeeze(1), k_cache, v_cache, block_table, cache_seqlens, softmax_scale).to(
+            q.dtype).unsqueeze(1)
+
+    ref_attn.flash_attn_varlen_func = fa_varlen
+    ref_attn.flash_attn_with_kvcache = fa_kvcache
+    cfg_dir = ROOT / "hilda_vllm_b200" / "model_configs" / "qwen3-0.6b"
+    cfg = AutoConfig.from_pretrained(cfg_dir)
+    torch.set_default_dtype(torch.bfloat16)
+    model = Qwen3ForCausalLM(cfg)
+    torch.set_default_dtype(torch.float32)
+    seed = 11
+    random_init(model, cfg, seed=seed, std=0.02, device="cpu")
+    nb, bs, hk, d = 4, 256, cfg.num_key_value_heads, 128
+    kv = torch.zeros(2, cfg.num_hidden_layers, nb, bs, hk, d, dtype=torch.bfloat16)
+    layer = 0
+    for m in model.modules():
+        if hasattr(m, "k_cache") and hasattr(m, "v_cache"):
+            m.k_cache, m.v_cache = kv[0, layer], kv[1, layer]
+            layer += 1
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg.vocab_size, (64,), generator=g).tolist() for _ in range(4)]
+    tables = [[0], [1], [2], [3]]
+    ids, pos, sm, cu = [], [], [], [0]
+    for p, t in zip(prompts, tables):
+        ids += p
+        pos += list(range(len(p)))
+        sm += [t[0] * bs + i for i in range(len(p))]
+        cu.append(cu[-1] + len(p))
+    cu_t = torch.tensor(cu, dtype=torch.int32)
+    set_context(True, cu_t, cu_t, 64, 64, torch.tensor(sm, dtype=torch.int32), None, None)
+    with torch.no_grad():
+        logits = model.compute_logits(model(torch.tensor(ids), torch.tensor(pos)))
+    reset_context()
+
+    def record(lg):
+        top = lg.float().topk(2, -1).values
+        return {"tokens": lg.argmax(-1).tolist(), "top1": top[:, 0].tolist(), "gap": (top[:, 0] - top[:, 1]).tolist()}
+
+    steps = [record(logits)]
+    seqs = [p + [t] for p, t in zip(prompts, steps[0]["tokens"])]
+    for _ in range(decode_steps):
+        lens = [len(s) for s in seqs]
+        sm = [t[0] * bs + n - 1 for n, t in zip(lens, tables)]
+        bt = torch.tensor(tables, dtype=torch.int32)
+        set_context(False, slot_mapping=torch.tensor(sm, dtype=torch.int32),
+                    context_lens=torch.tensor(lens, dtype=torch.int32), block_tables=bt)
+        with torch.no_grad():
+            logits = model.compute_logits(model(torch.tensor([s[-1] for s in seqs]), torch.tensor([n - 1 for n in lens])))
+        reset_context()
+        steps.append(record(logits))
+        seqs = [s + [t] for s, t in zip(seqs, steps[-1]["tokens"])]
+    with open(HERE / "qwen3_0_6b_greedy_32.json", "w") as f:
+        json.dump({"prompts": prompts, "seed": seed, "steps": steps, "config_dir": "hilda_vllm_b200/model_configs/qwen3-0.6b"}, f)
+
+
 def tiny_config_dict():
     return dict(architectures=["Qwen3ForCausalLM"], model_type="qwen3", attention_bias=False, hidden_act="silu",
                 hidden_size=256, intermediate_size=512, num_attention_heads=4, num_key_value_heads=2, head_dim=128,
@@ -375,6 +452,8 @@ def main():
         golden_tiny_model(args.reference)
     if not only or "sampler" in only:
         golden_sampler(args.reference)
+    if not only or "qwen3_0_6b" in only:
+        golden_qwen3_0_6b(args.reference)
 
 
 if __name__ == "__main__":
